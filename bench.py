@@ -1,0 +1,423 @@
+#!/usr/bin/env python
+"""Hot-path benchmark on B200: one 7B-class decode step's attention + MXFP4
+linears (BASELINE metric "decode-attn & MXFP4 GEMV HBM GB/s").
+
+A step = 32 layers x [ qkv GEMV (M=B) -> paged fp8 decode attention over
+B sequences of 4096 tokens (q read straight out of the qkv output) -> o_proj
+GEMV -> gate_up GEMV ; down GEMV (M=B, K=14336) ], every layer with its own
+weights and KV pool (3.9 GB at B=1, far above the 126 MB L2, so no flush is
+needed between steps).  value = algorithmic HBM bytes of the step / device time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
+
+N > 1 runs under torchrun as independent replicas (one model per GPU, weak
+scaling, no collective on the data path); the reported time is the max over
+ranks.  `--impl reference` times the reference's own CPU path for this work
+(the PyTorch dequant + attention / dequant + matmul checker restated in
+oracle/) on the host's cores, on a bounded sample (one layer per step).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gfx1201-tuning-log_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+sys.path.insert(0, PKG)
+
+import torch  # noqa: E402
+
+METRIC = "decode-attn & MXFP4 GEMV HBM GB/s; 7B decode tok/s at bs 1/4/8, 1–8 GPU"
+SHAPES = (("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336))
+HQ, HKV, D, PBLK = 32, 8, 128, 16
+
+
+def gemv_bytes(N, K, M):
+    """Algorithmic bytes of one MXFP4 matvec: W + scales + x + out."""
+    return N * K // 2 + N * K // 32 + 2 * M * K + 2 * M * N
+
+
+def decode_bytes(B, ctx):
+    """Algorithmic bytes of one decode-attention call: fp8 K+V, q, out, block table, lens."""
+    return B * (2 * ctx * HKV * D + HQ * D * 2 * 2 + (ctx // PBLK) * 4 + 8)
+
+
+def layer_bytes(B, ctx):
+    return sum(gemv_bytes(N, K, B) for _, N, K in SHAPES) + decode_bytes(B, ctx)
+
+
+def workload_config(args):
+    return {"workload": f"7B decode-step hot path: {args.layers} layers x [MXFP4 GEMV "
+                        f"qkv/o/gate_up/down at M={args.batch} + fp8 paged decode attention "
+                        f"{args.batch} seq x {args.ctx} ctx, GQA 32/8, D 128, block 16]",
+            "batch": args.batch, "ctx": args.ctx, "layers": args.layers,
+            "l2": "inputs larger than L2 (distinct weights/KV per layer), no flush",
+            "parallelism": f"replicas x{args.gpus}"}
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+def build_model(args, dev):
+    """Random-init weights and KV pools for `layers` layers on `dev`."""
+    B, ctx, L = args.batch, args.ctx, args.layers
+    g = torch.Generator(device=dev).manual_seed(1234 + args.rank)
+    layers = []
+    nblk = ctx // PBLK
+    for _ in range(L):
+        lay = {}
+        for name, N, K in SHAPES:
+            W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
+            St = torch.randint(119, 126, (N, K // 32), dtype=torch.uint8, device=dev, generator=g)
+            lay[name] = (W, St)
+        nb = B * nblk
+        kf = torch.randn(nb, PBLK, HKV, D, device=dev, generator=g)
+        ks = kf.abs().max() / 448.0
+        lay["k"] = (kf / ks).to(torch.float8_e4m3fn)
+        del kf
+        vf = torch.randn(nb, PBLK, HKV, D, device=dev, generator=g)
+        vs = vf.abs().max() / 448.0
+        lay["v"] = (vf / vs).to(torch.float8_e4m3fn)
+        del vf
+        lay["ks"] = ks.reshape(1).float()
+        lay["vs"] = vs.reshape(1).float()
+        lay["bt"] = torch.randperm(nb, device=dev, generator=g).to(torch.int32).view(B, nblk)
+        lay["x"] = torch.randn(B, 4096, device=dev, generator=g).to(torch.bfloat16)
+        lay["act"] = torch.randn(B, 14336, device=dev, generator=g).to(torch.bfloat16)
+        layers.append(lay)
+    bufs = {
+        "qkv": torch.empty(B, 6144, dtype=torch.bfloat16, device=dev),
+        "attn": torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev),
+        "o": torch.empty(B, 4096, dtype=torch.bfloat16, device=dev),
+        "gate_up": torch.empty(B, 28672, dtype=torch.bfloat16, device=dev),
+        "down": torch.empty(B, 4096, dtype=torch.bfloat16, device=dev),
+        "qsl": torch.arange(B + 1, dtype=torch.int32, device=dev),
+        "slens": torch.full((B,), ctx, dtype=torch.int32, device=dev),
+    }
+    return layers, bufs
+
+
+def run_step(layers, bufs, args, which=("gemv", "attn")):
+    """One hot-path step through the public API (h4mv.mxfp4_gemv, fp8kv_v3.run)."""
+    import fp8kv_v3
+    import h4mv
+    B = args.batch
+    sm = D ** -0.5
+    do_g, do_a = "gemv" in which, "attn" in which
+    for lay in layers:
+        if do_g:
+            h4mv.mxfp4_gemv(lay["x"], *lay["qkv"], out=bufs["qkv"])
+        if do_a:
+            q = bufs["qkv"][:, :HQ * D].unflatten(1, (HQ, D))
+            fp8kv_v3.run(q, lay["k"], lay["v"], bufs["attn"], bufs["qsl"], bufs["slens"], lay["bt"],
+                         lay["ks"], lay["vs"], sm, max_seq_len=args.ctx)
+        if do_g:
+            h4mv.mxfp4_gemv(bufs["attn"].view(B, HQ * D), *lay["o"], out=bufs["o"])
+            h4mv.mxfp4_gemv(bufs["o"], *lay["gate_up"], out=bufs["gate_up"])
+            h4mv.mxfp4_gemv(lay["act"], *lay["down"], out=bufs["down"])
+
+
+def capture(fn):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # sizes the decode workspace outside the capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    return graph
+
+
+def time_graph(graph, steps, warmup, barrier=None):
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    return e0.elapsed_time(e1) / steps
+
+
+def max_over_ranks(x, dist_on, dev):
+    if not dist_on:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+# ---------------------------------------------------------------------------
+def cpu_layer_sample(args, seed=0):
+    """One layer of the hot path on the host through the oracle (reference
+    PyTorch path).  Returns (seconds, bytes)."""
+    sys.path.insert(0, ORACLE)
+    import fp8kv_oracle as FO
+    import mxfp4_oracle as MO
+    torch.set_num_threads(os.cpu_count())
+    B = args.batch
+    cases = [MO.make_case(N, K, B, seed=seed + i) for i, (_, N, K) in enumerate(SHAPES)]
+    dc = FO.make_decode_case(B, [args.ctx] * B, seed=seed)
+    t0 = time.perf_counter()
+    for W, S, St, X in cases:
+        MO.mxfp4_linear_reference(W, S, X)
+    FO.decode_reference(dc["q"], dc["k_cache"], dc["v_cache"], dc["qsl"], dc["seq_lens"],
+                        dc["block_table"], dc["k_scale"], dc["v_scale"], dc["sm_scale"])
+    return time.perf_counter() - t0, layer_bytes(B, args.ctx)
+
+
+def cpu_baseline(args, reps=3):
+    cpu_layer_sample(args, seed=99)  # warm
+    times = []
+    for r in range(reps):
+        t, nbytes = cpu_layer_sample(args, seed=r)
+        times.append(t)
+    t = statistics.median(times)
+    return {"value": nbytes / t / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"1 of {args.layers} layers (4 MXFP4 GEMVs at M={args.batch} + decode attention "
+                      f"{args.batch}x{args.ctx}), torch fp32 oracle, median of {reps}, "
+                      f"{t * 1e3:.0f} ms/layer"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_layer_sample(args, seed=1000)
+    times, nbytes = [], 0
+    for i in range(args.steps):
+        t, nbytes = cpu_layer_sample(args, seed=i)
+        times.append(t)
+    t = sum(times) / len(times)
+    val = nbytes / t / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args),
+            "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": "each step = 1 layer of the hot path through the torch fp32 "
+                                       "oracle (reference PyTorch dequant+attention / dequant+matmul)"},
+            "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def run_b200(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    args.rank = rank
+    dist_on = world > 1
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    barrier = None
+    if dist_on:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        barrier = dist.barrier
+
+    layers, bufs = build_model(args, dev)
+    step_bytes = args.layers * layer_bytes(args.batch, args.ctx)
+    launches_per_step = args.layers * 5
+
+    g_step = capture(lambda: run_step(layers, bufs, args))
+    g_gemv = capture(lambda: run_step(layers, bufs, args, which=("gemv",)))
+    g_attn = capture(lambda: run_step(layers, bufs, args, which=("attn",)))
+
+    # ---- timed region: whole steps (graph replay), clocks sampled meanwhile --
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms = time_graph(g_step, args.steps, args.warmup, barrier)
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, dist_on, dev)
+
+    # ---- per-kernel breakdown (same graphs, kernel class alone) ------------
+    ms_gemv = max_over_ranks(time_graph(g_gemv, args.steps, 2, barrier), dist_on, dev)
+    ms_attn = max_over_ranks(time_graph(g_attn, args.steps, 2, barrier), dist_on, dev)
+    gemv_bytes_step = args.layers * sum(gemv_bytes(N, K, args.batch) for _, N, K in SHAPES)
+    attn_bytes_step = args.layers * decode_bytes(args.batch, args.ctx)
+
+    # ---- e2e through the public API with host buffers ----------------------
+    B = args.batch
+    h_x = torch.randn(args.layers, B, 4096).to(torch.bfloat16).pin_memory()
+    h_act = torch.randn(args.layers, B, 14336).to(torch.bfloat16).pin_memory()
+    d_x = torch.stack([lay["x"] for lay in layers])  # staging views refreshed per step
+    d_act = torch.stack([lay["act"] for lay in layers])
+    for i, lay in enumerate(layers):
+        lay["x"] = d_x[i]
+        lay["act"] = d_act[i]
+    g_e2e = capture(lambda: run_step(layers, bufs, args))
+    h_out = torch.empty(B, 4096, dtype=torch.bfloat16).pin_memory()
+    h_attn = torch.empty(B, HQ, D, dtype=torch.bfloat16).pin_memory()
+    h2d = h_x.numel() * 2 + h_act.numel() * 2
+    d2h = h_out.numel() * 2 + h_attn.numel() * 2
+
+    def e2e_step():
+        d_x.copy_(h_x, non_blocking=True)
+        d_act.copy_(h_act, non_blocking=True)
+        g_e2e.replay()
+        h_out.copy_(bufs["down"], non_blocking=True)
+        h_attn.copy_(bufs["attn"], non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps, dist_on, dev)
+
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    gemv_gbs = gemv_bytes_step / (ms_gemv * 1e-3) / 1e9
+    n_gemv = args.layers * 4
+
+    result = None
+    if rank == 0:
+        cpu = cpu_baseline(args) if world == 1 else None
+        value = world * step_bytes / (ms * 1e-3) / 1e9
+        result = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": workload_config(args),
+            "tok_s_hot_path_only": world * args.batch / (ms * 1e-3),
+            "parts": {
+                "mxfp4_gemv": {"us_per_step": ms_gemv * 1e3, "launches_per_step": n_gemv,
+                               "gbs": gemv_gbs},
+                "decode_attn": {"us_per_step": ms_attn * 1e3, "launches_per_step": args.layers,
+                                "gbs": attn_bytes_step / (ms_attn * 1e-3) / 1e9},
+            },
+            "roofline": {"bound": "hbm", "kernel": "mxfp4_gemv_kernel",
+                         "achieved": gemv_gbs, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": gemv_gbs / hbm_peak, "peak_source": peak_src,
+                         "bytes_per_launch_avg": gemv_bytes_step / n_gemv,
+                         "us_per_launch_avg": ms_gemv * 1e3 / n_gemv,
+                         "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * step_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "pinned host activations -> H2D, graph of public-API calls "
+                            "(h4mv.mxfp4_gemv, fp8kv_v3.run), D2H of outputs"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(result), flush=True)
+    del g_step, g_gemv, g_attn, g_e2e
+    if dist_on:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
+    args.rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,86 @@
+"""ctypes binding of libb200kv.so (the sm_100a kernels behind this directory's
+drop-in modules).
+
+The library is the product path: there is no CPU or Triton fallback.  If the
+shared object is missing, importing this module raises ImportError with the
+build command, so a mis-deployed drop-in fails loudly instead of silently
+falling back (the reference's fallbacks exist only in the vLLM override layer,
+where they route to vLLM's own stock kernels).
+
+Entry points mirror include/b200kv.h; every call returns a status that
+`check()` turns into a RuntimeError naming the call.
+"""
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("B200KV_LIB", os.path.join(_HERE, "libb200kv.so"))
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(
+        f"libb200kv.so not found at {LIB_PATH}; build it with `make -C {_HERE}` "
+        "(nvcc, sm_100a) or python -c 'import __graft_entry__ as g; g.build()'")
+
+lib = ctypes.CDLL(LIB_PATH)
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+lib.b200kv_version.restype = _i32
+lib.b200kv_version.argtypes = []
+lib.b200kv_status_string.restype = ctypes.c_char_p
+lib.b200kv_status_string.argtypes = [_i32]
+lib.b200kv_last_error.restype = _i32
+lib.b200kv_last_error.argtypes = []
+lib.b200kv_get_device_status.restype = _i32
+lib.b200kv_get_device_status.argtypes = [_vp, ctypes.POINTER(_i32)]
+lib.b200kv_reset_device_status.restype = _i32
+lib.b200kv_reset_device_status.argtypes = [_vp]
+
+lib.b200kv_mxfp4_gemv.restype = _i32
+lib.b200kv_mxfp4_gemv.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]
+# identical to the reference binding h4mv/fp8kv_hipw4.py:21-23
+lib.h4mv_launch.restype = None
+lib.h4mv_launch.argtypes = [_vp] * 4 + [_i32] * 3 + [_vp]
+
+lib.b200kv_decode_attn_workspace_size.restype = _i32
+lib.b200kv_decode_attn_workspace_size.argtypes = [_i32] * 8 + [ctypes.POINTER(_sz)]
+lib.b200kv_decode_attn.restype = _i32
+lib.b200kv_decode_attn.argtypes = (
+    [_vp, _i64, _i64,                 # q, strides
+     _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,  # caches, strides
+     _vp, _i64, _i64,                 # out, strides
+     _vp, _vp, _vp, _i64,             # qsl, seq_lens, block_table, bt stride
+     _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
+     _i32, _i32, _i32, _i32, _i32, _i32, _i32,  # num_seqs .. max_seq_len_hint
+     _i32, _i32, _i32,                # kv_dtype, out_by_qsl, num_splits
+     _vp, _sz, _vp])                  # workspace, bytes, stream
+
+KV_FP8_E4M3 = 0
+KV_BF16 = 1
+
+
+class B200KVError(RuntimeError):
+    def __init__(self, what, status):
+        self.status = status
+        msg = lib.b200kv_status_string(status).decode()
+        super().__init__(f"{what} failed: {msg} (status {status})")
+
+
+def check(status, what):
+    if status != 0:
+        raise B200KVError(what, status)
+
+
+def device_status(stream=0):
+    """Device-side status word (0 = no kernel hit a bounded-wait limit)."""
+    v = _i32(0)
+    check(lib.b200kv_get_device_status(_vp(stream), ctypes.byref(v)), "b200kv_get_device_status")
+    return v.value
+
+
+def reset_device_status(stream=0):
+    check(lib.b200kv_reset_device_status(_vp(stream)), "b200kv_reset_device_status")

@@ -1,0 +1,76 @@
+// Shared device/host helpers for libb200kv (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace b200kv {
+
+// ---- device status word ------------------------------------------------------
+// Written (atomicExch) by a kernel that gave up on a bounded wait.  Codes:
+enum DeviceStatus : int {
+  kDevOk = 0,
+  kDevMbarrierTimeout = 0x101,   // a bulk copy never completed on its mbarrier
+  kDevSplitOverflow = 0x102,     // seq_len larger than the context bound given
+};
+extern __device__ int g_device_status;
+
+// ---- host helpers ------------------------------------------------------------
+int num_sms_current_device();     // cached per device; 0 when no device
+int sm_major_current_device();
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// ---- device helpers ----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Bounded wait on an mbarrier phase.  Returns false (and records the device
+// status) when the phase did not complete within `max_tries` polls.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint32_t max_tries = (1u << 22)) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t i = 0; i < max_tries; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  atomicExch(&g_device_status, kDevMbarrierTimeout);
+  return false;
+}
+
+// One-dimensional bulk copy global -> shared (TMA engine), completion counted
+// in bytes on `bar`.  dst, src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+}  // namespace b200kv

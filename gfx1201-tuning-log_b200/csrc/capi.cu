@@ -1,0 +1,144 @@
+// Exported C ABI of libb200kv.so (declared in include/b200kv.h).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b200kv.h"
+#include "b200kv_common.cuh"
+
+namespace b200kv {
+
+__device__ int g_device_status = 0;
+
+namespace {
+constexpr int kMaxDevices = 64;
+int g_sms[kMaxDevices];    // 0 = not cached yet
+int g_major[kMaxDevices];
+
+int current_device_slot() {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return -1;
+  }
+  if (g_sms[dev] == 0) {
+    int sms = 0, major = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
+    g_major[dev] = major;
+    g_sms[dev] = sms;  // written last: a racing reader sees 0 and recomputes
+  }
+  return dev;
+}
+
+thread_local int t_last_error = B200KV_OK;
+}  // namespace
+
+int num_sms_current_device() {
+  const int d = current_device_slot();
+  return d < 0 ? 0 : g_sms[d];
+}
+
+int sm_major_current_device() {
+  const int d = current_device_slot();
+  return d < 0 ? 0 : g_major[d];
+}
+
+int mxfp4_gemv_launch(const void* W, const void* St, const void* X, void* out, int N, int K,
+                      int M, void* stream);
+int decode_attn_workspace_size(int num_seqs, int hq, int hkv, int head_dim, int block_size,
+                               int max_blocks, int hint, int num_splits, size_t* bytes);
+int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
+                       const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
+                       int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
+                       const int32_t* qsl, const int32_t* seq_lens, const int32_t* bt,
+                       int64_t bt_stride, const float* k_scale, const float* v_scale,
+                       float sm_scale, int num_seqs, int hq, int hkv, int head_dim,
+                       int block_size, int max_blocks, int hint, int kv_dtype, int out_by_qsl,
+                       int num_splits, void* ws, size_t ws_bytes, void* stream);
+
+void set_last_error(int e) { t_last_error = e; }
+
+}  // namespace b200kv
+
+extern "C" {
+
+int b200kv_version(void) { return 100; }
+
+const char* b200kv_status_string(int status) {
+  switch (status) {
+    case B200KV_OK: return "ok";
+    case B200KV_ERR_INVALID_ARG: return "invalid argument";
+    case B200KV_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case B200KV_ERR_MISALIGNED: return "misaligned pointer or stride";
+    case B200KV_ERR_WORKSPACE: return "workspace missing or too small";
+    case B200KV_ERR_LAUNCH: return "kernel launch failed";
+    case B200KV_ERR_NO_DEVICE: return "no sm_100 device is current";
+    default: return "unknown status";
+  }
+}
+
+int b200kv_last_error(void) { return b200kv::t_last_error; }
+
+int b200kv_get_device_status(void* stream, int* status_out) {
+  if (!status_out) return B200KV_ERR_INVALID_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, b200kv::g_device_status, sizeof(int), 0,
+                                cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaGetLastError();
+    return B200KV_ERR_LAUNCH;
+  }
+  *status_out = v;
+  return B200KV_OK;
+}
+
+int b200kv_reset_device_status(void* stream) {
+  static const int zero = 0;
+  if (cudaMemcpyToSymbolAsync(b200kv::g_device_status, &zero, sizeof(int), 0,
+                              cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return B200KV_ERR_LAUNCH;
+  }
+  return B200KV_OK;
+}
+
+int b200kv_mxfp4_gemv(const void* W, const void* St, const void* X, void* out, int N, int K, int M,
+                      void* stream) {
+  return b200kv::mxfp4_gemv_launch(W, St, X, out, N, K, M, stream);
+}
+
+void h4mv_launch(const void* W, const void* St, const void* Xb, void* Out, int N, int K, int M,
+                 void* stream) {
+  b200kv::set_last_error(b200kv::mxfp4_gemv_launch(W, St, Xb, Out, N, K, M, stream));
+}
+
+int b200kv_decode_attn_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
+                                      int head_dim, int block_size, int max_blocks_per_seq,
+                                      int max_seq_len_hint, int num_splits, size_t* bytes_out) {
+  return b200kv::decode_attn_workspace_size(num_seqs, num_q_heads, num_kv_heads, head_dim,
+                                            block_size, max_blocks_per_seq, max_seq_len_hint,
+                                            num_splits, bytes_out);
+}
+
+int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                       const void* k_cache, const void* v_cache, int64_t sk0, int64_t sk1,
+                       int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2, void* out,
+                       int64_t out_stride_tok, int64_t out_stride_head, const int32_t* qsl,
+                       const int32_t* seq_lens, const int32_t* block_table, int64_t bt_stride,
+                       const float* k_scale, const float* v_scale, float sm_scale, int num_seqs,
+                       int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                       int max_blocks_per_seq, int max_seq_len_hint, int kv_dtype, int out_by_qsl,
+                       int num_splits, void* workspace, size_t workspace_bytes, void* stream) {
+  return b200kv::decode_attn_launch(
+      q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
+      out_stride_tok, out_stride_head, qsl, seq_lens, block_table, bt_stride, k_scale, v_scale,
+      sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
+      max_seq_len_hint, kv_dtype, out_by_qsl, num_splits, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

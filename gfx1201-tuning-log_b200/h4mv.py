@@ -1,0 +1,45 @@
+"""MXFP4 W4A16 matvec -- host entry points over libb200kv.so.
+
+`launch` mirrors the reference test helper h4mv/h4mv_test.py:13-15 (same
+argument order, raw ctypes call of h4mv_launch on the current stream);
+`mxfp4_gemv` is the checked torch-level entry used by the op override
+(fp8kv_hipw4.py) and by the benchmarks.
+"""
+import torch
+
+from _b200kv import check, lib
+
+MAX_M = 8
+
+
+def launch(W, St, X, Y, N, K, M):
+    """Raw reference-style launch: h4mv_launch(W, St, X, Y, N, K, M, stream)."""
+    lib.h4mv_launch(W.data_ptr(), St.data_ptr(), X.data_ptr(), Y.data_ptr(), N, K, M,
+                    torch.cuda.current_stream().cuda_stream)
+    check(lib.b200kv_last_error(), "h4mv_launch")
+
+
+def mxfp4_gemv(x, weight, scale_t, out=None):
+    """out[M, N] = x[M, K] @ dequant(weight [N, K/2] e2m1, scale_t [N, K/32] e8m0)^T.
+
+    x bf16 contiguous with 1 <= M <= 8; weight uint8; scale_t uint8 (already
+    transposed to [N, K/32]).  Returns bf16 [M, N].
+    """
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D bfloat16 tensor")
+    if weight.dtype != torch.uint8 or scale_t.dtype != torch.uint8:
+        raise TypeError("weight and scale must be uint8")
+    M, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] * 2 != K or tuple(scale_t.shape) != (N, K // 32):
+        raise ValueError(f"shape mismatch x={tuple(x.shape)} w={tuple(weight.shape)} "
+                         f"s={tuple(scale_t.shape)}")
+    if not (weight.is_contiguous() and scale_t.is_contiguous()):
+        raise ValueError("weight and scale must be contiguous")
+    if out is None:
+        out = torch.empty((M, N), device=x.device, dtype=torch.bfloat16)
+    check(lib.b200kv_mxfp4_gemv(weight.data_ptr(), scale_t.data_ptr(), x.data_ptr(),
+                                out.data_ptr(), N, K, M,
+                                torch.cuda.current_stream(x.device).cuda_stream),
+          "b200kv_mxfp4_gemv")
+    return out

@@ -1,0 +1,143 @@
+/*
+ * b200kv.h — C ABI of libb200kv.so, the sm_100a (B200) implementation of the
+ * pty819/gfx1201-tuning-log inference hot path:
+ *
+ *   - MXFP4 (e2m1 weights + e8m0 group scales) W4A16 matvec / skinny GEMM
+ *   - fp8-e4m3 (or bf16) paged-KV split-K decode attention
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers unless stated otherwise; the caller owns
+ *     every buffer. Nothing here allocates device memory.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Every call is asynchronous on that stream and never synchronises the host,
+ *     so calls can be captured into CUDA graphs.
+ *   - Entry points return 0 (B200KV_OK) or a B200KV_ERR_* code; on error nothing
+ *     was launched. b200kv_status_string() names a code.
+ *   - Strides are in ELEMENTS of the tensor's own dtype (torch's Tensor.stride()),
+ *     innermost stride 1.
+ *   - No global mutable host state beyond a cached device-attribute table and the
+ *     thread-local last error of the void-returning h4mv_launch().
+ */
+#ifndef B200KV_H
+#define B200KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------- */
+#define B200KV_OK                 0
+#define B200KV_ERR_INVALID_ARG    1  /* null pointer, negative/zero size, bad stride */
+#define B200KV_ERR_UNSUPPORTED    2  /* shape/dtype outside what the kernels implement */
+#define B200KV_ERR_MISALIGNED     3  /* pointer or stride violates a 16-byte rule */
+#define B200KV_ERR_WORKSPACE      4  /* workspace missing or smaller than required */
+#define B200KV_ERR_LAUNCH         5  /* the CUDA launch itself failed */
+#define B200KV_ERR_NO_DEVICE      6  /* no sm_100 device current */
+
+/* dtype tags for KV caches */
+#define B200KV_KV_FP8_E4M3        0  /* 1 byte/elem, per-tensor fp32 k/v scales */
+#define B200KV_KV_BF16            1  /* 2 bytes/elem, scales ignored             */
+
+/* Library version (major*10000 + minor*100 + patch). */
+int b200kv_version(void);
+
+/* Human-readable name of a status code (static string). */
+const char* b200kv_status_string(int status);
+
+/* Status of the most recent h4mv_launch() on the calling host thread. */
+int b200kv_last_error(void);
+
+/*
+ * Device-side status word written by kernels that hit a bounded wait limit
+ * (an mbarrier that never completed).  0 = clean.  Reading it synchronises
+ * the given stream.  b200kv_reset_device_status() clears it (async on stream).
+ */
+int b200kv_get_device_status(void* stream, int* status_out);
+int b200kv_reset_device_status(void* stream);
+
+/* ---- MXFP4 W4A16 matvec ------------------------------------------------------
+ *
+ * out[m, n] = bf16_rn( sum_g scale(St[n, g]) * sum_{j<32} e2m1(W[n, 32g+j]) * X[m, 32g+j] )
+ *
+ *   W   uint8 [N, K/2]   two e2m1 codes per byte, low nibble = even k; 16-B aligned
+ *   St  uint8 [N, K/32]  e8m0 group scales, already transposed from the checkpoint's
+ *                        [K/32, N] layout; scale(b) = 2^(b-127) for 1<=b<=254,
+ *                        scale(0) = 0 and scale(255) = inf (the bit pattern b<<23
+ *                        read as fp32, exactly as the reference kernel does)
+ *   X   bf16  [M, K]     contiguous, 16-B aligned
+ *   out bf16  [M, N]     contiguous
+ *   1 <= M <= 8, K % 32 == 0, N >= 1.
+ *
+ * Replaces h4mv/h4mv.cu:106-122 (h4mv_launch) of the reference, with a status
+ * return.  Accumulation is fp32; products e2m1 x bf16 are exact.
+ */
+int b200kv_mxfp4_gemv(const void* W, const void* St, const void* X, void* out,
+                      int N, int K, int M, void* stream);
+
+/*
+ * Drop-in for the reference's own symbol (h4mv/h4mv.cu:106-107), same
+ * signature and argument meaning, loadable through the same ctypes binding
+ * (h4mv/fp8kv_hipw4.py:21-23).  Unlike the reference it does NOT silently run
+ * M>8 as M=8: invalid arguments launch nothing and set b200kv_last_error().
+ */
+void h4mv_launch(const void* W, const void* St, const void* Xb, void* Out,
+                 int N, int K, int M, void* stream);
+
+/* ---- fp8 paged-KV decode attention ------------------------------------------
+ *
+ * For every sequence s < num_seqs and query head h (GQA = num_q_heads/num_kv_heads,
+ * kv head kh = h / GQA), with L = seq_lens[s] and token t = qsl[s]:
+ *
+ *   score[j] = (q[t, h, :] . K[j, kh, :]) * sm_scale * k_scale      j < L
+ *   out[r, h, :] = v_scale * softmax(score) @ V[:L, kh, :]           (bf16)
+ *
+ * where K[j] lives in block block_table[s, j / block_size] at slot j % block_size:
+ *   key element (j, kh, d) = k_cache[blk*sk0 + slot*sk1 + kh*sk2 + d]
+ * and r = qsl[s] when out_by_qsl != 0 (fp8kv_kernel.py:70), r = s otherwise
+ * (fp8kv_v3.py:112).  Sequences with L == 0 produce zeros.
+ *
+ * Replaces the Python entry points vllm-fp8kv/fp8kv_v3.py:116-139 (split +
+ * reduce Triton kernels) and vllm-fp8kv/fp8kv_kernel.py:75-88.
+ *
+ *   q            bf16 [*, num_q_heads, head_dim]   strides (q_stride_tok, q_stride_head, 1)
+ *   k/v_cache    fp8 e4m3 or bf16 (kv_dtype), strides (s*0, s*1, s*2, 1) in elements
+ *   out          bf16, strides (out_stride_tok, out_stride_head, 1)
+ *   qsl          int32 [num_seqs+1]; seq_lens int32 [num_seqs]
+ *   block_table  int32 [num_seqs, >= max_blocks_per_seq], row stride bt_stride
+ *   k/v_scale    device fp32 scalars (ignored for bf16 KV)
+ *   head_dim must be 128; GQA must be 1, 2, 4 or 8.
+ *   num_splits   0 = choose automatically; otherwise the context bound
+ *                (max_seq_len_hint, or max_blocks_per_seq*block_size when the hint
+ *                is 0) is cut into num_splits spans, each at most 256 tokens.
+ *   workspace    device buffer of at least b200kv_decode_attn_workspace_size()
+ *                bytes, 256-B aligned, ZERO-FILLED before its first use; the kernels
+ *                leave it zero-filled where it matters (a per-(seq, kv head) arrival
+ *                counter), so it can be reused by later calls on the same stream.
+ *                Calls that overlap in time must not share a workspace.
+ */
+int b200kv_decode_attn_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
+                                      int head_dim, int block_size, int max_blocks_per_seq,
+                                      int max_seq_len_hint, int num_splits,
+                                      size_t* bytes_out);
+
+int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                       const void* k_cache, const void* v_cache,
+                       int64_t sk0, int64_t sk1, int64_t sk2,
+                       int64_t sv0, int64_t sv1, int64_t sv2,
+                       void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                       const int32_t* qsl, const int32_t* seq_lens,
+                       const int32_t* block_table, int64_t bt_stride,
+                       const float* k_scale, const float* v_scale, float sm_scale,
+                       int num_seqs, int num_q_heads, int num_kv_heads, int head_dim,
+                       int block_size, int max_blocks_per_seq, int max_seq_len_hint,
+                       int kv_dtype, int out_by_qsl, int num_splits,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200KV_H */

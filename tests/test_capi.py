@@ -1,0 +1,104 @@
+"""C-ABI checks that need no GPU: the library loads, exports every symbol that
+include/b200kv.h declares, and rejects bad arguments with the documented status
+codes before touching a device."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                      "include", "b200kv.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b([A-Za-z_]\w*)\s*\(", text, flags=re.M)
+    return sorted(set(n for n in names if n not in ("defined",)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for must in ("b200kv_mxfp4_gemv", "h4mv_launch", "b200kv_decode_attn",
+                 "b200kv_decode_attn_workspace_size", "b200kv_status_string"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol(libpath):
+    lib = ctypes.CDLL(libpath)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_status_strings(b200):
+    lib = b200.lib
+    assert lib.b200kv_status_string(0) == b"ok"
+    for code in range(1, 7):
+        assert lib.b200kv_status_string(code) not in (b"ok", b"unknown status")
+    assert lib.b200kv_status_string(99) == b"unknown status"
+    assert lib.b200kv_version() >= 100
+
+
+def test_gemv_argument_validation(b200):
+    lib = b200.lib
+    A = 0x10000  # never dereferenced: every call below fails validation first
+    assert lib.b200kv_mxfp4_gemv(None, A, A, A, 8, 32, 1, None) == 1
+    assert lib.b200kv_mxfp4_gemv(A, A, A, A, 0, 32, 1, None) == 1
+    assert lib.b200kv_mxfp4_gemv(A, A, A, A, 8, 32, 9, None) == 2
+    assert lib.b200kv_mxfp4_gemv(A, A, A, A, 8, 33, 1, None) == 2
+    assert lib.b200kv_mxfp4_gemv(A + 8, A, A, A, 8, 32, 1, None) == 3
+    assert lib.b200kv_mxfp4_gemv(A, A, A + 4, A, 8, 32, 1, None) == 3
+    lib.h4mv_launch(A, A, A, A, 8, 32, 9, None)
+    assert lib.b200kv_last_error() == 2
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="fake pointers are only safe without a GPU")
+def test_gemv_no_device(b200):
+    A = 0x10000
+    assert b200.lib.b200kv_mxfp4_gemv(A, A, A, A, 8, 32, 1, None) == 6
+
+
+def _decode_call(lib, **over):
+    A = 0x10000
+    args = dict(q=A, qst=32 * 128, qsh=128, k=A, v=A, sk0=16 * 8 * 128, sk1=8 * 128, sk2=128,
+                sv0=16 * 8 * 128, sv1=8 * 128, sv2=128, out=A, ost=32 * 128, osh=128,
+                qsl=A, sl=A, bt=A, bts=4, ks=A, vs=A, sm=0.088, ns=2, hq=32, hkv=8, d=128,
+                pblk=16, maxblk=4, hint=0, kvdt=0, obq=0, nsplit=0, ws=A, wsb=1 << 30, st=None)
+    args.update(over)
+    a = args
+    return lib.b200kv_decode_attn(a["q"], a["qst"], a["qsh"], a["k"], a["v"], a["sk0"], a["sk1"],
+                                  a["sk2"], a["sv0"], a["sv1"], a["sv2"], a["out"], a["ost"],
+                                  a["osh"], a["qsl"], a["sl"], a["bt"], a["bts"], a["ks"], a["vs"],
+                                  a["sm"], a["ns"], a["hq"], a["hkv"], a["d"], a["pblk"],
+                                  a["maxblk"], a["hint"], a["kvdt"], a["obq"], a["nsplit"],
+                                  a["ws"], a["wsb"], a["st"])
+
+
+def test_decode_argument_validation(b200):
+    lib = b200.lib
+    assert _decode_call(lib, q=None) == 1
+    assert _decode_call(lib, d=64) == 2
+    assert _decode_call(lib, hq=24) == 2           # GQA 3
+    assert _decode_call(lib, hq=30) == 1           # not a multiple of HKV
+    assert _decode_call(lib, kvdt=7) == 2
+    assert _decode_call(lib, ks=None) == 1         # fp8 needs scales
+    assert _decode_call(lib, wsb=16) == 4
+    assert _decode_call(lib, ws=0x10010) == 3      # workspace not 256-B aligned
+    assert _decode_call(lib, sk1=8 * 128 + 1) == 3  # row not 16-B aligned
+    assert _decode_call(lib, k=0x10008) == 3
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="fake pointers are only safe without a GPU")
+def test_decode_no_device(b200):
+    assert _decode_call(b200.lib) == 6
+
+
+def test_decode_workspace_size(b200):
+    import _decode
+    a = _decode.workspace_size(1, 32, 8, 128, 16, 256)
+    b = _decode.workspace_size(8, 32, 8, 128, 16, 256)
+    assert 0 < a < b
+    with pytest.raises(b200.B200KVError):
+        _decode.workspace_size(1, 32, 8, 64, 16, 256)
