@@ -181,7 +181,7 @@ def capture(fn):
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        fn()  # sizes the decode workspace outside the capture
+        fn()  # warm-up outside the capture
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()

@@ -27,7 +27,6 @@ _vp = ctypes.c_void_p
 _i32 = ctypes.c_int
 _i64 = ctypes.c_int64
 _f32 = ctypes.c_float
-_sz = ctypes.c_size_t
 
 lib.b200kv_version.restype = _i32
 lib.b200kv_version.argtypes = []
@@ -46,8 +45,6 @@ lib.b200kv_mxfp4_gemv.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]
 lib.h4mv_launch.restype = None
 lib.h4mv_launch.argtypes = [_vp] * 4 + [_i32] * 3 + [_vp]
 
-lib.b200kv_decode_attn_workspace_size.restype = _i32
-lib.b200kv_decode_attn_workspace_size.argtypes = [_i32] * 8 + [ctypes.POINTER(_sz)]
 lib.b200kv_decode_attn.restype = _i32
 lib.b200kv_decode_attn.argtypes = (
     [_vp, _i64, _i64,                 # q, strides
@@ -57,7 +54,11 @@ lib.b200kv_decode_attn.argtypes = (
      _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
      _i32, _i32, _i32, _i32, _i32, _i32, _i32,  # num_seqs .. max_seq_len_hint
      _i32, _i32, _i32,                # kv_dtype, out_by_qsl, num_splits
-     _vp, _sz, _vp])                  # workspace, bytes, stream
+     _vp])                            # stream
+
+lib.b200kv_kv_write.restype = _i32
+lib.b200kv_kv_write.argtypes = ([_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp] + [_i64] * 6 +
+                                [_vp, _vp, _vp] + [_i32] * 5 + [_vp])
 
 KV_FP8_E4M3 = 0
 KV_BF16 = 1

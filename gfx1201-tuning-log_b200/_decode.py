@@ -1,60 +1,14 @@
 """Host side of the paged-KV decode attention: argument mapping from torch
-tensors to the C ABI entry b200kv_decode_attn, plus workspace management.
+tensors to the C ABI entry b200kv_decode_attn.
 
 Shared by fp8kv_v3.run (reference vllm-fp8kv/fp8kv_v3.py:116-139) and
-fp8kv_kernel.run (reference vllm-fp8kv/fp8kv_kernel.py:75-88).
+fp8kv_kernel.run (reference vllm-fp8kv/fp8kv_kernel.py:75-88).  The kernel
+needs no workspace: the split partials of a (sequence, kv head) are merged
+inside a thread-block cluster through distributed shared memory.
 """
-import ctypes
-
 import torch
 
 from _b200kv import KV_BF16, KV_FP8_E4M3, check, lib
-
-
-class DecodeWorkspace:
-    """Zero-initialised device workspace for split-K partials and the
-    per-(sequence, kv head) arrival counters.  The kernel leaves the counters at
-    zero after every call, so one workspace serves any number of sequential
-    calls on one stream; calls that may overlap need separate workspaces."""
-
-    def __init__(self, device, nbytes=0):
-        self.device = torch.device(device)
-        self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=self.device)
-
-    @property
-    def nbytes(self):
-        return self.buf.numel()
-
-    def ensure(self, nbytes):
-        if nbytes > self.buf.numel():
-            if torch.cuda.is_current_stream_capturing():
-                raise RuntimeError(
-                    f"decode workspace too small ({self.buf.numel()} < {nbytes} bytes) "
-                    "during CUDA graph capture; size it before capturing")
-            self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
-        return self.buf
-
-
-_default_ws = {}
-
-
-def default_workspace(device):
-    dev = torch.device(device)
-    key = (dev.type, dev.index if dev.index is not None else torch.cuda.current_device())
-    ws = _default_ws.get(key)
-    if ws is None:
-        ws = DecodeWorkspace(dev)
-        _default_ws[key] = ws
-    return ws
-
-
-def workspace_size(num_seqs, num_q_heads, num_kv_heads, head_dim, block_size,
-                   max_blocks, max_seq_len_hint=0, num_splits=0):
-    out = ctypes.c_size_t(0)
-    check(lib.b200kv_decode_attn_workspace_size(
-        num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks,
-        max_seq_len_hint, num_splits, ctypes.byref(out)), "b200kv_decode_attn_workspace_size")
-    return out.value
 
 
 def _scale_tensor(s, device):
@@ -67,12 +21,13 @@ def _scale_tensor(s, device):
 
 def decode_attention(q, k_cache, v_cache, out, qsl, seq_lens, block_table,
                      k_scale, v_scale, sm_scale, *, out_by_qsl, num_splits=0,
-                     max_seq_len_hint=0, workspace=None):
+                     max_seq_len_hint=0):
     """Launch the decode kernel on the current stream.
 
     q [T, HQ, D] bf16; k_cache/v_cache [NB, PBLK, HKV, D] (fp8 e4m3 or bf16, any
     strides with the innermost 1); out [*, HQ, D] bf16; qsl int32 [NS+1];
-    seq_lens int32 [NS]; block_table int32 [NS, maxblk].
+    seq_lens int32 [NS]; block_table int32 [NS, maxblk].  num_splits = CTAs per
+    (sequence, kv head), 0 = automatic, at most 16.
     """
     if q.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
         raise TypeError("q and out must be bfloat16")
@@ -93,17 +48,8 @@ def decode_attention(q, k_cache, v_cache, out, qsl, seq_lens, block_table,
     if not (qsl.is_contiguous() and seq_lens.is_contiguous() and block_table.stride(1) == 1):
         raise ValueError("qsl/seq_lens must be contiguous, block_table rows contiguous")
     dev = q.device
-    num_seqs = block_table.shape[0]
-    hq = q.shape[1]
-    hkv = k_cache.shape[2]
-    d = q.shape[2]
-    pblk = k_cache.shape[1]
-    maxblk = block_table.shape[1]
     ks = _scale_tensor(k_scale, dev)
     vs = _scale_tensor(v_scale, dev)
-    need = workspace_size(num_seqs, hq, hkv, d, pblk, maxblk, max_seq_len_hint, num_splits)
-    ws = workspace if workspace is not None else default_workspace(dev)
-    buf = ws.ensure(need)
     stream = torch.cuda.current_stream(dev).cuda_stream
     check(lib.b200kv_decode_attn(
         q.data_ptr(), q.stride(0), q.stride(1),
@@ -113,7 +59,7 @@ def decode_attention(q, k_cache, v_cache, out, qsl, seq_lens, block_table,
         out.data_ptr(), out.stride(0), out.stride(1),
         qsl.data_ptr(), seq_lens.data_ptr(), block_table.data_ptr(), block_table.stride(0),
         ks.data_ptr(), vs.data_ptr(), float(sm_scale),
-        num_seqs, hq, hkv, d, pblk, maxblk, int(max_seq_len_hint),
-        kv_dtype, 1 if out_by_qsl else 0, int(num_splits),
-        buf.data_ptr(), buf.numel(), stream), "b200kv_decode_attn")
+        block_table.shape[0], q.shape[1], k_cache.shape[2], q.shape[2], k_cache.shape[1],
+        block_table.shape[1], int(max_seq_len_hint),
+        kv_dtype, 1 if out_by_qsl else 0, int(num_splits), stream), "b200kv_decode_attn")
     return out

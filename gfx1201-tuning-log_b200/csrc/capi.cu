@@ -48,8 +48,6 @@ int sm_major_current_device() {
 
 int mxfp4_gemv_launch(const void* W, const void* St, const void* X, void* out, int N, int K,
                       int M, void* stream);
-int decode_attn_workspace_size(int num_seqs, int hq, int hkv, int head_dim, int block_size,
-                               int max_blocks, int hint, int num_splits, size_t* bytes);
 int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                        const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
                        int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
@@ -57,7 +55,13 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        int64_t bt_stride, const float* k_scale, const float* v_scale,
                        float sm_scale, int num_seqs, int hq, int hkv, int head_dim,
                        int block_size, int max_blocks, int hint, int kv_dtype, int out_by_qsl,
-                       int num_splits, void* ws, size_t ws_bytes, void* stream);
+                       int num_splits, void* stream);
+
+int kv_write_launch(const void* key, int64_t k_st, int64_t k_sh, const void* value, int64_t v_st,
+                    int64_t v_sh, void* k_cache, void* v_cache, int64_t sk0, int64_t sk1,
+                    int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2, const int64_t* slots,
+                    const float* k_scale, const float* v_scale, int num_tokens, int hkv,
+                    int head_dim, int block_size, int kv_dtype, void* stream);
 
 void set_last_error(int e) { t_last_error = e; }
 
@@ -117,14 +121,6 @@ void h4mv_launch(const void* W, const void* St, const void* Xb, void* Out, int N
   b200kv::set_last_error(b200kv::mxfp4_gemv_launch(W, St, Xb, Out, N, K, M, stream));
 }
 
-int b200kv_decode_attn_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
-                                      int head_dim, int block_size, int max_blocks_per_seq,
-                                      int max_seq_len_hint, int num_splits, size_t* bytes_out) {
-  return b200kv::decode_attn_workspace_size(num_seqs, num_q_heads, num_kv_heads, head_dim,
-                                            block_size, max_blocks_per_seq, max_seq_len_hint,
-                                            num_splits, bytes_out);
-}
-
 int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                        const void* k_cache, const void* v_cache, int64_t sk0, int64_t sk1,
                        int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2, void* out,
@@ -133,12 +129,24 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
                        const float* k_scale, const float* v_scale, float sm_scale, int num_seqs,
                        int num_q_heads, int num_kv_heads, int head_dim, int block_size,
                        int max_blocks_per_seq, int max_seq_len_hint, int kv_dtype, int out_by_qsl,
-                       int num_splits, void* workspace, size_t workspace_bytes, void* stream) {
+                       int num_splits, void* stream) {
   return b200kv::decode_attn_launch(
       q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
       out_stride_tok, out_stride_head, qsl, seq_lens, block_table, bt_stride, k_scale, v_scale,
       sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
-      max_seq_len_hint, kv_dtype, out_by_qsl, num_splits, workspace, workspace_bytes, stream);
+      max_seq_len_hint, kv_dtype, out_by_qsl, num_splits, stream);
+}
+
+int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_head,
+                    const void* value, int64_t value_stride_tok, int64_t value_stride_head,
+                    void* k_cache, void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2,
+                    int64_t sv0, int64_t sv1, int64_t sv2, const int64_t* slot_mapping,
+                    const float* k_scale, const float* v_scale, int num_tokens, int num_kv_heads,
+                    int head_dim, int block_size, int kv_dtype, void* stream) {
+  return b200kv::kv_write_launch(key, key_stride_tok, key_stride_head, value, value_stride_tok,
+                                 value_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1,
+                                 sv2, slot_mapping, k_scale, v_scale, num_tokens, num_kv_heads,
+                                 head_dim, block_size, kv_dtype, stream);
 }
 
 }  // extern "C"

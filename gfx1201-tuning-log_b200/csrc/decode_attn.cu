@@ -8,24 +8,26 @@
 //
 // B200 design (CUDA cores, no tensor cores -- the work is 4 multiply-adds per
 // KV byte at GQA 4 and the kernel is HBM-bound):
-//  * One CTA (4 warps) per (split, kv head, sequence).  A split is a span of at
-//    most 256 tokens.  At entry the CTA hands every 128-byte K row and V row of
-//    its span to the TMA engine as one-dimensional bulk copies into shared
-//    memory (two mbarriers: K lands first), so the whole span is in flight at
-//    once -- the memory-level parallelism the HBM needs -- and the block table
-//    gather costs one cached int load per row.
+//  * One thread-block CLUSTER of CS CTAs (CS <= 16) per (sequence, kv head);
+//    CTA r of the cluster owns an equal share of the context.  The shares'
+//    (m, l, o) partials are merged through distributed shared memory at the
+//    end, so there is no global scratch, no atomic and no second launch.
+//  * A CTA (16 warps; 8 for GQA 8) streams its share in 128-token chunks with 16-byte
+//    asynchronous copies (cp.async) of every K and V row into a double-buffered
+//    shared-memory stage: the next chunk is in flight while the current one is
+//    computed.  The block-table gather is one cached int load per row.
 //  * Pass 1 (QK): 16 lanes per token, 8 dims per lane, fp8x2 -> f16x2 hardware
 //    converts, packed fp32 FMA (FFMA2) against the pre-scaled query held in
 //    registers, and a 16-lane reduce-scatter so each lane ends with one
 //    (token, head) score.  Scores go to shared memory in the log2 domain.
-//  * Because the span is resident, the softmax is exact per span (no online
-//    rescaling): max, exp2, sum per head, then Pass 2 (PV) accumulates
-//    p * V in fp32 registers and a shared-memory reduction folds the 8 token
-//    groups.
-//  * Splits write (m, l, o) partials; the last CTA of a (sequence, kv head) --
-//    found with one atomic on a self-resetting counter -- merges them with the
-//    log-sum-exp weights of fp8kv_v3.py:97-113 and writes bf16.  One launch.
+//  * The softmax is exact inside a chunk (max, exp2, sum per head); chunks are
+//    merged online (running max and sum, one rescale of the fp32 accumulators
+//    per chunk).  Pass 2 (PV) accumulates p * V with FFMA2 and a shared-memory
+//    reduction folds the token groups.
+//  * The log-sum-exp merge of the cluster's partials is the one the reference
+//    does in its reduce kernel (fp8kv_v3.py:97-113).
 
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -35,11 +37,13 @@
 #include "b200kv.h"
 #include "b200kv_common.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace b200kv {
 
 constexpr int kHeadDim = 128;
-constexpr int kSpanMax = 256;
-constexpr int kDecodeThreads = 128;
+constexpr int kChunk = 128;          // tokens staged per pipeline stage
+constexpr int kMaxCluster = 16;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct DecodeParams {
@@ -57,10 +61,7 @@ struct DecodeParams {
   const float* k_scale;
   const float* v_scale;
   float sm_scale;
-  int num_seqs, hkv, block_size, span, max_splits, out_by_qsl;
-  int* counters;   // [num_seqs * hkv]
-  float* part_ml;  // [num_seqs][hkv][max_splits][GQA][2]
-  float* part_o;   // [num_seqs][hkv][max_splits][GQA][128]
+  int block_size, out_by_qsl;
 };
 
 namespace {
@@ -99,12 +100,6 @@ struct KvConvert<false> {
   }
 };
 
-// K+V staging region; after pass 2 it holds the [8 groups][GQA][128] fp32
-// reduction, so it is at least that large.
-__host__ __device__ constexpr int kv_region_bytes(int span, int rb, int gqa) {
-  return (2 * span * rb > 8 * gqa * kHeadDim * 4) ? 2 * span * rb : 8 * gqa * kHeadDim * 4;
-}
-
 // 16-lane reduce-scatter: on entry v[0..15] are this lane's partials; on exit
 // v[0] holds the sum over the 16 lanes of entry v[sub] (sub = lane % 16).
 __device__ __forceinline__ void reduce_scatter16(float (&v)[16], int sub) {
@@ -120,78 +115,77 @@ __device__ __forceinline__ void reduce_scatter16(float (&v)[16], int sub) {
   }
 }
 
+template <int GQA>
+struct DecodeSmem {
+  float sc[GQA][kChunk];      // scores of the chunk (log2 domain)
+  float pt[kChunk][GQA];      // probabilities, token-major for pass 2
+  float part_o[GQA][kHeadDim];  // this CTA's unnormalised o (read by cluster peers)
+  float part_m[8], part_l[8];   // this CTA's running max / sum (read by peers)
+  float alpha[8];               // per-chunk rescale of the running o
+  float run_m[8], run_l[8];
+  float comb_m[8], comb_l[8];
+};
+
+// Threads per CTA: 512 (32 token groups of 16 lanes) keeps 16 warps per SM busy
+// even when a (sequence, kv head) gets only one CTA per SM; GQA 8 needs twice
+// the query/accumulator registers per lane, so it runs 256 threads.
+template <int GQA>
+constexpr int decode_threads() { return GQA <= 4 ? 512 : 256; }
+
 template <int GQA, bool FP8>
-__global__ void __launch_bounds__(kDecodeThreads)
+__global__ void __launch_bounds__(decode_threads<GQA>())
     decode_attn_kernel(const DecodeParams p) {
   using Cvt = KvConvert<FP8>;
+  constexpr int NTHR = decode_threads<GQA>();
+  constexpr int NWARP = NTHR / 32;
+  constexpr int NG = NTHR / 16;       // 16-lane token groups
   constexpr int RB = Cvt::kRowBytes;
-  constexpr int TQ = 16 / GQA;  // tokens per 16-lane group step in pass 1
+  constexpr int CPR = RB / 16;        // 16-byte chunks per row
+  constexpr int TQ = 16 / GQA;        // tokens per 16-lane group step in pass 1
+  constexpr int STAGE = 2 * kChunk * RB;
+  static_assert(2 * STAGE >= NWARP * GQA * kHeadDim * 4, "stages must hold the warp reduction");
 
   extern __shared__ __align__(128) uint8_t smem[];
-  // layout (span = p.span): [K rows | V rows] (at least 8*GQA*128 floats, reused
-  // for the token-group reduction), scores [GQA][span], p [span][GQA], stats, barriers
-  const int span = p.span;
-  const int kv_bytes = kv_region_bytes(span, RB, GQA);
-  uint8_t* ks = smem;
-  uint8_t* vs = smem + span * RB;
-  float* sc = reinterpret_cast<float*>(smem + kv_bytes);  // [GQA][span]
-  float* pt = sc + GQA * span;                              // [span][GQA]
-  float* stat_m = pt + GQA * span;                          // [8]
-  float* stat_l = stat_m + 8;                               // [8]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(stat_l + 8); // [2]
-  int* flag = reinterpret_cast<int*>(bars + 2);
+  uint8_t* stages = smem;                                         // [2][K|V][kChunk][RB]
+  DecodeSmem<GQA>& S = *reinterpret_cast<DecodeSmem<GQA>*>(smem + 2 * STAGE);
 
-  const int sp = blockIdx.x;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int csize = (int)cluster.num_blocks();
   const int kh = blockIdx.y;
   const int seq = blockIdx.z;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int sub = lane & 15;
-  const int grp = tid >> 4;  // 0..7
+  const int grp = tid >> 4;  // 0..NG-1
 
-  const int seqlen = p.seq_lens[seq];
+  const int seqlen = max(p.seq_lens[seq], 0);
   const int q_tok = p.qsl[seq];
   const int out_row = p.out_by_qsl ? q_tok : seq;
-  const int lo = sp * p.span;
-  __nv_bfloat16* out_base = p.out + (int64_t)out_row * p.o_st + (int64_t)(kh * GQA) * p.o_sh;
-
-  if (seqlen <= 0) {
-    if (sp == 0)
-      for (int i = tid; i < GQA * kHeadDim; i += kDecodeThreads)
-        out_base[(int64_t)(i / kHeadDim) * p.o_sh + (i % kHeadDim)] = __float2bfloat16_rn(0.f);
-    return;
-  }
-  int nsplit = (seqlen + p.span - 1) / p.span;
-  if (nsplit > p.max_splits) {
-    if (sp == 0 && kh == 0 && tid == 0) atomicExch(&g_device_status, kDevSplitOverflow);
-    nsplit = p.max_splits;
-  }
-  if (lo >= seqlen || sp >= nsplit) return;
-  const int hi = min(seqlen, lo + p.span);
-  const int nt = hi - lo;
-
-  // ---- stage K and V rows of the span through the TMA engine ---------------
-  if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    fence_mbar_init();
-    mbar_arrive_expect_tx(&bars[0], (uint32_t)(nt * RB));
-    mbar_arrive_expect_tx(&bars[1], (uint32_t)(nt * RB));
-  }
-  __syncthreads();
+  // this CTA's token range: an equal share, rounded to 16 tokens
+  const int per = ((seqlen + csize - 1) / csize + 15) & ~15;
+  const int lo = min(seqlen, rank * per);
+  const int hi = min(seqlen, lo + per);
+  const int nchunks = (hi - lo + kChunk - 1) / kChunk;
   const int32_t* bt_row = p.bt + (int64_t)seq * p.bt_stride;
-  for (int i = tid; i < nt; i += kDecodeThreads) {
-    const int tok = lo + i;
-    const int64_t blk = bt_row[tok / p.block_size];
-    const int64_t slot = tok % p.block_size;
-    bulk_g2s(ks + i * RB, p.k + blk * p.sk0 + slot * p.sk1 + kh * p.sk2, RB, &bars[0]);
-  }
-  for (int i = tid; i < nt; i += kDecodeThreads) {
-    const int tok = lo + i;
-    const int64_t blk = bt_row[tok / p.block_size];
-    const int64_t slot = tok % p.block_size;
-    bulk_g2s(vs + i * RB, p.v + blk * p.sv0 + slot * p.sv1 + kh * p.sv2, RB, &bars[1]);
-  }
+
+  auto issue_chunk = [&](int c) {
+    uint8_t* ks = stages + (c & 1) * STAGE;
+    uint8_t* vs = ks + kChunk * RB;
+    const int t0 = lo + c * kChunk;
+    const int nt = min(kChunk, hi - t0);
+    for (int i = tid; i < nt * CPR; i += NTHR) {
+      const int r = i / CPR, ch = i % CPR;
+      const int tok = t0 + r;
+      const int64_t blk = bt_row[tok / p.block_size];
+      const int64_t slot = tok % p.block_size;
+      cp_async16(ks + r * RB + ch * 16, p.k + blk * p.sk0 + slot * p.sk1 + kh * p.sk2 + ch * 16);
+      cp_async16(vs + r * RB + ch * 16, p.v + blk * p.sv0 + slot * p.sv1 + kh * p.sv2 + ch * 16);
+    }
+    cp_async_commit();
+  };
+  if (nchunks > 0) issue_chunk(0);
 
   // ---- query: this lane's 8 dims of every GQA head, pre-scaled ------------
   const float qscale = p.sm_scale * (FP8 ? __ldg(p.k_scale) : 1.f) * kLog2e;
@@ -208,224 +202,230 @@ __global__ void __launch_bounds__(kDecodeThreads)
                                __uint_as_float(w[i] & 0xFFFF0000u) * qscale);
     }
   }
-
-  // ---- pass 1: scores ---------------------------------------------------------
-  if (__syncthreads_or(!mbar_wait_bounded(&bars[0], 0))) return;
-  // both 16-lane groups of a warp run the same trip count (full-warp shuffles)
-  for (int wbase = (tid >> 5) * 2 * TQ; wbase < nt; wbase += 8 * TQ) {
-    const int base = wbase + (grp & 1) * TQ;
-    float v[16];
-#pragma unroll
-    for (int i = 0; i < TQ; ++i) {
-      const int tok = base + i;
-      float2 kf[4];
-      if (tok < nt) {
-        Cvt::load8(ks + tok * RB + 8 * sub * (RB / kHeadDim), kf);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) kf[e] = make_float2(0.f, 0.f);
-      }
-#pragma unroll
-      for (int h = 0; h < GQA; ++h) {
-        float2 a = __fmul2_rn(qf[h][0], kf[0]);
-#pragma unroll
-        for (int e = 1; e < 4; ++e) a = __ffma2_rn(qf[h][e], kf[e], a);
-        v[i * GQA + h] = a.x + a.y;
-      }
-    }
-    reduce_scatter16(v, sub);
-    const int tok = base + sub / GQA;
-    if (tok < nt) sc[(sub % GQA) * span + tok] = v[0];
+  if (tid < 8) {
+    S.run_m[tid] = -INFINITY;
+    S.run_l[tid] = 0.f;
   }
-  __syncthreads();
-
-  // ---- exact softmax statistics of the span, per head -----------------------
-  const int warp = tid >> 5;
-  for (int h = warp; h < GQA; h += kDecodeThreads / 32) {
-    float m = -INFINITY;
-    for (int t = lane; t < nt; t += 32) m = fmaxf(m, sc[h * span + t]);
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int t = lane; t < nt; t += 32) {
-      const float e = exp2f(sc[h * span + t] - m);
-      pt[t * GQA + h] = e;
-      l += e;
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) {
-      stat_m[h] = m;
-      stat_l[h] = l;
-    }
-  }
-  __syncthreads();
-
-  // ---- pass 2: o = sum_t p[t] * V[t] ---------------------------------------
-  if (__syncthreads_or(!mbar_wait_bounded(&bars[1], 0))) return;
   float2 of[GQA][4];
 #pragma unroll
   for (int h = 0; h < GQA; ++h)
 #pragma unroll
     for (int e = 0; e < 4; ++e) of[h][e] = make_float2(0.f, 0.f);
-  for (int tok = grp; tok < nt; tok += 8) {
-    float2 vf[4];
-    Cvt::load8(vs + tok * RB + 8 * sub * (RB / kHeadDim), vf);
-    float pw[GQA];
-    if constexpr (GQA == 4) {
-      const float4 p4 = *reinterpret_cast<const float4*>(pt + tok * 4);
-      pw[0] = p4.x; pw[1] = p4.y; pw[2] = p4.z; pw[3] = p4.w;
+
+  for (int c = 0; c < nchunks; ++c) {
+    __syncthreads();  // stage (c+1)&1 and the score buffers are free again
+    if (c + 1 < nchunks) {
+      issue_chunk(c + 1);
+      cp_async_wait<1>();
     } else {
-#pragma unroll
-      for (int h = 0; h < GQA; ++h) pw[h] = pt[tok * GQA + h];
+      cp_async_wait<0>();
     }
+    __syncthreads();
+    const uint8_t* ks = stages + (c & 1) * STAGE;
+    const uint8_t* vs = ks + kChunk * RB;
+    const int nt = min(kChunk, hi - (lo + c * kChunk));
+
+    // ---- pass 1: scores (both 16-lane groups of a warp run the same trips) --
+    for (int wbase = warp * 2 * TQ; wbase < nt; wbase += NG * TQ) {
+      const int base = wbase + (grp & 1) * TQ;
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < TQ; ++i) {
+        const int tok = base + i;
+        float2 kf[4];
+        if (tok < nt) {
+          Cvt::load8(ks + tok * RB + 8 * sub * (RB / kHeadDim), kf);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) kf[e] = make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int h = 0; h < GQA; ++h) {
+          float2 a = __fmul2_rn(qf[h][0], kf[0]);
+#pragma unroll
+          for (int e = 1; e < 4; ++e) a = __ffma2_rn(qf[h][e], kf[e], a);
+          v[i * GQA + h] = a.x + a.y;
+        }
+      }
+      reduce_scatter16(v, sub);
+      const int tok = base + sub / GQA;
+      if (tok < nt) S.sc[sub % GQA][tok] = v[0];
+    }
+    __syncthreads();
+
+    // ---- chunk statistics and online merge into the running state ---------
+    for (int h = warp; h < GQA; h += NWARP) {
+      float m = -INFINITY;
+      for (int t = lane; t < nt; t += 32) m = fmaxf(m, S.sc[h][t]);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float m_old = S.run_m[h];
+      const float m_new = fmaxf(m_old, m);
+      float l = 0.f;
+      for (int t = lane; t < nt; t += 32) {
+        const float e = exp2f(S.sc[h][t] - m_new);
+        S.pt[t][h] = e;
+        l += e;
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+      if (lane == 0) {
+        const float a = exp2f(m_old - m_new);  // 0 on the first chunk
+        S.alpha[h] = a;
+        S.run_l[h] = S.run_l[h] * a + l;
+        S.run_m[h] = m_new;
+      }
+    }
+    __syncthreads();
+
+    // ---- pass 2: o = o * alpha + sum_t p[t] * V[t] --------------------------
 #pragma unroll
     for (int h = 0; h < GQA; ++h) {
-      const float2 pp = make_float2(pw[h], pw[h]);
+      const float2 a2 = make_float2(S.alpha[h], S.alpha[h]);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) of[h][e] = __ffma2_rn(pp, vf[e], of[h][e]);
+      for (int e = 0; e < 4; ++e) of[h][e] = __fmul2_rn(of[h][e], a2);
+    }
+    for (int tok = grp; tok < nt; tok += NG) {
+      float2 vf[4];
+      Cvt::load8(vs + tok * RB + 8 * sub * (RB / kHeadDim), vf);
+      float pw[GQA];
+      if constexpr (GQA == 4) {
+        const float4 p4 = *reinterpret_cast<const float4*>(&S.pt[tok][0]);
+        pw[0] = p4.x; pw[1] = p4.y; pw[2] = p4.z; pw[3] = p4.w;
+      } else {
+#pragma unroll
+        for (int h = 0; h < GQA; ++h) pw[h] = S.pt[tok][h];
+      }
+#pragma unroll
+      for (int h = 0; h < GQA; ++h) {
+        const float2 pp = make_float2(pw[h], pw[h]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) of[h][e] = __ffma2_rn(pp, vf[e], of[h][e]);
+      }
     }
   }
-  __syncthreads();  // K region is free now: reuse it for the group reduction
-  float* red = reinterpret_cast<float*>(ks);  // [8 groups][GQA][128]
+
+  // ---- fold the token groups: this CTA's unnormalised partial ---------------
+  // (the two groups of a warp through a shuffle, the warps through the staging
+  // buffers, which are free now)
 #pragma unroll
-  for (int h = 0; h < GQA; ++h) {
-    float4* dst = reinterpret_cast<float4*>(red + (grp * GQA + h) * kHeadDim + 8 * sub);
-    dst[0] = make_float4(of[h][0].x, of[h][0].y, of[h][1].x, of[h][1].y);
-    dst[1] = make_float4(of[h][2].x, of[h][2].y, of[h][3].x, of[h][3].y);
+  for (int h = 0; h < GQA; ++h)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      of[h][e].x += __shfl_xor_sync(0xffffffffu, of[h][e].x, 16);
+      of[h][e].y += __shfl_xor_sync(0xffffffffu, of[h][e].y, 16);
+    }
+  __syncthreads();
+  float (*red)[GQA][kHeadDim] = reinterpret_cast<float (*)[GQA][kHeadDim]>(stages);
+  if (lane < 16) {
+#pragma unroll
+    for (int h = 0; h < GQA; ++h) {
+      float4* dst = reinterpret_cast<float4*>(&red[warp][h][8 * sub]);
+      dst[0] = make_float4(of[h][0].x, of[h][0].y, of[h][1].x, of[h][1].y);
+      dst[1] = make_float4(of[h][2].x, of[h][2].y, of[h][3].x, of[h][3].y);
+    }
   }
   __syncthreads();
-
-  const int d = tid;  // kDecodeThreads == kHeadDim
-  float o_acc[GQA];
-#pragma unroll
-  for (int h = 0; h < GQA; ++h) {
+  for (int e = tid; e < GQA * kHeadDim; e += NTHR) {
+    const int h = e / kHeadDim, d = e % kHeadDim;
     float s = 0.f;
 #pragma unroll
-    for (int g = 0; g < 8; ++g) s += red[(g * GQA + h) * kHeadDim + d];
-    o_acc[h] = s;
+    for (int w = 0; w < NWARP; ++w) s += red[w][h][d];
+    S.part_o[h][d] = s;
+  }
+  if (tid < GQA) {
+    S.part_m[tid] = S.run_m[tid];
+    S.part_l[tid] = S.run_l[tid];
   }
   const float vsc = FP8 ? __ldg(p.v_scale) : 1.f;
+  __nv_bfloat16* out_base = p.out + (int64_t)out_row * p.o_st + (int64_t)(kh * GQA) * p.o_sh;
 
-  if (nsplit == 1) {
-#pragma unroll
-    for (int h = 0; h < GQA; ++h)
-      out_base[(int64_t)h * p.o_sh + d] = __float2bfloat16_rn(o_acc[h] * vsc / stat_l[h]);
-    return;
-  }
-
-  // ---- split partials + last-arriver combine ---------------------------------
-  const int64_t pair = (int64_t)seq * p.hkv + kh;
-  const int64_t pbase = (pair * p.max_splits + sp) * GQA;
-#pragma unroll
-  for (int h = 0; h < GQA; ++h) p.part_o[(pbase + h) * kHeadDim + d] = o_acc[h];
+  // ---- merge the cluster's partials through distributed shared memory -----
+  cluster.sync();
   if (tid < GQA) {
-    p.part_ml[(pbase + tid) * 2 + 0] = stat_m[tid];
-    p.part_ml[(pbase + tid) * 2 + 1] = stat_l[tid];
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int old = atomicAdd(&p.counters[pair], 1);
-    *flag = (old == nsplit - 1);
-  }
-  __syncthreads();
-  if (!*flag) return;
-  __threadfence();
-
-  const int64_t pb0 = pair * p.max_splits * GQA;
-  for (int h = warp; h < GQA; h += kDecodeThreads / 32) {
     float mg = -INFINITY;
-    for (int s = lane; s < nsplit; s += 32) mg = fmaxf(mg, __ldcg(&p.part_ml[(pb0 + s * GQA + h) * 2]));
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));
+    for (int r = 0; r < csize; ++r) mg = fmaxf(mg, cluster.map_shared_rank(&S.part_m[0], r)[tid]);
     float lg = 0.f;
-    for (int s = lane; s < nsplit; s += 32)
-      lg += exp2f(__ldcg(&p.part_ml[(pb0 + s * GQA + h) * 2]) - mg) *
-            __ldcg(&p.part_ml[(pb0 + s * GQA + h) * 2 + 1]);
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) lg += __shfl_xor_sync(0xffffffffu, lg, o);
-    if (lane == 0) {
-      stat_m[h] = mg;
-      stat_l[h] = lg;
-    }
+    if (mg != -INFINITY)
+      for (int r = 0; r < csize; ++r)
+        lg += exp2f(cluster.map_shared_rank(&S.part_m[0], r)[tid] - mg) *
+              cluster.map_shared_rank(&S.part_l[0], r)[tid];
+    S.comb_m[tid] = mg;
+    S.comb_l[tid] = lg;
   }
   __syncthreads();
-#pragma unroll
-  for (int h = 0; h < GQA; ++h) {
-    const float mg = stat_m[h];
+  // rank r writes elements [r*E/csize, (r+1)*E/csize) of the GQA x 128 output
+  constexpr int E = GQA * kHeadDim;
+  const int e0 = rank * E / csize, e1 = (rank + 1) * E / csize;
+  for (int e = e0 + tid; e < e1; e += NTHR) {
+    const int h = e / kHeadDim, d = e % kHeadDim;
+    const float mg = S.comb_m[h];
     float acc = 0.f;
-    for (int s = 0; s < nsplit; ++s)
-      acc += exp2f(__ldcg(&p.part_ml[(pb0 + s * GQA + h) * 2]) - mg) *
-             __ldcg(&p.part_o[(pb0 + s * GQA + h) * kHeadDim + d]);
-    out_base[(int64_t)h * p.o_sh + d] = __float2bfloat16_rn(acc * vsc / stat_l[h]);
+    if (mg != -INFINITY)
+      for (int r = 0; r < csize; ++r)
+        acc += exp2f(cluster.map_shared_rank(&S.part_m[0], r)[h] - mg) *
+               cluster.map_shared_rank(&S.part_o[0][0], r)[h * kHeadDim + d];
+    const float lg = S.comb_l[h];
+    out_base[(int64_t)h * p.o_sh + d] = __float2bfloat16_rn(lg > 0.f ? acc * vsc / lg : 0.f);
   }
-  if (tid == 0) p.counters[pair] = 0;  // ready for the next call
-}
-
-size_t decode_smem_bytes(int span, bool fp8, int gqa) {
-  const int rb = fp8 ? kHeadDim : 2 * kHeadDim;
-  return (size_t)kv_region_bytes(span, rb, gqa) + 2 * (size_t)gqa * span * sizeof(float) +
-         16 * sizeof(float) + 2 * sizeof(uint64_t) + 16;
+  cluster.sync();  // peers' shared memory stays alive until every rank is done
 }
 
 template <int GQA, bool FP8>
-cudaError_t launch_decode(const DecodeParams& p, dim3 grid, cudaStream_t stream) {
-  const size_t smem = decode_smem_bytes(p.span, FP8, GQA);
+size_t decode_smem_bytes() {
+  const size_t rb = FP8 ? kHeadDim : 2 * kHeadDim;
+  return 2 * 2 * kChunk * rb + sizeof(DecodeSmem<GQA>);
+}
+
+template <int GQA, bool FP8>
+cudaError_t launch_decode(const DecodeParams& p, int csize, int hkv, int num_seqs,
+                          cudaStream_t stream) {
+  const size_t smem = decode_smem_bytes<GQA, FP8>();
   cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<GQA, FP8>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  decode_attn_kernel<GQA, FP8><<<grid, kDecodeThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  if (csize > 8) {
+    e = cudaFuncSetAttribute(decode_attn_kernel<GQA, FP8>,
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(csize, hkv, num_seqs);
+  lc.blockDim = dim3(decode_threads<GQA>(), 1, 1);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, decode_attn_kernel<GQA, FP8>, p);
 }
 
 }  // namespace
 
-// Split geometry shared by the workspace-size query and the launch.
-struct DecodePlan {
-  int span, max_splits;
-  size_t off_counters, off_ml, off_o, total;
-};
-
-static int decode_plan(int num_seqs, int hq, int hkv, int block_size, int max_blocks, int hint,
-                       int num_splits, DecodePlan* plan) {
-  if (num_seqs <= 0 || hq <= 0 || hkv <= 0 || block_size <= 0 || max_blocks <= 0)
-    return B200KV_ERR_INVALID_ARG;
-  if (hq % hkv) return B200KV_ERR_INVALID_ARG;
-  const int ctx = hint > 0 ? hint : max_blocks * block_size;
-  int span;
-  if (num_splits > 0) {
-    span = cdiv(ctx, num_splits);
+// Cluster size (CTAs per (sequence, kv head)): the largest power of two <= 16
+// that keeps the grid within one CTA per SM, but at least one CTA per 4096
+// tokens of the context bound, and at least 64 tokens per CTA.
+int decode_cluster_size(int num_seqs, int hkv, int ctx_bound, int requested) {
+  int want;
+  if (requested > 0) {
+    want = requested;
   } else {
     const int sms = num_sms_current_device() > 0 ? num_sms_current_device() : 148;
     const int pairs = num_seqs * hkv;
-    const int splits = cdiv(4 * sms, pairs);
-    span = cdiv(ctx, splits);
-    if (span < 64) span = 64;
+    want = 1;
+    while (want * 2 <= kMaxCluster && pairs * want * 2 <= sms) want *= 2;
+    const int need = cdiv(ctx_bound, 4096);
+    if (want < need) want = need;
+    const int cap = cdiv(ctx_bound, 64);
+    if (want > cap) want = cap;
   }
-  span = (span + 15) & ~15;
-  if (span > kSpanMax) span = kSpanMax;
-  if (span < 16) span = 16;
-  plan->span = span;
-  plan->max_splits = cdiv(ctx, span);
-  const int gqa = hq / hkv;
-  const size_t pairs = (size_t)num_seqs * hkv;
-  plan->off_counters = 0;
-  plan->off_ml = align_up(pairs * sizeof(int), 256);
-  plan->off_o = plan->off_ml + align_up(pairs * plan->max_splits * gqa * 2 * sizeof(float), 256);
-  plan->total = plan->off_o + align_up(pairs * plan->max_splits * gqa * kHeadDim * sizeof(float), 256);
-  return B200KV_OK;
-}
-
-int decode_attn_workspace_size(int num_seqs, int hq, int hkv, int head_dim, int block_size,
-                               int max_blocks, int hint, int num_splits, size_t* bytes) {
-  if (!bytes) return B200KV_ERR_INVALID_ARG;
-  if (head_dim != kHeadDim) return B200KV_ERR_UNSUPPORTED;
-  DecodePlan plan;
-  const int rc = decode_plan(num_seqs, hq, hkv, block_size, max_blocks, hint, num_splits, &plan);
-  if (rc) return rc;
-  *bytes = plan.total;
-  return B200KV_OK;
+  int cs = 1;
+  while (cs < want && cs < kMaxCluster) cs *= 2;
+  return cs;
 }
 
 int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
@@ -435,21 +435,19 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        int64_t bt_stride, const float* k_scale, const float* v_scale,
                        float sm_scale, int num_seqs, int hq, int hkv, int head_dim,
                        int block_size, int max_blocks, int hint, int kv_dtype, int out_by_qsl,
-                       int num_splits, void* ws, size_t ws_bytes, void* stream) {
+                       int num_splits, void* stream) {
   if (!q || !k_cache || !v_cache || !out || !qsl || !seq_lens || !bt) return B200KV_ERR_INVALID_ARG;
+  if (num_seqs <= 0 || hq <= 0 || hkv <= 0 || block_size <= 0 || max_blocks <= 0)
+    return B200KV_ERR_INVALID_ARG;
+  if (hq % hkv) return B200KV_ERR_INVALID_ARG;
   if (head_dim != kHeadDim) return B200KV_ERR_UNSUPPORTED;
   if (kv_dtype != B200KV_KV_FP8_E4M3 && kv_dtype != B200KV_KV_BF16) return B200KV_ERR_UNSUPPORTED;
   const bool fp8 = kv_dtype == B200KV_KV_FP8_E4M3;
   if (fp8 && (!k_scale || !v_scale)) return B200KV_ERR_INVALID_ARG;
-  DecodePlan plan;
-  int rc = decode_plan(num_seqs, hq, hkv, block_size, max_blocks, hint, num_splits, &plan);
-  if (rc) return rc;
   const int gqa = hq / hkv;
   if (gqa != 1 && gqa != 2 && gqa != 4 && gqa != 8) return B200KV_ERR_UNSUPPORTED;
-  if (!ws || ws_bytes < plan.total) return B200KV_ERR_WORKSPACE;
-  if (reinterpret_cast<uintptr_t>(ws) & 255) return B200KV_ERR_MISALIGNED;
+  if (num_splits < 0 || num_splits > kMaxCluster) return B200KV_ERR_UNSUPPORTED;
   const int esz = fp8 ? 1 : 2;
-  // bulk copies need 16-byte aligned rows
   const int64_t strides[6] = {sk0, sk1, sk2, sv0, sv1, sv2};
   for (int i = 0; i < 6; ++i)
     if ((strides[i] * esz) % 16) return B200KV_ERR_MISALIGNED;
@@ -476,29 +474,22 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
   p.k_scale = k_scale;
   p.v_scale = v_scale;
   p.sm_scale = sm_scale;
-  p.num_seqs = num_seqs;
-  p.hkv = hkv;
   p.block_size = block_size;
-  p.span = plan.span;
-  p.max_splits = plan.max_splits;
   p.out_by_qsl = out_by_qsl;
-  uint8_t* w = static_cast<uint8_t*>(ws);
-  p.counters = reinterpret_cast<int*>(w + plan.off_counters);
-  p.part_ml = reinterpret_cast<float*>(w + plan.off_ml);
-  p.part_o = reinterpret_cast<float*>(w + plan.off_o);
 
-  const dim3 grid(plan.max_splits, hkv, num_seqs);
+  const int ctx = hint > 0 ? hint : max_blocks * block_size;
+  const int cs = decode_cluster_size(num_seqs, hkv, ctx, num_splits);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (gqa * 2 + (fp8 ? 1 : 0)) {
-    case 3: e = launch_decode<1, true>(p, grid, st); break;
-    case 2: e = launch_decode<1, false>(p, grid, st); break;
-    case 5: e = launch_decode<2, true>(p, grid, st); break;
-    case 4: e = launch_decode<2, false>(p, grid, st); break;
-    case 9: e = launch_decode<4, true>(p, grid, st); break;
-    case 8: e = launch_decode<4, false>(p, grid, st); break;
-    case 17: e = launch_decode<8, true>(p, grid, st); break;
-    case 16: e = launch_decode<8, false>(p, grid, st); break;
+    case 3: e = launch_decode<1, true>(p, cs, hkv, num_seqs, st); break;
+    case 2: e = launch_decode<1, false>(p, cs, hkv, num_seqs, st); break;
+    case 5: e = launch_decode<2, true>(p, cs, hkv, num_seqs, st); break;
+    case 4: e = launch_decode<2, false>(p, cs, hkv, num_seqs, st); break;
+    case 9: e = launch_decode<4, true>(p, cs, hkv, num_seqs, st); break;
+    case 8: e = launch_decode<4, false>(p, cs, hkv, num_seqs, st); break;
+    case 17: e = launch_decode<8, true>(p, cs, hkv, num_seqs, st); break;
+    case 16: e = launch_decode<8, false>(p, cs, hkv, num_seqs, st); break;
     default: return B200KV_ERR_UNSUPPORTED;
   }
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;

@@ -6,19 +6,20 @@ Same signature and argument meaning.  Differences a caller can observe:
   * TILE / warps / stages are accepted and ignored (they tuned the Triton
     kernel's tile shape); `nsplit` is a split-count request -- None (default)
     lets the library size the splits for the B200's 148 SMs, an int asks for
-    that many spans of the context bound, each capped at 256 tokens.
-  * `scratch` may be a DecodeWorkspace (or None for the per-device default).
-    The reference's 3-tuple of fp32 buffers is accepted and ignored: the
-    partials live in the library workspace.
+    that many CTAs per (sequence, kv head), rounded up to a power of two <= 16.
+  * `scratch` is accepted and ignored: the split partials are merged inside a
+    thread-block cluster through distributed shared memory, so the kernel
+    needs no global scratch.
+  * `max_seq_len` (extra, optional) is a host-side bound on seq_lens used to
+    size the splits; without it the block table width bounds the context.
   * Sequences with seq_len == 0 produce zeros (the reference divides 0 by 0).
 Like the reference, the output row of sequence s is `out[s]` (fp8kv_v3.py:112).
 """
-from _decode import DecodeWorkspace, decode_attention
+from _decode import decode_attention
 
 
 def run(q, k_cache, v_cache, out, qsl, slens, bt, kscale, vscale, sm_scale,
         TILE=32, warps=4, stages=3, nsplit=None, scratch=None, max_seq_len=0):
-    ws = scratch if isinstance(scratch, DecodeWorkspace) else None
     decode_attention(q, k_cache, v_cache, out, qsl, slens, bt, kscale, vscale, sm_scale,
                      out_by_qsl=False, num_splits=int(nsplit or 0),
-                     max_seq_len_hint=int(max_seq_len or 0), workspace=ws)
+                     max_seq_len_hint=int(max_seq_len or 0))

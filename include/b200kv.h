@@ -109,20 +109,12 @@ void h4mv_launch(const void* W, const void* St, const void* Xb, void* Out,
  *   block_table  int32 [num_seqs, >= max_blocks_per_seq], row stride bt_stride
  *   k/v_scale    device fp32 scalars (ignored for bf16 KV)
  *   head_dim must be 128; GQA must be 1, 2, 4 or 8.
- *   num_splits   0 = choose automatically; otherwise the context bound
- *                (max_seq_len_hint, or max_blocks_per_seq*block_size when the hint
- *                is 0) is cut into num_splits spans, each at most 256 tokens.
- *   workspace    device buffer of at least b200kv_decode_attn_workspace_size()
- *                bytes, 256-B aligned, ZERO-FILLED before its first use; the kernels
- *                leave it zero-filled where it matters (a per-(seq, kv head) arrival
- *                counter), so it can be reused by later calls on the same stream.
- *                Calls that overlap in time must not share a workspace.
+ *   num_splits   CTAs (a thread-block cluster) that share one (sequence, kv head):
+ *                0 = choose from the SM count and the context bound (max_seq_len_hint,
+ *                or max_blocks_per_seq*block_size when the hint is 0); otherwise a
+ *                request, rounded up to a power of two, at most 16.
+ * No workspace: the split partials are merged through distributed shared memory.
  */
-int b200kv_decode_attn_workspace_size(int num_seqs, int num_q_heads, int num_kv_heads,
-                                      int head_dim, int block_size, int max_blocks_per_seq,
-                                      int max_seq_len_hint, int num_splits,
-                                      size_t* bytes_out);
-
 int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                        const void* k_cache, const void* v_cache,
                        int64_t sk0, int64_t sk1, int64_t sk2,
@@ -133,8 +125,34 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
                        const float* k_scale, const float* v_scale, float sm_scale,
                        int num_seqs, int num_q_heads, int num_kv_heads, int head_dim,
                        int block_size, int max_blocks_per_seq, int max_seq_len_hint,
-                       int kv_dtype, int out_by_qsl, int num_splits,
-                       void* workspace, size_t workspace_bytes, void* stream);
+                       int kv_dtype, int out_by_qsl, int num_splits, void* stream);
+
+/* ---- paged KV-cache write ------------------------------------------------------
+ *
+ * For every token t < num_tokens with slot = slot_mapping[t] >= 0:
+ *   k_cache[slot / block_size, slot % block_size, h, :] = q8(key[t, h, :] / k_scale)
+ *   v_cache[...same...]                                 = q8(value[t, h, :] / v_scale)
+ * where q8 is fp32 IEEE division then round-to-nearest-even e4m3 with saturation to
+ * +-448 (kv_dtype FP8_E4M3), or a plain copy (kv_dtype BF16, scales ignored).
+ * Negative slots (padding tokens) are skipped.
+ *
+ * Replaces vLLM's reshape_and_cache_flash custom op, which the reference's engine
+ * runs ahead of its attention kernels (profiling/prof_h4mv.txt:9); same slot and
+ * quantisation semantics.
+ *
+ *   key/value   bf16 [num_tokens, num_kv_heads, head_dim], strides (st, sh, 1)
+ *   k/v_cache   [NB, block_size, num_kv_heads, head_dim], strides (s*0, s*1, s*2, 1)
+ *   slot_mapping int64 [num_tokens]; k/v_scale device fp32 scalars
+ *   head_dim % 16 == 0; cache rows 16-byte aligned.
+ */
+int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_head,
+                    const void* value, int64_t value_stride_tok, int64_t value_stride_head,
+                    void* k_cache, void* v_cache,
+                    int64_t sk0, int64_t sk1, int64_t sk2,
+                    int64_t sv0, int64_t sv1, int64_t sv2,
+                    const int64_t* slot_mapping, const float* k_scale, const float* v_scale,
+                    int num_tokens, int num_kv_heads, int head_dim, int block_size,
+                    int kv_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -22,7 +22,7 @@ def declared_functions():
 def test_header_declares_expected_entry_points():
     names = declared_functions()
     for must in ("b200kv_mxfp4_gemv", "h4mv_launch", "b200kv_decode_attn",
-                 "b200kv_decode_attn_workspace_size", "b200kv_status_string"):
+                 "b200kv_kv_write", "b200kv_status_string"):
         assert must in names
 
 
@@ -65,7 +65,7 @@ def _decode_call(lib, **over):
     args = dict(q=A, qst=32 * 128, qsh=128, k=A, v=A, sk0=16 * 8 * 128, sk1=8 * 128, sk2=128,
                 sv0=16 * 8 * 128, sv1=8 * 128, sv2=128, out=A, ost=32 * 128, osh=128,
                 qsl=A, sl=A, bt=A, bts=4, ks=A, vs=A, sm=0.088, ns=2, hq=32, hkv=8, d=128,
-                pblk=16, maxblk=4, hint=0, kvdt=0, obq=0, nsplit=0, ws=A, wsb=1 << 30, st=None)
+                pblk=16, maxblk=4, hint=0, kvdt=0, obq=0, nsplit=0, st=None)
     args.update(over)
     a = args
     return lib.b200kv_decode_attn(a["q"], a["qst"], a["qsh"], a["k"], a["v"], a["sk0"], a["sk1"],
@@ -73,7 +73,7 @@ def _decode_call(lib, **over):
                                   a["osh"], a["qsl"], a["sl"], a["bt"], a["bts"], a["ks"], a["vs"],
                                   a["sm"], a["ns"], a["hq"], a["hkv"], a["d"], a["pblk"],
                                   a["maxblk"], a["hint"], a["kvdt"], a["obq"], a["nsplit"],
-                                  a["ws"], a["wsb"], a["st"])
+                                  a["st"])
 
 
 def test_decode_argument_validation(b200):
@@ -84,8 +84,7 @@ def test_decode_argument_validation(b200):
     assert _decode_call(lib, hq=30) == 1           # not a multiple of HKV
     assert _decode_call(lib, kvdt=7) == 2
     assert _decode_call(lib, ks=None) == 1         # fp8 needs scales
-    assert _decode_call(lib, wsb=16) == 4
-    assert _decode_call(lib, ws=0x10010) == 3      # workspace not 256-B aligned
+    assert _decode_call(lib, nsplit=17) == 2       # more than 16 CTAs per cluster
     assert _decode_call(lib, sk1=8 * 128 + 1) == 3  # row not 16-B aligned
     assert _decode_call(lib, k=0x10008) == 3
 
@@ -95,10 +94,22 @@ def test_decode_no_device(b200):
     assert _decode_call(b200.lib) == 6
 
 
-def test_decode_workspace_size(b200):
-    import _decode
-    a = _decode.workspace_size(1, 32, 8, 128, 16, 256)
-    b = _decode.workspace_size(8, 32, 8, 128, 16, 256)
-    assert 0 < a < b
-    with pytest.raises(b200.B200KVError):
-        _decode.workspace_size(1, 32, 8, 64, 16, 256)
+def test_kv_write_argument_validation(b200):
+    lib = b200.lib
+    A = 0x10000
+
+    def call(**o):
+        a = dict(key=A, kst=1024, ksh=128, val=A, vst=1024, vsh=128, kc=A, vc=A, sk0=16384,
+                 sk1=1024, sk2=128, sv0=16384, sv1=1024, sv2=128, slots=A, ks=A, vs=A, T=4,
+                 hkv=8, d=128, pblk=16, dt=0)
+        a.update(o)
+        return lib.b200kv_kv_write(a["key"], a["kst"], a["ksh"], a["val"], a["vst"], a["vsh"],
+                                   a["kc"], a["vc"], a["sk0"], a["sk1"], a["sk2"], a["sv0"],
+                                   a["sv1"], a["sv2"], a["slots"], a["ks"], a["vs"], a["T"],
+                                   a["hkv"], a["d"], a["pblk"], a["dt"], None)
+    assert call(key=None) == 1
+    assert call(d=24) == 2
+    assert call(dt=5) == 2
+    assert call(ks=None) == 1
+    assert call(sk1=1000) == 3
+    assert call(kst=1020) == 3

@@ -92,7 +92,7 @@ def test_ragged_lengths_all_gqa(cuda, gqa):
     _check(out, ref)
 
 
-@pytest.mark.parametrize("nsplit", [1, 2, 7, 64, 500])
+@pytest.mark.parametrize("nsplit", [1, 2, 3, 8, 16])
 def test_explicit_split_counts(cuda, nsplit):
     c = FO.make_decode_case(3, [3000, 17, 1500], seed=20)
     out = _run_v3(c, cuda, nsplit=nsplit)
@@ -115,8 +115,11 @@ def test_bf16_kv_cache(cuda):
 
 
 def test_scale_folding(cuda):
-    # fp8kv_v3.py:169-177: ks = 0.5, vs = 2.0
+    # fp8kv_v3.py:169-177: cache = (randn * 2) cast straight to fp8, then ks = 0.5, vs = 2.0
     c = FO.make_decode_case(2, [4096, 300], seed=40)
+    g = torch.Generator().manual_seed(41)
+    c["k_cache"] = (torch.randn(c["k_cache"].shape, generator=g) * 2).to(torch.float8_e4m3fn)
+    c["v_cache"] = (torch.randn(c["v_cache"].shape, generator=g) * 2).to(torch.float8_e4m3fn)
     c["k_scale"], c["v_scale"] = 0.5, 2.0
     out = _run_v3(c, cuda)
     ref = FO.decode_reference(c["q"], c["k_cache"], c["v_cache"], c["qsl"], c["seq_lens"],
@@ -173,21 +176,20 @@ def test_block_table_index_probe(cuda):
         assert torch.equal(out[0, 0], want), target
 
 
-def test_long_context_32k(cuda):
+@pytest.mark.parametrize("hint", [0, 32768])
+def test_long_context_32k(cuda, hint):
     c = FO.make_decode_case(2, [32768, 20000], hq=8, hkv=2, seed=80)
-    out = _run_v3(c, cuda)
+    out = _run_v3(c, cuda, max_seq_len=hint)
     ref = FO.decode_reference(c["q"], c["k_cache"], c["v_cache"], c["qsl"], c["seq_lens"],
                               c["block_table"], c["k_scale"], c["v_scale"], c["sm_scale"])
     _check(out, ref)
 
 
-def test_workspace_reuse_and_determinism(cuda):
-    from _decode import DecodeWorkspace
+def test_determinism(cuda):
     import _b200kv
     c = FO.make_decode_case(4, [4096, 33, 2000, 4096], seed=90)
-    ws = DecodeWorkspace(cuda)
-    a = _run_v3(c, cuda, scratch=ws)
-    b = _run_v3(c, cuda, scratch=ws)
+    a = _run_v3(c, cuda)
+    b = _run_v3(c, cuda)
     assert torch.equal(a, b)
     torch.cuda.synchronize()
     assert _b200kv.device_status() == 0
@@ -202,7 +204,7 @@ def test_cuda_graph_capture(cuda):
     out = torch.zeros(2, 32, 128, dtype=torch.bfloat16, device=cuda)
     args = (g["q"], g["k_cache"], g["v_cache"], out, g["qsl"], g["seq_lens"], g["block_table"],
             ks, vs, c["sm_scale"])
-    fp8kv_v3.run(*args)   # sizes the workspace outside the capture
+    fp8kv_v3.run(*args)
     graph = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
