@@ -6,26 +6,33 @@
 // heads of the sequence's query token attend over its paged K/V; k_scale is
 // folded into the score scale and v_scale is applied to the output.
 //
-// B200 design (CUDA cores, no tensor cores -- the work is 4 multiply-adds per
-// KV byte at GQA 4 and the kernel is HBM-bound):
+// B200 design.  The work is 4 multiply-adds per KV byte at GQA 4, and on CUDA
+// cores the fp8 -> fp32 converts, packed FMAs and cross-lane reductions cost
+// ~11 instructions per HBM byte (measured with ncu on the first version of
+// this kernel, 47% issue utilisation at 1.3 TB/s), far more than an HBM-bound
+// kernel can afford.  So the dot products run on the tensor pipe (mma.sync,
+// fp32 accumulation), the way the reference's own kernel used tl.dot
+// (fp8kv_v3.py:67,73), and the kernel stays HBM-bound:
 //  * One thread-block CLUSTER of CS CTAs (CS <= 16) per (sequence, kv head);
 //    CTA r of the cluster owns an equal share of the context.  The shares'
 //    (m, l, o) partials are merged through distributed shared memory at the
 //    end, so there is no global scratch, no atomic and no second launch.
-//  * A CTA (16 warps; 8 for GQA 8) streams its share in 128-token chunks with 16-byte
-//    asynchronous copies (cp.async) of every K and V row into a double-buffered
-//    shared-memory stage: the next chunk is in flight while the current one is
+//  * A CTA (4 warps) streams its share in 128-token chunks: one thread per K
+//    and V row issues 16-byte asynchronous copies (cp.async) into a
+//    double-buffered stage, so the next chunk is in flight while this one is
 //    computed.  The block-table gather is one cached int load per row.
-//  * Pass 1 (QK): 16 lanes per token, 8 dims per lane, fp8x2 -> f16x2 hardware
-//    converts, packed fp32 FMA (FFMA2) against the pre-scaled query held in
-//    registers, and a 16-lane reduce-scatter so each lane ends with one
-//    (token, head) score.  Scores go to shared memory in the log2 domain.
-//  * The softmax is exact inside a chunk (max, exp2, sum per head); chunks are
-//    merged online (running max and sum, one rescale of the fp32 accumulators
-//    per chunk).  Pass 2 (PV) accumulates p * V with FFMA2 and a shared-memory
-//    reduction folds the token groups.
-//  * The log-sum-exp merge of the cluster's partials is the one the reference
-//    does in its reduce kernel (fp8kv_v3.py:97-113).
+//  * Each warp owns 32 tokens of a chunk.  S^T = q K^T with the GQA heads as
+//    the 16 rows of the A operand (q, pre-scaled to f16 by an exact power of
+//    two per head) and 8 tokens as the B operand, read straight from the fp8
+//    rows with one 32-bit load and two fp8x2 -> f16x2 hardware converts
+//    (exact).  The S^T accumulator fragments ARE the B-operand fragments of
+//    O^T += V^T P^T, so P never leaves registers; V^T comes from ldmatrix.trans
+//    over the rows converted to f16 (exact).  P is rounded to f16 for the MMA
+//    (the reference rounds it to bf16, fp8kv_v3.py:73).
+//  * Online softmax per warp in the log2 domain; warps and cluster peers merge
+//    with the log-sum-exp weights of the reference's reduce (fp8kv_v3.py:97-113).
+//  * bf16 caches (fp8kv_kernel.py's K_FP8=False) run the same schedule with
+//    bf16 operands and no converts.
 
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
@@ -43,6 +50,8 @@ namespace b200kv {
 
 constexpr int kHeadDim = 128;
 constexpr int kChunk = 128;          // tokens staged per pipeline stage
+constexpr int kWarps = 4;            // each warp owns 32 tokens of a chunk
+constexpr int kThreads = kWarps * 32;
 constexpr int kMaxCluster = 16;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -61,93 +70,79 @@ struct DecodeParams {
   const float* k_scale;
   const float* v_scale;
   float sm_scale;
-  int block_size, out_by_qsl;
+  int block_size, bs_shift, out_by_qsl;  // bs_shift = log2(block_size) or -1
 };
 
 namespace {
 
-// 8 KV elements (one lane's 8 dims) -> 8 fp32.
-template <bool FP8>
-struct KvConvert;
-
-template <>
-struct KvConvert<true> {
-  static constexpr int kRowBytes = kHeadDim;
-  __device__ __forceinline__ static void load8(const uint8_t* p, float2 (&f)[4]) {
-    const uint2 raw = *reinterpret_cast<const uint2*>(p);
-    const uint32_t w[2] = {raw.x, raw.y};
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const __half2_raw lo =
-          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] & 0xFFFFu), __NV_E4M3);
-      const __half2_raw hi =
-          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> 16), __NV_E4M3);
-      f[2 * i] = __half22float2(*reinterpret_cast<const __half2*>(&lo));
-      f[2 * i + 1] = __half22float2(*reinterpret_cast<const __half2*>(&hi));
-    }
-  }
-};
-
-template <>
-struct KvConvert<false> {
-  static constexpr int kRowBytes = kHeadDim * 2;
-  __device__ __forceinline__ static void load8(const uint8_t* p, float2 (&f)[4]) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(p);
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      f[i] = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
-  }
-};
-
-// 16-lane reduce-scatter: on entry v[0..15] are this lane's partials; on exit
-// v[0] holds the sum over the 16 lanes of entry v[sub] (sub = lane % 16).
-__device__ __forceinline__ void reduce_scatter16(float (&v)[16], int sub) {
-#pragma unroll
-  for (int half = 8; half >= 1; half >>= 1) {
-    const bool upper = (sub & half) != 0;
-#pragma unroll
-    for (int j = 0; j < half; ++j) {
-      const float keep = upper ? v[j + half] : v[j];
-      const float send = upper ? v[j] : v[j + half];
-      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, half);
-    }
+// ---- small PTX helpers -----------------------------------------------------
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  uint32_t r;
+  asm("{\n .reg .b16 t;\n cvt.u16.u32 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}" : "=r"(r) : "r"(two_bytes));
+  return r;
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+template <bool F16>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (F16) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
   }
 }
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+
+// Shared-memory layout of one CTA.  K rows are padded so the 8 tokens x 4
+// lanes of a B-fragment load hit distinct banks; V rows that ldmatrix reads are
+// padded to 272 bytes so its 8 row addresses hit distinct 16-byte groups.
+template <bool FP8>
+struct Layout {
+  static constexpr int KP = FP8 ? 144 : 288;        // K row pitch (bytes)
+  static constexpr int VP = FP8 ? 128 : 272;        // V row pitch as staged
+  static constexpr int CP = 272;                    // f16 V row pitch after convert
+  static constexpr int STAGE = kChunk * (KP + VP);
+  static constexpr int VCONV = FP8 ? kWarps * 32 * CP : 0;
+  static constexpr int BYTES = 2 * STAGE + VCONV;
+};
 
 template <int GQA>
-struct DecodeSmem {
-  float sc[GQA][kChunk];      // scores of the chunk (log2 domain)
-  float pt[kChunk][GQA];      // probabilities, token-major for pass 2
-  float part_o[GQA][kHeadDim];  // this CTA's unnormalised o (read by cluster peers)
-  float part_m[8], part_l[8];   // this CTA's running max / sum (read by peers)
-  float alpha[8];               // per-chunk rescale of the running o
-  float run_m[8], run_l[8];
+struct DecodeShared {
+  float wm[kWarps][8], wl[kWarps][8];     // per-warp softmax state at the end
+  float part_o[GQA][kHeadDim];            // this CTA's unnormalised o (read by peers)
+  float part_m[8], part_l[8];             // this CTA's max / sum (read by peers)
   float comb_m[8], comb_l[8];
 };
 
-// Threads per CTA: 512 (32 token groups of 16 lanes) keeps 16 warps per SM busy
-// even when a (sequence, kv head) gets only one CTA per SM; GQA 8 needs twice
-// the query/accumulator registers per lane, so it runs 256 threads.
-template <int GQA>
-constexpr int decode_threads() { return GQA <= 4 ? 512 : 256; }
-
+// One CTA = 4 warps = one share of a (sequence, kv head)'s context; cluster
+// peers hold the other shares.  Per 128-token chunk each warp owns 32 tokens:
+//   S^T = q (A: 16 rows = the GQA heads, zero-padded) x K^T (B: 8 tokens)
+//   O^T += V^T (A: 16 dims x 16 tokens, ldmatrix.trans) x P^T (B: the S^T
+//          accumulator fragments rounded to f16 -- same register layout)
+// with an online softmax per warp; warps and cluster peers merge at the end.
 template <int GQA, bool FP8>
-__global__ void __launch_bounds__(decode_threads<GQA>())
-    decode_attn_kernel(const DecodeParams p) {
-  using Cvt = KvConvert<FP8>;
-  constexpr int NTHR = decode_threads<GQA>();
-  constexpr int NWARP = NTHR / 32;
-  constexpr int NG = NTHR / 16;       // 16-lane token groups
-  constexpr int RB = Cvt::kRowBytes;
-  constexpr int CPR = RB / 16;        // 16-byte chunks per row
-  constexpr int TQ = 16 / GQA;        // tokens per 16-lane group step in pass 1
-  constexpr int STAGE = 2 * kChunk * RB;
-  static_assert(2 * STAGE >= NWARP * GQA * kHeadDim * 4, "stages must hold the warp reduction");
-
+__global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeParams p) {
+  using L = Layout<FP8>;
+  constexpr int RB = FP8 ? kHeadDim : 2 * kHeadDim;  // bytes per cached row
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* stages = smem;                                         // [2][K|V][kChunk][RB]
-  DecodeSmem<GQA>& S = *reinterpret_cast<DecodeSmem<GQA>*>(smem + 2 * STAGE);
+  __shared__ DecodeShared<GQA> S;
 
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
@@ -157,185 +152,268 @@ __global__ void __launch_bounds__(decode_threads<GQA>())
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int sub = lane & 15;
-  const int grp = tid >> 4;  // 0..NG-1
+  const int g = lane >> 2;   // fragment row group: head (S^T) / token (K^T)
+  const int c = lane & 3;
 
   const int seqlen = max(p.seq_lens[seq], 0);
   const int q_tok = p.qsl[seq];
   const int out_row = p.out_by_qsl ? q_tok : seq;
-  // this CTA's token range: an equal share, rounded to 16 tokens
   const int per = ((seqlen + csize - 1) / csize + 15) & ~15;
   const int lo = min(seqlen, rank * per);
   const int hi = min(seqlen, lo + per);
   const int nchunks = (hi - lo + kChunk - 1) / kChunk;
   const int32_t* bt_row = p.bt + (int64_t)seq * p.bt_stride;
 
-  auto issue_chunk = [&](int c) {
-    uint8_t* ks = stages + (c & 1) * STAGE;
-    uint8_t* vs = ks + kChunk * RB;
-    const int t0 = lo + c * kChunk;
+  // ---- chunk loader: one thread per row, 16-byte cp.async pieces ----------
+  auto issue_chunk = [&](int ch) {
+    uint8_t* ks = smem + (ch & 1) * L::STAGE;
+    uint8_t* vs = ks + kChunk * L::KP;
+    const int t0 = lo + ch * kChunk;
     const int nt = min(kChunk, hi - t0);
-    for (int i = tid; i < nt * CPR; i += NTHR) {
-      const int r = i / CPR, ch = i % CPR;
+    for (int r = tid; r < nt; r += kThreads) {
       const int tok = t0 + r;
-      const int64_t blk = bt_row[tok / p.block_size];
-      const int64_t slot = tok % p.block_size;
-      cp_async16(ks + r * RB + ch * 16, p.k + blk * p.sk0 + slot * p.sk1 + kh * p.sk2 + ch * 16);
-      cp_async16(vs + r * RB + ch * 16, p.v + blk * p.sv0 + slot * p.sv1 + kh * p.sv2 + ch * 16);
+      const int bi = p.bs_shift >= 0 ? tok >> p.bs_shift : tok / p.block_size;
+      const int64_t slot = p.bs_shift >= 0 ? tok & (p.block_size - 1) : tok % p.block_size;
+      const int64_t blk = bt_row[bi];
+      const uint8_t* kg = p.k + blk * p.sk0 + slot * p.sk1 + kh * p.sk2;
+      const uint8_t* vg = p.v + blk * p.sv0 + slot * p.sv1 + kh * p.sv2;
+#pragma unroll
+      for (int j = 0; j < RB / 16; ++j) {
+        cp_async16(ks + r * L::KP + j * 16, kg + j * 16);
+        cp_async16(vs + r * L::VP + j * 16, vg + j * 16);
+      }
     }
     cp_async_commit();
   };
   if (nchunks > 0) issue_chunk(0);
 
-  // ---- query: this lane's 8 dims of every GQA head, pre-scaled ------------
-  const float qscale = p.sm_scale * (FP8 ? __ldg(p.k_scale) : 1.f) * kLog2e;
-  float2 qf[GQA][4];
+  // ---- q as the A operand: rows = heads (g < GQA), per-head exact prescale --
+  // A fragment of 16 dims: a0 = (head g, dims 4c, 4c+1), a2 = (head g, dims
+  // 4c+2, 4c+3); rows 8..15 (a1, a3) are zero.  The same dim order is used for
+  // the K^T B fragments, so the permutation inside a 16-dim slice cancels.
+  uint32_t qa[8][2];
+  float score_scale;
   {
-    const __nv_bfloat16* qb = p.q + (int64_t)q_tok * p.q_st + (int64_t)(kh * GQA) * p.q_sh;
+    const int h = g < GQA ? g : 0;
+    const __nv_bfloat16* qb = p.q + (int64_t)q_tok * p.q_st + (int64_t)(kh * GQA + h) * p.q_sh;
+    float qv[8][4];
 #pragma unroll
-    for (int h = 0; h < GQA; ++h) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(qb + (int64_t)h * p.q_sh + 8 * sub);
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        qf[h][i] = make_float2(__uint_as_float(w[i] << 16) * qscale,
-                               __uint_as_float(w[i] & 0xFFFF0000u) * qscale);
+    for (int ds = 0; ds < 8; ++ds) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(qb + 16 * ds + 4 * c);
+      qv[ds][0] = __uint_as_float(raw.x << 16);
+      qv[ds][1] = __uint_as_float(raw.x & 0xFFFF0000u);
+      qv[ds][2] = __uint_as_float(raw.y << 16);
+      qv[ds][3] = __uint_as_float(raw.y & 0xFFFF0000u);
     }
-  }
-  if (tid < 8) {
-    S.run_m[tid] = -INFINITY;
-    S.run_l[tid] = 0.f;
-  }
-  float2 of[GQA][4];
+    float base = p.sm_scale * (FP8 ? __ldg(p.k_scale) : 1.f) * kLog2e;
+    if constexpr (FP8) {
+      float mx = 0.f;
 #pragma unroll
-  for (int h = 0; h < GQA; ++h)
+      for (int ds = 0; ds < 8; ++ds)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) of[h][e] = make_float2(0.f, 0.f);
+        for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(qv[ds][e]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+      int sh = (E == 0xFF || mx == 0.f) ? 0 : 131 - E;  // head max * 2^sh in [2^4, 2^5)
+      sh = max(-126, min(127, sh));
+      const float up = __uint_as_float((uint32_t)(sh + 127) << 23);
+      base *= __uint_as_float((uint32_t)(127 - sh) << 23);
+#pragma unroll
+      for (int ds = 0; ds < 8; ++ds) {
+        qa[ds][0] = pack_f16x2(qv[ds][0] * up, qv[ds][1] * up);
+        qa[ds][1] = pack_f16x2(qv[ds][2] * up, qv[ds][3] * up);
+      }
+    } else {
+#pragma unroll
+      for (int ds = 0; ds < 8; ++ds) {
+        qa[ds][0] = pack_bf16x2(qv[ds][0], qv[ds][1]);
+        qa[ds][1] = pack_bf16x2(qv[ds][2], qv[ds][3]);
+      }
+    }
+    if (g >= GQA) {
+#pragma unroll
+      for (int ds = 0; ds < 8; ++ds) qa[ds][0] = qa[ds][1] = 0u;
+    }
+    score_scale = base;
+  }
 
-  for (int c = 0; c < nchunks; ++c) {
-    __syncthreads();  // stage (c+1)&1 and the score buffers are free again
-    if (c + 1 < nchunks) {
-      issue_chunk(c + 1);
+  // ---- per-warp online softmax state (thread (g, c) tracks head g) ---------
+  float m_run = -INFINITY, l_run = 0.f;
+  float o[8][4];  // O^T fragments: dims 16i + {g, g+8}, heads {2c, 2c+1}
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
+
+  for (int ch = 0; ch < nchunks; ++ch) {
+    __syncthreads();  // stage (ch+1)&1 is free (its last readers were chunk ch-1)
+    if (ch + 1 < nchunks) {
+      issue_chunk(ch + 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    const uint8_t* ks = stages + (c & 1) * STAGE;
-    const uint8_t* vs = ks + kChunk * RB;
-    const int nt = min(kChunk, hi - (lo + c * kChunk));
+    const uint8_t* ks = smem + (ch & 1) * L::STAGE;
+    const uint8_t* vs = ks + kChunk * L::KP;
+    const int nt = min(kChunk, hi - (lo + ch * kChunk));
+    const int w0 = warp * 32;                 // this warp's first token in the chunk
+    const int ntw = max(0, min(32, nt - w0));  // its valid tokens
+    if (ntw == 0) continue;
 
-    // ---- pass 1: scores (both 16-lane groups of a warp run the same trips) --
-    for (int wbase = warp * 2 * TQ; wbase < nt; wbase += NG * TQ) {
-      const int base = wbase + (grp & 1) * TQ;
-      float v[16];
+    // V rows of this warp as f16 (fp8 path), zero past the valid tokens
+    const uint8_t* vrows;
+    int vpitch;
+    if constexpr (FP8) {
+      uint8_t* vc = smem + 2 * L::STAGE + warp * 32 * L::CP;
+      for (int i = lane; i < 32 * 16; i += 32) {
+        const int r = i >> 4, j = i & 15;  // row, 8-byte piece
+        uint4 h = make_uint4(0, 0, 0, 0);
+        if (r < ntw) {
+          const uint2 raw = *reinterpret_cast<const uint2*>(vs + (w0 + r) * L::VP + j * 8);
+          h.x = e4m3x2_to_f16x2(raw.x & 0xFFFFu);
+          h.y = e4m3x2_to_f16x2(raw.x >> 16);
+          h.z = e4m3x2_to_f16x2(raw.y & 0xFFFFu);
+          h.w = e4m3x2_to_f16x2(raw.y >> 16);
+        }
+        *reinterpret_cast<uint4*>(vc + r * L::CP + j * 16) = h;
+      }
+      __syncwarp();
+      vrows = vc;
+      vpitch = L::CP;
+    } else {
+      // rows past the valid tokens hold stale bytes: zero them so 0 * V stays 0
+      uint8_t* vw = const_cast<uint8_t*>(vs) + w0 * L::VP;
+      for (int i = ntw * 16 + lane; i < 32 * 16; i += 32)
+        *reinterpret_cast<uint4*>(vw + (i >> 4) * L::VP + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
+      __syncwarp();
+      vrows = vw;
+      vpitch = L::VP;
+    }
+
+    // ---- S^T = q K^T over 4 token tiles of 8 --------------------------------
+    float sfr[4][4];
 #pragma unroll
-      for (int i = 0; i < TQ; ++i) {
-        const int tok = base + i;
-        float2 kf[4];
-        if (tok < nt) {
-          Cvt::load8(ks + tok * RB + 8 * sub * (RB / kHeadDim), kf);
+    for (int t = 0; t < 4; ++t) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sfr[t][e] = 0.f;
+      const uint8_t* krow = ks + (w0 + 8 * t + g) * L::KP;
+#pragma unroll
+      for (int ds = 0; ds < 8; ++ds) {
+        uint32_t b0, b1;
+        if constexpr (FP8) {
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(krow + 16 * ds + 4 * c);
+          b0 = e4m3x2_to_f16x2(w & 0xFFFFu);
+          b1 = e4m3x2_to_f16x2(w >> 16);
         } else {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) kf[e] = make_float2(0.f, 0.f);
+          const uint2 w = *reinterpret_cast<const uint2*>(krow + 32 * ds + 8 * c);
+          b0 = w.x;
+          b1 = w.y;
         }
-#pragma unroll
-        for (int h = 0; h < GQA; ++h) {
-          float2 a = __fmul2_rn(qf[h][0], kf[0]);
-#pragma unroll
-          for (int e = 1; e < 4; ++e) a = __ffma2_rn(qf[h][e], kf[e], a);
-          v[i * GQA + h] = a.x + a.y;
-        }
+        mma16816<FP8>(sfr[t], qa[ds][0], 0u, qa[ds][1], 0u, b0, b1);
       }
-      reduce_scatter16(v, sub);
-      const int tok = base + sub / GQA;
-      if (tok < nt) S.sc[sub % GQA][tok] = v[0];
     }
-    __syncthreads();
 
-    // ---- chunk statistics and online merge into the running state ---------
-    for (int h = warp; h < GQA; h += NWARP) {
-      float m = -INFINITY;
-      for (int t = lane; t < nt; t += 32) m = fmaxf(m, S.sc[h][t]);
+    // ---- online softmax for head g over this warp's tokens ------------------
+    float mx = -INFINITY;
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const float m_old = S.run_m[h];
-      const float m_new = fmaxf(m_old, m);
-      float l = 0.f;
-      for (int t = lane; t < nt; t += 32) {
-        const float e = exp2f(S.sc[h][t] - m_new);
-        S.pt[t][h] = e;
-        l += e;
-      }
+    for (int t = 0; t < 4; ++t)
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-      if (lane == 0) {
-        const float a = exp2f(m_old - m_new);  // 0 on the first chunk
-        S.alpha[h] = a;
-        S.run_l[h] = S.run_l[h] * a + l;
-        S.run_m[h] = m_new;
+      for (int e = 0; e < 2; ++e) {
+        const int tok = 8 * t + 2 * c + e;
+        const float v = tok < ntw ? sfr[t][e] * score_scale : -INFINITY;
+        sfr[t][e] = v;
+        mx = fmaxf(mx, v);
       }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);          // finite: ntw >= 1
+    const float alpha = exp2f(m_run - m_new);      // 0 on the first chunk
+    m_run = m_new;
+    float psum = 0.f;
+    uint32_t pb[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float p0 = exp2f(sfr[t][0] - m_new);
+      const float p1 = exp2f(sfr[t][1] - m_new);
+      psum += p0 + p1;
+      pb[t] = FP8 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
     }
-    __syncthreads();
+    l_run = l_run * alpha + psum;
+    // rescale O^T: this thread holds heads 2c and 2c+1, whose alpha lives in
+    // the lanes with g == 2c / 2c+1
+    const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * c) * 4);
+    const float a1 = __shfl_sync(0xffffffffu, alpha, (2 * c + 1) * 4);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      o[i][0] *= a0; o[i][1] *= a1; o[i][2] *= a0; o[i][3] *= a1;
+    }
 
-    // ---- pass 2: o = o * alpha + sum_t p[t] * V[t] --------------------------
+    // ---- O^T += V^T P^T over 2 token slices of 16 ---------------------------
 #pragma unroll
-    for (int h = 0; h < GQA; ++h) {
-      const float2 a2 = make_float2(S.alpha[h], S.alpha[h]);
+    for (int j = 0; j < 2; ++j) {
+      const int vtok = 16 * j + (lane & 7) + ((lane >> 4) << 3);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) of[h][e] = __fmul2_rn(of[h][e], a2);
-    }
-    for (int tok = grp; tok < nt; tok += NG) {
-      float2 vf[4];
-      Cvt::load8(vs + tok * RB + 8 * sub * (RB / kHeadDim), vf);
-      float pw[GQA];
-      if constexpr (GQA == 4) {
-        const float4 p4 = *reinterpret_cast<const float4*>(&S.pt[tok][0]);
-        pw[0] = p4.x; pw[1] = p4.y; pw[2] = p4.z; pw[3] = p4.w;
-      } else {
-#pragma unroll
-        for (int h = 0; h < GQA; ++h) pw[h] = S.pt[tok][h];
-      }
-#pragma unroll
-      for (int h = 0; h < GQA; ++h) {
-        const float2 pp = make_float2(pw[h], pw[h]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) of[h][e] = __ffma2_rn(pp, vf[e], of[h][e]);
+      for (int i = 0; i < 8; ++i) {
+        uint32_t a[4];
+        ldsm_x4_trans(a, vrows + vtok * vpitch + (16 * i + ((lane >> 3) & 1) * 8) * 2);
+        mma16816<FP8>(o[i], a[0], a[1], a[2], a[3], pb[2 * j], pb[2 * j + 1]);
       }
     }
   }
 
-  // ---- fold the token groups: this CTA's unnormalised partial ---------------
-  // (the two groups of a warp through a shuffle, the warps through the staging
-  // buffers, which are free now)
+  // ---- merge the 4 warps: per-warp state -> this CTA's partial --------------
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if (c == 0 && g < 8) {
+    S.wm[warp][g] = m_run;
+    S.wl[warp][g] = l_run;
+  }
+  __syncthreads();  // staging buffers are free from here on
+  float (*wo)[GQA][kHeadDim] = reinterpret_cast<float (*)[GQA][kHeadDim]>(smem);
+  {
+    // per-warp weight of head h relative to the CTA max
+    float wgt[2];
 #pragma unroll
-  for (int h = 0; h < GQA; ++h)
+    for (int e = 0; e < 2; ++e) {
+      const int h = 2 * c + e;
+      float mc = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      of[h][e].x += __shfl_xor_sync(0xffffffffu, of[h][e].x, 16);
-      of[h][e].y += __shfl_xor_sync(0xffffffffu, of[h][e].y, 16);
+      for (int w = 0; w < kWarps; ++w) mc = fmaxf(mc, S.wm[w][h & 7]);
+      const float mw = S.wm[warp][h & 7];
+      wgt[e] = (mw == -INFINITY) ? 0.f : exp2f(mw - mc);
     }
-  __syncthreads();
-  float (*red)[GQA][kHeadDim] = reinterpret_cast<float (*)[GQA][kHeadDim]>(stages);
-  if (lane < 16) {
 #pragma unroll
-    for (int h = 0; h < GQA; ++h) {
-      float4* dst = reinterpret_cast<float4*>(&red[warp][h][8 * sub]);
-      dst[0] = make_float4(of[h][0].x, of[h][0].y, of[h][1].x, of[h][1].y);
-      dst[1] = make_float4(of[h][2].x, of[h][2].y, of[h][3].x, of[h][3].y);
-    }
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int h = 2 * c + e;
+        if (h < GQA) {
+          wo[warp][h][16 * i + g] = o[i][e] * wgt[e];
+          wo[warp][h][16 * i + g + 8] = o[i][2 + e] * wgt[e];
+        }
+      }
   }
   __syncthreads();
-  for (int e = tid; e < GQA * kHeadDim; e += NTHR) {
+  for (int e = tid; e < GQA * kHeadDim; e += kThreads) {
     const int h = e / kHeadDim, d = e % kHeadDim;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < NWARP; ++w) s += red[w][h][d];
+    for (int w = 0; w < kWarps; ++w) s += wo[w][h][d];
     S.part_o[h][d] = s;
   }
   if (tid < GQA) {
-    S.part_m[tid] = S.run_m[tid];
-    S.part_l[tid] = S.run_l[tid];
+    float mc = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mc = fmaxf(mc, S.wm[w][tid]);
+    float lc = 0.f;
+    if (mc != -INFINITY)
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w)
+        if (S.wm[w][tid] != -INFINITY) lc += S.wl[w][tid] * exp2f(S.wm[w][tid] - mc);
+    S.part_m[tid] = mc;
+    S.part_l[tid] = lc;
   }
   const float vsc = FP8 ? __ldg(p.v_scale) : 1.f;
   __nv_bfloat16* out_base = p.out + (int64_t)out_row * p.o_st + (int64_t)(kh * GQA) * p.o_sh;
@@ -347,24 +425,26 @@ __global__ void __launch_bounds__(decode_threads<GQA>())
     for (int r = 0; r < csize; ++r) mg = fmaxf(mg, cluster.map_shared_rank(&S.part_m[0], r)[tid]);
     float lg = 0.f;
     if (mg != -INFINITY)
-      for (int r = 0; r < csize; ++r)
-        lg += exp2f(cluster.map_shared_rank(&S.part_m[0], r)[tid] - mg) *
-              cluster.map_shared_rank(&S.part_l[0], r)[tid];
+      for (int r = 0; r < csize; ++r) {
+        const float mr = cluster.map_shared_rank(&S.part_m[0], r)[tid];
+        if (mr != -INFINITY) lg += exp2f(mr - mg) * cluster.map_shared_rank(&S.part_l[0], r)[tid];
+      }
     S.comb_m[tid] = mg;
     S.comb_l[tid] = lg;
   }
   __syncthreads();
-  // rank r writes elements [r*E/csize, (r+1)*E/csize) of the GQA x 128 output
   constexpr int E = GQA * kHeadDim;
   const int e0 = rank * E / csize, e1 = (rank + 1) * E / csize;
-  for (int e = e0 + tid; e < e1; e += NTHR) {
+  for (int e = e0 + tid; e < e1; e += kThreads) {
     const int h = e / kHeadDim, d = e % kHeadDim;
     const float mg = S.comb_m[h];
     float acc = 0.f;
     if (mg != -INFINITY)
-      for (int r = 0; r < csize; ++r)
-        acc += exp2f(cluster.map_shared_rank(&S.part_m[0], r)[h] - mg) *
-               cluster.map_shared_rank(&S.part_o[0][0], r)[h * kHeadDim + d];
+      for (int r = 0; r < csize; ++r) {
+        const float mr = cluster.map_shared_rank(&S.part_m[0], r)[h];
+        if (mr != -INFINITY)
+          acc += exp2f(mr - mg) * cluster.map_shared_rank(&S.part_o[0][0], r)[h * kHeadDim + d];
+      }
     const float lg = S.comb_l[h];
     out_base[(int64_t)h * p.o_sh + d] = __float2bfloat16_rn(lg > 0.f ? acc * vsc / lg : 0.f);
   }
@@ -372,15 +452,10 @@ __global__ void __launch_bounds__(decode_threads<GQA>())
 }
 
 template <int GQA, bool FP8>
-size_t decode_smem_bytes() {
-  const size_t rb = FP8 ? kHeadDim : 2 * kHeadDim;
-  return 2 * 2 * kChunk * rb + sizeof(DecodeSmem<GQA>);
-}
-
-template <int GQA, bool FP8>
 cudaError_t launch_decode(const DecodeParams& p, int csize, int hkv, int num_seqs,
                           cudaStream_t stream) {
-  const size_t smem = decode_smem_bytes<GQA, FP8>();
+  const size_t smem = Layout<FP8>::BYTES;
+  static_assert(Layout<FP8>::BYTES >= kWarps * GQA * kHeadDim * 4, "stages must hold the merge");
   cudaError_t e = cudaFuncSetAttribute(decode_attn_kernel<GQA, FP8>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -391,7 +466,7 @@ cudaError_t launch_decode(const DecodeParams& p, int csize, int hkv, int num_seq
   }
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(csize, hkv, num_seqs);
-  lc.blockDim = dim3(decode_threads<GQA>(), 1, 1);
+  lc.blockDim = dim3(kThreads, 1, 1);
   lc.dynamicSmemBytes = smem;
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -407,7 +482,7 @@ cudaError_t launch_decode(const DecodeParams& p, int csize, int hkv, int num_seq
 }  // namespace
 
 // Cluster size (CTAs per (sequence, kv head)): the largest power of two <= 16
-// that keeps the grid within one CTA per SM, but at least one CTA per 4096
+// that keeps the grid within two CTAs per SM, but at least one CTA per 4096
 // tokens of the context bound, and at least 64 tokens per CTA.
 int decode_cluster_size(int num_seqs, int hkv, int ctx_bound, int requested) {
   int want;
@@ -417,7 +492,7 @@ int decode_cluster_size(int num_seqs, int hkv, int ctx_bound, int requested) {
     const int sms = num_sms_current_device() > 0 ? num_sms_current_device() : 148;
     const int pairs = num_seqs * hkv;
     want = 1;
-    while (want * 2 <= kMaxCluster && pairs * want * 2 <= sms) want *= 2;
+    while (want * 2 <= kMaxCluster && pairs * want * 2 <= 2 * sms) want *= 2;
     const int need = cdiv(ctx_bound, 4096);
     if (want < need) want = need;
     const int cap = cdiv(ctx_bound, 64);
@@ -475,6 +550,7 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
   p.v_scale = v_scale;
   p.sm_scale = sm_scale;
   p.block_size = block_size;
+  p.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz((unsigned)block_size) : -1;
   p.out_by_qsl = out_by_qsl;
 
   const int ctx = hint > 0 ? hint : max_blocks * block_size;

@@ -4,40 +4,44 @@
 // with fp32 accumulation -- the arithmetic of the reference kernel
 // h4mv/h4mv.cu:43-104 (h4mv_t<MT>), re-designed for B200:
 //
-//  * Work unit: a CTA owns 16*RT consecutive weight rows and one K-slice; the
-//    K-slices of a row tile form a thread-block cluster (up to 8 CTAs along y)
-//    that reduce their fp32 partials through distributed shared memory, so a
-//    small-N layer still puts several CTAs on every SM without global scratch.
-//  * Warp-specialised CTA: one producer warp streams the weight tile through a
-//    4-stage ring of ~8 KB K-chunks with bulk copies (TMA engine, one copy per
-//    row per stage, mbarrier full/empty handshake), so loads of later chunks
-//    overlap the math on earlier ones; the activation slice is staged once.
-//  * The activations are converted once per CTA to f16 with an exact per-row
-//    power-of-two prescale (the row maximum lands in [2^4, 2^5)): every bf16
-//    value within 2^-18 of its row's maximum keeps its 8-bit significand
-//    exactly, smaller ones are rounded to f16 subnormals (their products are
-//    below 2^-18 of the largest and vanish in the fp32 sum), and no value can
-//    overflow f16.  The prescale is undone exactly on the fp32 result; it can
-//    only push a partial sum past fp32's range when the reference's own result
-//    is within a factor 2^5 of it (scale bytes near 255).
+//  * Persistent thread-block clusters.  The ks CTAs of a cluster (ks in
+//    {1,2,4,8}) split K; the clusters split the 16-row weight tiles round-robin.
+//    ks is chosen to balance the tiles over the clusters (148 SMs rarely divide
+//    N/16) and to keep the activation slice small.  Each CTA keeps its tiles'
+//    fp32 partials in shared memory and the cluster reduces them once, at the
+//    end, through distributed shared memory: no global scratch, one launch.
+//  * Warp-specialised: one producer warp streams (tile, K-chunk) stages
+//    through a 4- to 6-deep ring with TMA tensor-map loads -- the weights as
+//    128-byte-swizzled 16-row boxes (2 KB per request) and the scales as a
+//    [kc groups x 16 rows] box -- with a full/empty mbarrier handshake, so HBM
+//    sees a continuous stream of large requests (small bulk requests were
+//    measured to cap at ~2 TB/s on this part).
+//  * The activation slice is staged once per CTA and converted to f16 with an
+//    exact per-row power-of-two prescale (row maximum in [2^4, 2^5)): every bf16
+//    value within 2^-18 of its row's maximum keeps its 8-bit significand,
+//    smaller ones round to f16 subnormals (their products vanish in the fp32
+//    sum), none can overflow.  The prescale is undone exactly at the end.
 //  * Weights are decoded with the Blackwell hardware convert
-//    cvt.rn.f16x2.e2m1x2 (one instruction per byte, exact), and the products
-//    and fp32 accumulation run on the tensor pipe through mma.sync m16n8k16
-//    (A = 16 weight rows x 16 k, B = 16 k x 8 activation rows), used as a wide
-//    fp32-accumulating dot-product engine: a matvec needs 2*M multiply-adds per
-//    weight byte, which would saturate the FP32 pipe and the issue slots long
-//    before HBM does.  The reference made the same move on gfx1201 with
-//    v_dot2_f32_bf16 (h4mv.cu:26-31).
-//  * The fragments are group-aligned: lane (r0 = lane/4, c = lane%4) takes bytes
+//    cvt.rn.f16x2.e2m1x2 (one instruction per byte, exact) and multiplied on
+//    the tensor pipe through mma.sync m16n8k16 (A = 16 weight rows x 16 k,
+//    B = 16 k x 8 activation rows), used as a wide fp32-accumulating dot
+//    product engine -- a matvec needs 2*M multiply-adds per weight byte, which
+//    would saturate the FP32 pipe and the issue slots long before HBM does.
+//    The reference made the same move on gfx1201 with v_dot2_f32_bf16
+//    (h4mv.cu:26-31).
+//  * Group-aligned fragments: lane (r0 = lane/4, c = lane%4) takes bytes
 //    4c..4c+3 of one 16-byte group (32 weights = one e8m0 group) of rows r0 and
-//    r0+8, so the two MMAs of a group cover exactly that group, and the group
-//    scale 2^(s-127) multiplies the group's fp32 partial -- the reference's
-//    per-group structure (h4mv.cu:72-90), exact for every scale byte.
+//    r0+8, so the two MMAs of a group cover exactly that group and the group
+//    scale multiplies the group's fp32 partial -- the reference's per-group
+//    structure (h4mv.cu:72-90), exact for every scale byte.
 //
 // Edge semantics follow the reference kernel: the scale is the fp32 bit pattern
-// s << 23, so byte 0 -> 0.0 and 255 -> inf.  Output rounding: fp32 -> bf16 RN-even.
+// s << 23, so byte 0 -> 0.0 and 255 -> inf.  The activation prescale can push
+// a partial sum past fp32's range only when the reference's own result is
+// within a factor 2^5 of it.  Output rounding: fp32 -> bf16 RN-even.
 
 #include <cooperative_groups.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -46,11 +50,16 @@
 
 #include "b200kv.h"
 #include "b200kv_common.cuh"
+#include "tma.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace b200kv {
 namespace {
+
+constexpr int kTileRows = 16;
+constexpr int kMaxStages = 8;
+constexpr int kMaxClusterK = 8;
 
 // 4 bytes = 8 e2m1 codes -> 4 f16x2 words (exact); word b holds byte b, low
 // nibble (even k) in the low half.
@@ -74,42 +83,49 @@ __device__ __forceinline__ void mma_16816_f16(float (&c)[4], uint32_t a0, uint32
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Shared-memory layout.  Weight rows of a stage: pitch == 16 (mod 128) bytes,
-// so the 8 rows x 4 lanes of a 32-bit load hit 32 distinct banks.  Activation
-// rows: pitch == 64 (mod 128), so the 8-lane phases of a 128-bit load hit
-// distinct 16-byte bank groups.  Scale rows: pitch == 4 (mod 8) words apart.
-constexpr int kStages = 4;
-__host__ __device__ constexpr int w_pitch(int kc) { return kc * 16 + 16; }
-__host__ __device__ constexpr int x_pitch(int slice_k) { return ((slice_k * 2 + 127) & ~127) + 64; }
-__host__ __device__ constexpr int s_pitch(int gps) { return ((gps + 15) & ~15) + 4; }
-
-struct GemvLayout {
-  int rows, gps, kc, m;
-  __host__ __device__ int wp() const { return w_pitch(kc); }
-  __host__ __device__ int xp() const { return x_pitch(gps * 32); }
-  __host__ __device__ int sp() const { return s_pitch(gps); }
-  __host__ __device__ size_t ring_off() const { return 0; }
-  __host__ __device__ size_t x_off() const { return (size_t)kStages * rows * wp(); }
-  __host__ __device__ size_t s_off() const { return x_off() + (size_t)m * xp(); }
-  __host__ __device__ size_t bytes() const { return s_off() + (((size_t)rows * sp() + 15) & ~(size_t)15); }
+struct GemvArgs {
+  const uint8_t* St;  // scale bytes [N, K/32] (read directly when not staged by TMA)
+  const __nv_bfloat16* X;
+  __nv_bfloat16* Out;
+  int N, K, M;
+  int gps;        // groups per K-slice (multiple of 16)
+  int kc;         // groups per stage (multiple of 16)
+  int nstages;    // ring depth (<= kMaxStages)
+  int ntiles;     // cdiv(N, 16)
+  int nclusters;  // clusters (each owns tiles cid, cid + nclusters, ...)
+  int tmax;       // cdiv(ntiles, nclusters): partial slots per CTA
 };
 
-// Warp-specialised: NW consumer warps do the math, one producer warp streams
-// the weight tile through a kStages-deep ring of K-chunks (kc groups each).
-template <int RT, int NW>
+// Shared-memory layout.  Stage = kc/8 weight boxes of [128 B x 16 rows]
+// (128B-swizzled, 2 KB each) + one scale box [kc B x 16 rows]; stages are
+// 1024-byte aligned as the swizzle pattern requires.  Activation rows: pitch
+// == 64 (mod 128) so the 8-lane phases of a 128-bit load hit distinct 16-byte
+// bank groups.  kc is a divisor of the slice's groups (no wasted loads).
+struct GemvLayout {
+  int kc, gps, m, tmax, nw, nstages;
+  __host__ __device__ int w_bytes() const { return kc * 16 * kTileRows; }
+  __host__ __device__ int stage_bytes() const { return (w_bytes() + kTileRows * kc + 1023) & ~1023; }
+  __host__ __device__ int xp() const { return ((gps * 64 + 127) & ~127) + 64; }
+  __host__ __device__ size_t x_off() const { return (size_t)nstages * stage_bytes(); }
+  __host__ __device__ size_t part_off() const { return x_off() + (((size_t)m * xp() + 15) & ~(size_t)15); }
+  __host__ __device__ size_t red_off() const { return part_off() + (size_t)tmax * kTileRows * 8 * 4; }
+  __host__ __device__ size_t bytes() const { return red_off() + (size_t)nw * kTileRows * 8 * 4 + 1024; }
+};
+
+// STMA: scales through the TMA ring (needs K/32 to be a multiple of 16 bytes);
+// otherwise each lane reads its scale bytes from global memory (L1-cached).
+template <int NW, bool STMA>
 __global__ void __launch_bounds__((NW + 1) * 32)
-    mxfp4_gemv_kernel(const uint8_t* __restrict__ W, const uint8_t* __restrict__ St,
-                      const __nv_bfloat16* __restrict__ X, __nv_bfloat16* __restrict__ Out,
-                      int N, int K, int M, int gps, int kc) {
-  constexpr int ROWS = 16 * RT;
-  constexpr int NC = NW * 32;        // consumer threads
+    mxfp4_gemv_kernel(const __grid_constant__ CUtensorMap wmap,
+                      const __grid_constant__ CUtensorMap smap, const GemvArgs a) {
+  constexpr int NC = NW * 32;  // consumer threads
   constexpr int NT = NC + 32;
-  __shared__ float red[NW][ROWS][8];
-  __shared__ float cta_part[ROWS][8];
   __shared__ float xunscale[8];
   __shared__ float xmax_part[NW][8];
-  __shared__ uint64_t full_bar[kStages], empty_bar[kStages], x_bar;
-  extern __shared__ __align__(128) uint8_t dsm[];
+  __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages], x_bar;
+  extern __shared__ uint8_t dsm_raw[];
+  // 1024-byte align the dynamic region (the 128-byte swizzle needs it)
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -117,21 +133,25 @@ __global__ void __launch_bounds__((NW + 1) * 32)
   const bool producer = warp == NW;
   const int r0 = lane >> 2;
   const int c = lane & 3;
-  const int ngroups = K >> 5;
-  const int row_base = blockIdx.x * ROWS;
-  const int g_begin = blockIdx.y * gps;
-  const int g_end = min(ngroups, g_begin + gps);
-  const int ng = g_end - g_begin;
-  const int nst = (ng + kc - 1) / kc;
-  const GemvLayout L{ROWS, gps, kc, M};
-  const int wp = L.wp(), xp = L.xp(), sp = L.sp();
-  uint8_t* ring = dsm + L.ring_off();   // [kStages][ROWS][wp]
-  uint8_t* xsm = dsm + L.x_off();       // [M][xp]: bf16 staged, f16 after convert
-  uint8_t* ssm = dsm + L.s_off();       // [ROWS][sp] scale bytes
-  const int nrows = min(ROWS, N - row_base);
+  const int M = a.M;
+  const int ngroups = a.K >> 5;
+  const int rank = blockIdx.x;  // K-slice = rank in the cluster
+  const int cid = blockIdx.y;
+  const int g_begin = rank * a.gps;
+  const int ng = max(0, min(ngroups, g_begin + a.gps) - g_begin);
+  const int kc = a.kc;
+  const int nch = (ng + kc - 1) / kc;
+  const int my_tiles = cid < a.ntiles ? (a.ntiles - cid + a.nclusters - 1) / a.nclusters : 0;
+  const int nstages = a.nstages;
+  const GemvLayout L{kc, a.gps, M, a.tmax, NW, nstages};
+  const int stage_bytes = L.stage_bytes();
+  const int xp = L.xp();
+  uint8_t* xsm = dsm + L.x_off();
+  float* part = reinterpret_cast<float*>(dsm + L.part_off());  // [tmax][16][8]
+  float* red = reinterpret_cast<float*>(dsm + L.red_off());    // [NW][16][8]
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < nstages; ++i) {
       mbar_init(&full_bar[i], 1);
       mbar_init(&empty_bar[i], NW);
     }
@@ -142,36 +162,43 @@ __global__ void __launch_bounds__((NW + 1) * 32)
 
   bool failed = false;
   if (producer) {
-    // ---- activation slice (once), then the weight ring ----------------------
-    if (lane == 0) mbar_arrive_expect_tx(&x_bar, (uint32_t)(M * ng * 64));
+    if (lane == 0) {
+      tma_prefetch_desc(&wmap);
+      tma_prefetch_desc(&smap);
+      mbar_arrive_expect_tx(&x_bar, (uint32_t)(M * ng * 64));
+    }
     __syncwarp();
-    if (lane < M)
-      bulk_g2s(xsm + lane * xp, X + (size_t)lane * K + (size_t)g_begin * 32, (uint32_t)(ng * 64), &x_bar);
-    for (int st = 0; st < nst && !failed; ++st) {
-      const int slot = st % kStages;
-      if (st >= kStages) failed = !mbar_wait_bounded(&empty_bar[slot], ((st / kStages) - 1) & 1);
-      const int g0 = st * kc;
-      const int kcs = min(kc, ng - g0);
-      if (lane == 0) mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(nrows * kcs * 16));
-      __syncwarp();
-      for (int r = lane; r < nrows; r += 32)
-        bulk_g2s(ring + (size_t)(slot * ROWS + r) * wp,
-                 W + (size_t)(row_base + r) * (K >> 1) + (size_t)(g_begin + g0) * 16,
-                 (uint32_t)(kcs * 16), &full_bar[slot]);
+    if (lane < M && ng > 0)
+      bulk_g2s(xsm + lane * xp, a.X + (size_t)lane * a.K + (size_t)g_begin * 32,
+               (uint32_t)(ng * 64), &x_bar);
+    // ---- (tile, chunk) stages through the ring --------------------------------
+    if (lane == 0) {
+      const uint32_t tx = (uint32_t)(L.w_bytes() + (STMA ? kTileRows * kc : 0));
+      int s = 0;
+      for (int i = 0; i < my_tiles && !failed; ++i) {
+        const int row0 = (cid + i * a.nclusters) * kTileRows;
+        for (int j = 0; j < nch && !failed; ++j, ++s) {
+          const int slot = s % nstages;
+          if (s >= nstages) failed = !mbar_wait_bounded(&empty_bar[slot], ((s / nstages) - 1) & 1);
+          if (failed) break;
+          uint8_t* st = dsm + (size_t)slot * stage_bytes;
+          mbar_arrive_expect_tx(&full_bar[slot], tx);
+          const int gx = g_begin + j * kc;
+          for (int b = 0; b < kc / 8; ++b)
+            tma_load_2d(st + b * 2048, &wmap, (gx + 8 * b) * 16, row0, &full_bar[slot]);
+          if (STMA) tma_load_2d(st + L.w_bytes(), &smap, gx, row0, &full_bar[slot]);
+        }
+      }
     }
+    __syncwarp();
   } else {
-    // ---- scales of the whole slice into padded rows ---------------------------
-    for (int i = tid; i < nrows * ng; i += NC) {
-      const int r = i / ng, g = i % ng;
-      ssm[r * sp + g] = __ldg(St + (size_t)(row_base + r) * ngroups + g_begin + g);
-    }
     // ---- activations: exact per-row power-of-two prescale into f16 ------------
-    failed = !mbar_wait_bounded(&x_bar, 0);
+    if (ng > 0) failed = !mbar_wait_bounded(&x_bar, 0);
     const int per_row = ng * 4;  // uint4 per row
     for (int m = 0; m < M; ++m) {
       const uint4* row = reinterpret_cast<const uint4*>(xsm + m * xp);
       float mx = 0.f;
-      for (int i = tid; i < per_row; i += NC) {
+      for (int i = tid; i < per_row && !failed; i += NC) {
         const uint4 v = row[i];
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -194,7 +221,7 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       const float up = __uint_as_float((uint32_t)(sh + 127) << 23);
       if (tid == 0) xunscale[m] = __uint_as_float((uint32_t)(127 - sh) << 23);
       uint4* row = reinterpret_cast<uint4*>(xsm + m * xp);
-      for (int i = tid; i < per_row; i += NC) {
+      for (int i = tid; i < per_row && !failed; i += NC) {
         const uint4 v = row[i];
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         uint32_t o[4];
@@ -208,103 +235,95 @@ __global__ void __launch_bounds__((NW + 1) * 32)
       }
     }
     named_bar_sync(1, NC);
-  }
 
-  float acc[RT][4];
-#pragma unroll
-  for (int t = 0; t < RT; ++t)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[t][i] = 0.f;
-
-  if (!producer) {
+    // ---- math: consumer warp w takes 4-group steps w, w+NW, ... of a chunk ----
     const uint8_t* xrow = xsm + min(r0, M - 1) * xp + 16 * c;
-    int lrow[RT][2];
+    const int swz = r0 & 7;  // 128-byte swizzle of rows r0 and r0+8
+    int s = 0;
+    for (int i = 0; i < my_tiles; ++i) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int row0 = (cid + i * a.nclusters) * kTileRows;
+      const uint8_t* sg_lo = a.St + (size_t)min(row0 + r0, a.N - 1) * ngroups + g_begin;
+      const uint8_t* sg_hi = a.St + (size_t)min(row0 + r0 + 8, a.N - 1) * ngroups + g_begin;
+      for (int j = 0; j < nch; ++j, ++s) {
+        const int slot = s % nstages;
+        if (!failed) failed = !mbar_wait_bounded(&full_bar[slot], (s / nstages) & 1);
+        const int kcs = failed ? 0 : min(kc, ng - j * kc);
+        const uint8_t* st = dsm + (size_t)slot * stage_bytes;
+        const uint8_t* ssc = st + L.w_bytes();
+        for (int q = warp; q * 4 < kcs; q += NW) {
+          uint32_t s4_lo, s4_hi;
+          if constexpr (STMA) {
+            s4_lo = *reinterpret_cast<const uint32_t*>(ssc + r0 * kc + 4 * q);
+            s4_hi = *reinterpret_cast<const uint32_t*>(ssc + (r0 + 8) * kc + 4 * q);
+          } else {
+            s4_lo = s4_hi = 0u;
 #pragma unroll
-    for (int t = 0; t < RT; ++t)
+            for (int u = 0; u < 4; ++u)
+              if (4 * q + u < kcs) {
+                s4_lo |= (uint32_t)__ldg(sg_lo + j * kc + 4 * q + u) << (8 * u);
+                s4_hi |= (uint32_t)__ldg(sg_hi + j * kc + 4 * q + u) << (8 * u);
+              }
+          }
 #pragma unroll
-      for (int h = 0; h < 2; ++h) lrow[t][h] = min(16 * t + 8 * h + r0, nrows - 1);
-    for (int st = 0; st < nst; ++st) {
-      const int slot = st % kStages;
-      if (!failed) failed = !mbar_wait_bounded(&full_bar[slot], (st / kStages) & 1);
-      const int g0 = st * kc;
-      const int kcs = failed ? 0 : min(kc, ng - g0);
-      const uint8_t* stage = ring + (size_t)slot * ROWS * wp;
-#pragma unroll 2
-      for (int gl = warp; gl < kcs; gl += NW) {
-        const int g = g0 + gl;
-        const uint4 xv = *reinterpret_cast<const uint4*>(xrow + g * 64);
-#pragma unroll
-        for (int t = 0; t < RT; ++t) {
-          const uint32_t w_lo = *reinterpret_cast<const uint32_t*>(stage + lrow[t][0] * wp + gl * 16 + 4 * c);
-          const uint32_t w_hi = *reinterpret_cast<const uint32_t*>(stage + lrow[t][1] * wp + gl * 16 + 4 * c);
-          uint32_t a_lo[4], a_hi[4];
-          e2m1x8_to_f16x2(w_lo, a_lo);
-          e2m1x8_to_f16x2(w_hi, a_hi);
-          float part[4] = {0.f, 0.f, 0.f, 0.f};
-          mma_16816_f16(part, a_lo[0], a_hi[0], a_lo[1], a_hi[1], xv.x, xv.y);
-          mma_16816_f16(part, a_lo[2], a_hi[2], a_lo[3], a_hi[3], xv.z, xv.w);
-          const float s_lo = __uint_as_float((uint32_t)ssm[lrow[t][0] * sp + g] << 23);
-          const float s_hi = __uint_as_float((uint32_t)ssm[lrow[t][1] * sp + g] << 23);
-          acc[t][0] = fmaf(part[0], s_lo, acc[t][0]);
-          acc[t][1] = fmaf(part[1], s_lo, acc[t][1]);
-          acc[t][2] = fmaf(part[2], s_hi, acc[t][2]);
-          acc[t][3] = fmaf(part[3], s_hi, acc[t][3]);
+          for (int u = 0; u < 4; ++u) {
+            const int gl = 4 * q + u;
+            if (gl < kcs) {
+              const uint4 xv = *reinterpret_cast<const uint4*>(xrow + (j * kc + gl) * 64);
+              const uint8_t* box = st + (gl >> 3) * 2048 + (((gl & 7) ^ swz) << 4) + 4 * c;
+              const uint32_t w_lo = *reinterpret_cast<const uint32_t*>(box + r0 * 128);
+              const uint32_t w_hi = *reinterpret_cast<const uint32_t*>(box + (r0 + 8) * 128);
+              uint32_t a_lo[4], a_hi[4];
+              e2m1x8_to_f16x2(w_lo, a_lo);
+              e2m1x8_to_f16x2(w_hi, a_hi);
+              float pr[4] = {0.f, 0.f, 0.f, 0.f};
+              mma_16816_f16(pr, a_lo[0], a_hi[0], a_lo[1], a_hi[1], xv.x, xv.y);
+              mma_16816_f16(pr, a_lo[2], a_hi[2], a_lo[3], a_hi[3], xv.z, xv.w);
+              const float sl = __uint_as_float(((s4_lo >> (8 * u)) & 0xFFu) << 23);
+              const float sh = __uint_as_float(((s4_hi >> (8 * u)) & 0xFFu) << 23);
+              acc[0] = fmaf(pr[0], sl, acc[0]);
+              acc[1] = fmaf(pr[1], sl, acc[1]);
+              acc[2] = fmaf(pr[2], sh, acc[2]);
+              acc[3] = fmaf(pr[3], sh, acc[3]);
+            }
+          }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[slot]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty_bar[slot]);
-    }
+      // ---- fold the consumer warps: tile partial (activation prescale undone) --
+      red[(warp * kTileRows + r0) * 8 + 2 * c] = acc[0];
+      red[(warp * kTileRows + r0) * 8 + 2 * c + 1] = acc[1];
+      red[(warp * kTileRows + r0 + 8) * 8 + 2 * c] = acc[2];
+      red[(warp * kTileRows + r0 + 8) * 8 + 2 * c + 1] = acc[3];
+      named_bar_sync(1, NC);
+      if (tid < kTileRows * 8) {
+        float v = 0.f;
 #pragma unroll
-    for (int t = 0; t < RT; ++t) {
-      red[warp][16 * t + r0][2 * c] = acc[t][0];
-      red[warp][16 * t + r0][2 * c + 1] = acc[t][1];
-      red[warp][16 * t + r0 + 8][2 * c] = acc[t][2];
-      red[warp][16 * t + r0 + 8][2 * c + 1] = acc[t][3];
+        for (int w = 0; w < NW; ++w) v += red[w * kTileRows * 8 + tid];
+        const int m = tid & 7;
+        part[i * kTileRows * 8 + tid] = m < M ? v * xunscale[m] : 0.f;
+      }
+      named_bar_sync(1, NC);
     }
   }
-  __syncthreads();  // all warps, the producer included, meet here
 
-  // ---- reduce the NW warps of this CTA (and undo the activation prescale) ----
-  for (int i = tid; i < ROWS * 8; i += NT) {
-    const int r = i >> 3, m = i & 7;
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) s += red[w][r][m];
-    cta_part[r][m] = m < M ? s * xunscale[m] : 0.f;
-  }
-
-  if (gridDim.y == 1) {
-    __syncthreads();
-    for (int i = tid; i < ROWS * M; i += NT) {
-      const int m = i / ROWS, r = i % ROWS;
-      const int n = row_base + r;
-      if (n < N) Out[(size_t)m * N + n] = __float2bfloat16_rn(cta_part[r][m]);
-    }
-    return;
-  }
-
-  // ---- reduce the K-slices of the cluster through distributed shared memory --
+  // ---- reduce the cluster's K-slices through distributed shared memory -------
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
-  if (cluster.block_rank() == 0) {
-    const int nranks = (int)cluster.num_blocks();
-    for (int i = tid; i < ROWS * M; i += NT) {
-      const int m = i / ROWS, r = i % ROWS;
-      float s = cta_part[r][m];
-      for (int q = 1; q < nranks; ++q) {
-        const float* peer = cluster.map_shared_rank(&cta_part[0][0], q);
-        s += peer[r * 8 + m];
-      }
-      const int n = row_base + r;
-      if (n < N) Out[(size_t)m * N + n] = __float2bfloat16_rn(s);
+  const int ks = (int)cluster.num_blocks();
+  for (int i = rank; i < my_tiles; i += ks) {
+    const int row0 = (cid + i * a.nclusters) * kTileRows;
+    for (int e = tid; e < kTileRows * M; e += NT) {
+      const int m = e / kTileRows, r = e % kTileRows;
+      float v = 0.f;
+      for (int q = 0; q < ks; ++q) v += cluster.map_shared_rank(part, q)[(i * kTileRows + r) * 8 + m];
+      const int n = row0 + r;
+      if (n < a.N) a.Out[(size_t)m * a.N + n] = __float2bfloat16_rn(v);
     }
   }
-  cluster.sync();  // keep every peer's shared memory alive until rank 0 is done
+  cluster.sync();  // peers' shared memory stays alive until every rank is done
 }
-
-struct GemvConfig {
-  int rt, nw, ksplit, kc;
-};
 
 int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
@@ -312,57 +331,98 @@ int env_int(const char* name, int dflt) {
   return atoi(v);
 }
 
-// Row tile 16*RT (RT grows with M so the activation slice is amortised over
-// more weight rows); K-split (a cluster) so that the activation slice stays
-// <= 16 KB and there are >= 2 CTAs per SM; kc groups per pipeline stage so a
-// stage is ~8 KB of weights.
-GemvConfig choose_config(int N, int K, int M) {
+struct GemvPlan {
+  int ks, nclusters, gps, kc, nstages, tmax;
+  size_t smem;
+};
+
+// K-split ks in {1,2,4,8}: 1 unless there are too few 16-row tiles for the
+// CTAs (then the best-balanced split), subject to an activation slice of at
+// most 64 KB and at least 32 groups per slice.  Stage = kc groups (the largest
+// of 64/48/32/16 dividing the slice); 4 stages with two CTAs per SM when they
+// fit, else one CTA with 6 stages.  (Measured on B200: 64-group stages with 8
+// consumer warps beat better-balanced splits with smaller stages.)
+bool plan_gemv(int N, int K, int M, int nw, GemvPlan* P) {
   const int sms = num_sms_current_device() > 0 ? num_sms_current_device() : 148;
-  GemvConfig cfg;
-  cfg.rt = M <= 2 ? 1 : (M <= 4 ? 2 : 4);
-  cfg.nw = 4;
   const int ngroups = K / 32;
-  const int tiles = cdiv(N, 16 * cfg.rt);
-  cfg.ksplit = 1;
-  while (cfg.ksplit < 8 && ngroups / (cfg.ksplit * 2) >= 8 &&
-         ((size_t)M * 2 * K / cfg.ksplit > 16384 || tiles * cfg.ksplit < 2 * sms))
-    cfg.ksplit *= 2;
-  cfg.kc = 32 / cfg.rt;  // groups per stage: 16*RT rows x kc*16 bytes = 8 KB
-  // explicit overrides for tuning sweeps
-  cfg.rt = env_int("B200KV_GEMV_RT", cfg.rt);
-  cfg.nw = env_int("B200KV_GEMV_NW", cfg.nw);
-  cfg.ksplit = env_int("B200KV_GEMV_KSPLIT", cfg.ksplit);
-  cfg.kc = env_int("B200KV_GEMV_KC", cfg.kc);
-  return cfg;
+  const int ntiles = cdiv(N, kTileRows);
+  const int forced = env_int("B200KV_GEMV_KSPLIT", 0);
+  const int kc_env = env_int("B200KV_GEMV_KC", 0);
+  const int st_env = env_int("B200KV_GEMV_STAGES", 0);
+  double best = -1.0;
+  bool ok = false;
+  for (int ks = 1; ks <= kMaxClusterK; ks *= 2) {
+    if (forced && ks != forced) continue;
+    int gps = cdiv(ngroups, ks);
+    gps = (gps + 15) & ~15;
+    if (cdiv(ngroups, gps) != ks) continue;  // would leave a rank without groups
+    if (!forced && ks > 1 && (gps < 32 || ntiles >= 4 * sms)) continue;
+    if (!forced && (size_t)M * gps * 64 > 65536 && ks < kMaxClusterK) continue;
+    int kc = 16;
+    for (int cand : {64, 48, 32, 16})
+      if (gps % cand == 0) { kc = cand; break; }
+    if (kc_env) kc = kc_env;
+    if (kc < 16 || kc % 16 || kc > 256) return false;
+    for (int cps = 2; cps >= 1; --cps) {
+      int ncl = sms * cps / ks;
+      if (ncl > ntiles) ncl = ntiles;
+      if (ncl < 1) ncl = 1;
+      const int tmax = cdiv(ntiles, ncl);
+      int nst = st_env ? st_env : (cps == 2 ? 4 : 6);
+      if (nst > kMaxStages) nst = kMaxStages;
+      const GemvLayout L{kc, gps, M, tmax, nw, nst};
+      const size_t smem = L.bytes();
+      if (smem * cps > 220 * 1024) continue;
+      const double bal = (double)ntiles / ncl / tmax + (ks == 1 ? 1e-3 : 0.0) + cps * 1e-4;
+      if (bal > best) {
+        best = bal;
+        *P = GemvPlan{ks, ncl, gps, kc, nst, tmax, smem};
+        ok = true;
+      }
+      break;  // the larger cps that fits is preferred
+    }
+  }
+  return ok;
 }
 
-template <int RT, int NW>
-cudaError_t launch_gemv(const GemvConfig& cfg, const uint8_t* W, const uint8_t* St,
-                        const __nv_bfloat16* X, __nv_bfloat16* Out, int N, int K, int M,
-                        cudaStream_t stream) {
-  const int ngroups = K / 32;
-  const int gps = cdiv(ngroups, cfg.ksplit);
-  const int ksplit = cdiv(ngroups, gps);
-  const int kc = cfg.kc < gps ? cfg.kc : gps;
-  const GemvLayout L{16 * RT, gps, kc, M};
-  const size_t smem = L.bytes();
-  if (smem > 200 * 1024 || kc < 1 || ksplit > 8) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(mxfp4_gemv_kernel<RT, NW>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+template <int NW, bool STMA>
+cudaError_t launch_gemv(const GemvPlan& P, const CUtensorMap& wmap, const CUtensorMap& smap,
+                        const uint8_t* St, const __nv_bfloat16* X, __nv_bfloat16* Out, int N,
+                        int K, int M, cudaStream_t stream) {
+  static int attr_set = 0;  // largest dynamic smem already enabled for this instantiation
+  cudaError_t e = cudaSuccess;
+  if ((int)P.smem > attr_set) {
+    e = cudaFuncSetAttribute(mxfp4_gemv_kernel<NW, STMA>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P.smem);
+    if (e != cudaSuccess) return e;
+    attr_set = (int)P.smem;
+  }
+  GemvArgs a;
+  a.St = St;
+  a.X = X;
+  a.Out = Out;
+  a.N = N;
+  a.K = K;
+  a.M = M;
+  a.gps = P.gps;
+  a.kc = P.kc;
+  a.nstages = P.nstages;
+  a.ntiles = cdiv(N, kTileRows);
+  a.nclusters = P.nclusters;
+  a.tmax = P.tmax;
   cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(cdiv(N, 16 * RT), ksplit, 1);
+  lc.gridDim = dim3(P.ks, P.nclusters, 1);
   lc.blockDim = dim3((NW + 1) * 32, 1, 1);
-  lc.dynamicSmemBytes = smem;
+  lc.dynamicSmemBytes = P.smem;
   lc.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = ksplit;
+  attr[0].val.clusterDim.x = P.ks;
+  attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   lc.attrs = attr;
   lc.numAttrs = 1;
-  return cudaLaunchKernelEx(&lc, mxfp4_gemv_kernel<RT, NW>, W, St, X, Out, N, K, M, gps, kc);
+  return cudaLaunchKernelEx(&lc, mxfp4_gemv_kernel<NW, STMA>, wmap, smap, a);
 }
 
 }  // namespace
@@ -372,25 +432,38 @@ int mxfp4_gemv_launch(const void* W, const void* St, const void* X, void* out, i
   if (!W || !St || !X || !out) return B200KV_ERR_INVALID_ARG;
   if (N <= 0 || K <= 0 || M <= 0) return B200KV_ERR_INVALID_ARG;
   if (M > 8 || (K % 32) != 0) return B200KV_ERR_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(X) & 15) ||
-      (reinterpret_cast<uintptr_t>(out) & 1))
+  // TMA: 16-byte aligned bases and row pitches (K/2 and K/32 bytes)
+  if ((reinterpret_cast<uintptr_t>(W) & 15) ||
+      ((K / 32) % 16 == 0 && (reinterpret_cast<uintptr_t>(St) & 15)) ||
+      (reinterpret_cast<uintptr_t>(X) & 15) || (reinterpret_cast<uintptr_t>(out) & 1))
     return B200KV_ERR_MISALIGNED;
   if (sm_major_current_device() < 10) return B200KV_ERR_NO_DEVICE;
-  const GemvConfig cfg = choose_config(N, K, M);
-  if (cfg.ksplit < 1 || cfg.ksplit > 8) return B200KV_ERR_INVALID_ARG;
-  const uint8_t* w = static_cast<const uint8_t*>(W);
-  const uint8_t* s = static_cast<const uint8_t*>(St);
+  const bool stma = (K / 32) % 16 == 0;  // scale rows are 16-byte multiples
+  const int nw = env_int("B200KV_GEMV_NW", 8);
+  GemvPlan P;
+  if (!plan_gemv(N, K, M, nw, &P)) return B200KV_ERR_UNSUPPORTED;
+  CUtensorMap wmap, smap;
+  if (!encode_u8_2d(&wmap, W, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128, kTileRows, true))
+    return B200KV_ERR_LAUNCH;
+  if (stma) {
+    if (!encode_u8_2d(&smap, St, (uint64_t)K / 32, (uint64_t)N, (uint64_t)K / 32, (uint32_t)P.kc,
+                      kTileRows, false))
+      return B200KV_ERR_LAUNCH;
+  } else {
+    smap = wmap;  // unused
+  }
+  const uint8_t* sb = static_cast<const uint8_t*>(St);
   const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(X);
   __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
-  const int key = cfg.rt * 100 + cfg.nw;
-  switch (key) {
-    case 104: e = launch_gemv<1, 4>(cfg, w, s, x, o, N, K, M, st); break;
-    case 108: e = launch_gemv<1, 8>(cfg, w, s, x, o, N, K, M, st); break;
-    case 204: e = launch_gemv<2, 4>(cfg, w, s, x, o, N, K, M, st); break;
-    case 208: e = launch_gemv<2, 8>(cfg, w, s, x, o, N, K, M, st); break;
-    case 404: e = launch_gemv<4, 4>(cfg, w, s, x, o, N, K, M, st); break;
+  switch (nw * 2 + (stma ? 1 : 0)) {
+    case 9: e = launch_gemv<4, true>(P, wmap, smap, sb, x, o, N, K, M, st); break;
+    case 8: e = launch_gemv<4, false>(P, wmap, smap, sb, x, o, N, K, M, st); break;
+    case 17: e = launch_gemv<8, true>(P, wmap, smap, sb, x, o, N, K, M, st); break;
+    case 16: e = launch_gemv<8, false>(P, wmap, smap, sb, x, o, N, K, M, st); break;
+    case 33: e = launch_gemv<16, true>(P, wmap, smap, sb, x, o, N, K, M, st); break;
+    case 32: e = launch_gemv<16, false>(P, wmap, smap, sb, x, o, N, K, M, st); break;
     default: return B200KV_ERR_INVALID_ARG;
   }
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;

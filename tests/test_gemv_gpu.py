@@ -103,12 +103,14 @@ def test_ragged_shapes(cuda, N, K, M):
     assert MO.rel_to_max_err(Y, ref) < TOL
 
 
-@pytest.mark.parametrize("ksplit", ["1", "2", "4", "8"])
-@pytest.mark.parametrize("rt,nw", [("1", "4"), ("1", "8"), ("2", "4"), ("2", "8"), ("4", "4")])
-def test_launch_geometries(cuda, monkeypatch, ksplit, rt, nw):
+@pytest.mark.parametrize("ksplit", ["1", "2", "4"])
+@pytest.mark.parametrize("nw,kc,stages", [("4", "16", "2"), ("4", "32", "4"), ("8", "64", "3"),
+                                          ("8", "16", "8")])
+def test_launch_geometries(cuda, monkeypatch, ksplit, nw, kc, stages):
     monkeypatch.setenv("B200KV_GEMV_KSPLIT", ksplit)
-    monkeypatch.setenv("B200KV_GEMV_RT", rt)
     monkeypatch.setenv("B200KV_GEMV_NW", nw)
+    monkeypatch.setenv("B200KV_GEMV_KC", kc)
+    monkeypatch.setenv("B200KV_GEMV_STAGES", stages)
     W, S, St, X = MO.make_case(200, 2048, 5, seed=11)
     ref = MO.mxfp4_linear_reference(W, S, X)
     Y = _run(W, St, X, cuda).float().cpu()
