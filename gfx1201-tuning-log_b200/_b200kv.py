@@ -56,6 +56,17 @@ lib.b200kv_decode_attn.argtypes = (
      _i32, _i32, _i32,                # kv_dtype, out_by_qsl, num_splits
      _vp])                            # stream
 
+lib.b200kv_prefill_attn.restype = _i32
+lib.b200kv_prefill_attn.argtypes = (
+    [_vp, _i64, _i64,                 # q, strides
+     _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,  # caches, strides
+     _vp, _i64, _i64,                 # out, strides
+     _vp, _vp, _vp, _i64,             # cu_seqlens_q, seq_lens, block_table, bt stride
+     _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
+     _i32, _i32, _i32, _i32,          # num_seqs, max_qlen, q0_single, qlen_single
+     _i32, _i32, _i32, _i32, _i32,    # hq, hkv, head_dim, block_size, kv_dtype
+     _vp])
+
 lib.b200kv_kv_write.restype = _i32
 lib.b200kv_kv_write.argtypes = ([_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp] + [_i64] * 6 +
                                 [_vp, _vp, _vp] + [_i32] * 5 + [_vp])

@@ -63,6 +63,15 @@ int kv_write_launch(const void* key, int64_t k_st, int64_t k_sh, const void* val
                     const float* k_scale, const float* v_scale, int num_tokens, int hkv,
                     int head_dim, int block_size, int kv_dtype, void* stream);
 
+int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
+                        const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
+                        int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
+                        const int32_t* cu_seqlens_q, const int32_t* seq_lens,
+                        const int32_t* block_table, int64_t bt_stride, const float* k_scale,
+                        const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
+                        int q0_single, int qlen_single, int hq, int hkv, int head_dim,
+                        int block_size, int kv_dtype, void* stream);
+
 void set_last_error(int e) { t_last_error = e; }
 
 }  // namespace b200kv
@@ -135,6 +144,22 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
       out_stride_tok, out_stride_head, qsl, seq_lens, block_table, bt_stride, k_scale, v_scale,
       sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
       max_seq_len_hint, kv_dtype, out_by_qsl, num_splits, stream);
+}
+
+int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                        const void* k_cache, const void* v_cache, int64_t sk0, int64_t sk1,
+                        int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2, void* out,
+                        int64_t out_stride_tok, int64_t out_stride_head,
+                        const int32_t* cu_seqlens_q, const int32_t* seq_lens,
+                        const int32_t* block_table, int64_t bt_stride, const float* k_scale,
+                        const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
+                        int q0_single, int qlen_single, int num_q_heads, int num_kv_heads,
+                        int head_dim, int block_size, int kv_dtype, void* stream) {
+  return b200kv::prefill_attn_launch(
+      q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
+      out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
+      v_scale, sm_scale, num_seqs, max_qlen, q0_single, qlen_single, num_q_heads, num_kv_heads,
+      head_dim, block_size, kv_dtype, stream);
 }
 
 int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_head,

@@ -1,0 +1,74 @@
+"""fp8-KV causal prefill attention -- drop-in for the reference module
+vllm-fp8kv/fp8kv_prefill.py: `run` (:124-144) with the same signature, backed
+by the tcgen05 kernel in csrc/prefill_attn.cu, plus `prefill_attention`, the
+varlen generalisation (several sequences packed with cu_seqlens, each with
+its own block-table row and kv length), and `_install`, the vLLM
+TritonAttentionImpl.forward patch gated by FP8KV_PREFILL=1 (:147-198).
+
+BM / BN / warps / stages tuned the Triton tile and are accepted and ignored:
+the B200 kernel always uses 128-row query tiles (GQA heads packed with
+tokens, as the reference packs them) and 128-key KV tiles.
+"""
+import os
+import sys
+
+import torch
+
+from _b200kv import KV_BF16, KV_FP8_E4M3, check, lib
+
+
+def _scale(s, device):
+    if torch.is_tensor(s):
+        return s.to(device=device, dtype=torch.float32).reshape(-1)[:1].contiguous()
+    return torch.tensor([float(s)], device=device, dtype=torch.float32)
+
+
+def _kv_dtype(t):
+    if t.dtype == torch.float8_e4m3fn:
+        return KV_FP8_E4M3
+    if t.dtype == torch.bfloat16:
+        return KV_BF16
+    raise TypeError(f"unsupported KV cache dtype {t.dtype}")
+
+
+def _launch(q, k_cache, v_cache, out, cu, lens, bt, kscale, vscale, sm_scale, num_seqs,
+            max_qlen, q0_single, qlen_single):
+    if q.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise TypeError("q and out must be bfloat16")
+    if bt.dtype != torch.int32 or bt.stride(-1) != 1:
+        raise TypeError("block_table must be int32 with contiguous rows")
+    dev = q.device
+    ks, vs = _scale(kscale, dev), _scale(vscale, dev)
+    check(lib.b200kv_prefill_attn(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_cache.data_ptr(), v_cache.data_ptr(),
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+        v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        cu.data_ptr() if cu is not None else None,
+        lens.data_ptr() if lens is not None else None,
+        bt.data_ptr(), bt.stride(0), ks.data_ptr(), vs.data_ptr(), float(sm_scale),
+        num_seqs, max_qlen, q0_single, qlen_single, q.shape[1], k_cache.shape[2], q.shape[2],
+        k_cache.shape[1], _kv_dtype(k_cache), torch.cuda.current_stream(dev).cuda_stream),
+        "b200kv_prefill_attn")
+    return out
+
+
+def run(q, k_cache, v_cache, out, bt, kscale, vscale, sm_scale, q0, qlen,
+        BM=64, BN=32, warps=2, stages=2):
+    """Single-sequence causal prefill (reference signature): query rows 0..qlen-1
+    at positions q0..q0+qlen-1 over keys 0..q0+qlen-1 through block_table row 0."""
+    return _launch(q, k_cache, v_cache, out, None, None, bt, kscale, vscale, sm_scale,
+                   1, int(qlen), int(q0), int(qlen))
+
+
+def prefill_attention(q, k_cache, v_cache, out, cu_seqlens_q, seq_lens, block_table,
+                      k_scale, v_scale, sm_scale, max_qlen=None):
+    """Varlen causal prefill: sequence s owns query rows cu[s]..cu[s+1]-1 and
+    kv length seq_lens[s]; the last qlen keys are its own tokens (q0 = L - qlen)."""
+    if cu_seqlens_q.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise TypeError("cu_seqlens_q and seq_lens must be int32")
+    if max_qlen is None:  # host sync; callers on the hot path pass it
+        max_qlen = int((cu_seqlens_q[1:] - cu_seqlens_q[:-1]).max().item())
+    return _launch(q, k_cache, v_cache, out, cu_seqlens_q, seq_lens, block_table, k_scale,
+                   v_scale, sm_scale, block_table.shape[0], int(max_qlen), 0, 0)

@@ -4,6 +4,8 @@
  *
  *   - MXFP4 (e2m1 weights + e8m0 group scales) W4A16 matvec / skinny GEMM
  *   - fp8-e4m3 (or bf16) paged-KV split-K decode attention
+ *   - fp8-e4m3 paged-KV causal (varlen) prefill attention on tcgen05
+ *   - the paged KV-cache write (bf16 -> fp8 quantise + scatter)
  *
  * Conventions shared by every entry point:
  *   - All pointers are device pointers unless stated otherwise; the caller owns
@@ -126,6 +128,37 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
                        int num_seqs, int num_q_heads, int num_kv_heads, int head_dim,
                        int block_size, int max_blocks_per_seq, int max_seq_len_hint,
                        int kv_dtype, int out_by_qsl, int num_splits, void* stream);
+
+/* ---- fp8 paged-KV causal prefill attention -----------------------------------
+ *
+ * For every sequence s with query rows cu_seqlens_q[s] .. cu_seqlens_q[s+1]-1
+ * (qlen of them) and kv length L = seq_lens[s], query i sits at position
+ * q0 + i with q0 = L - qlen and attends keys 0 .. q0 + i of the same kv head:
+ *
+ *   out[row, h, :] = v_scale * softmax_j<=q0+i((q . K[j]) * sm_scale * k_scale) @ V
+ *
+ * Keys are gathered through block_table[s, :] exactly as in b200kv_decode_attn.
+ * When cu_seqlens_q and seq_lens are both NULL the call is the reference's
+ * single-sequence form (vllm-fp8kv/fp8kv_prefill.py:124-144, `run(..., q0, qlen)`):
+ * num_seqs must be 1, rows 0 .. qlen_single-1, q0 = q0_single, table row 0.
+ *
+ * Replaces the reference's Triton kernel vllm-fp8kv/fp8kv_prefill.py:32-121,
+ * generalised to varlen batches.  Runs on tcgen05 tensor cores (f16 operands,
+ * fp32 accumulation in tensor memory).  head_dim 128, GQA 1/2/4/8.
+ *   max_qlen   upper bound of the per-sequence query lengths (grid size);
+ *              ignored in the single-sequence form.
+ */
+int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                        const void* k_cache, const void* v_cache,
+                        int64_t sk0, int64_t sk1, int64_t sk2,
+                        int64_t sv0, int64_t sv1, int64_t sv2,
+                        void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        const int32_t* cu_seqlens_q, const int32_t* seq_lens,
+                        const int32_t* block_table, int64_t bt_stride,
+                        const float* k_scale, const float* v_scale, float sm_scale,
+                        int num_seqs, int max_qlen, int q0_single, int qlen_single,
+                        int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                        int kv_dtype, void* stream);
 
 /* ---- paged KV-cache write ------------------------------------------------------
  *
