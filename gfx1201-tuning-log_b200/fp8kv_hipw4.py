@@ -1,0 +1,206 @@
+"""Route small-M MXFP4 linears through the B200 matvec -- the drop-in for the
+reference module h4mv/fp8kv_hipw4.py.
+
+With FP8KV_HIPW4=1 the CUDA implementation of the op radiance::mxfp4_linear
+(x, weight, weight_scale, wref) -> Tensor is replaced, as in the reference
+(fp8kv_hipw4.py:14-99):
+
+  * gate (fp8kv_hipw4.py:70-76): x 2-D, contiguous, bf16, 1 <= M <= MAX_M;
+    K % 32 == 0; N >= 8; weight_scale rows == K/32; weight 16-byte aligned;
+  * the checkpoint's scale layout [K/32, N] is repacked once to [N, K/32] and
+    cached by (data_ptr, shape), never while a CUDA graph is being captured
+    (fp8kv_hipw4.py:32-43);
+  * out = torch.empty(M, N, bf16) and one launch on the current stream;
+  * everything else goes to the op's original CUDA body.
+
+FP8KV_HIPW4_MAX_M keeps the reference's default of 4; the B200 kernel itself
+handles M <= 8 (the reference capped at 4 because of a gfx1201 M=8 cliff).
+
+The reference stole the body of the radiance fork's op once that module
+appeared (a 1500 x 0.2 s poll, fp8kv_hipw4.py:45-59).  The fork is not part
+of this environment, so when `radiance_mxfp4` cannot be imported this module
+defines the op schema itself; the original body is then `mxfp4_linear_chunked`,
+which runs the same B200 kernel over 8-row slices of x, so no shape falls back
+to a CPU or Python implementation.
+"""
+import os
+import sys
+import threading
+
+OP = "radiance::mxfp4_linear"
+SCHEMA = "mxfp4_linear(Tensor x, Tensor weight, Tensor weight_scale, Tensor wref) -> Tensor"
+
+_state = {"installed": False, "lib": None, "fast": 0, "slow": 0, "calls": 0, "logged": False}
+_repack_cache = {}
+
+
+def max_m():
+    return int(os.environ.get("FP8KV_HIPW4_MAX_M", "4"))
+
+
+def _capturing(t):
+    import torch
+    return t.is_cuda and torch.cuda.is_current_stream_capturing()
+
+
+def scale_t_for(s):
+    """weight_scale [K/32, N] -> [N, K/32] contiguous, cached by (data_ptr, shape);
+    None while capturing a CUDA graph (no allocations or side launches then)."""
+    import torch
+    key = (s.data_ptr(), tuple(s.shape), s.device)
+    ent = _repack_cache.get(key)
+    if ent is not None:
+        return ent
+    if _capturing(s):
+        return None
+    st = s.t().contiguous()
+    if len(_repack_cache) > 512:
+        _repack_cache.clear()
+    _repack_cache[key] = st
+    return st
+
+
+def eligible(x, weight, weight_scale, m_limit):
+    """The reference's gate (fp8kv_hipw4.py:70-76)."""
+    import torch
+    if not (torch.is_tensor(x) and x.dim() == 2 and x.is_contiguous()
+            and x.dtype == torch.bfloat16 and 1 <= x.shape[0] <= m_limit):
+        return False
+    N = weight.shape[0]
+    K = weight.shape[1] * 2
+    return (K % 32 == 0 and N >= 8 and weight_scale.shape[0] == K // 32
+            and weight.data_ptr() % 16 == 0 and weight.dtype == torch.uint8)
+
+
+def mxfp4_linear_chunked(x, weight, weight_scale, wref=None):
+    """x [M, K] @ dequant(weight, weight_scale)^T for any M, through the B200
+    matvec on 8-row slices of x (weight_scale in the checkpoint layout)."""
+    import torch
+
+    import h4mv
+    M = x.shape[0]
+    N = weight.shape[0]
+    st = scale_t_for(weight_scale)
+    if st is None:
+        raise RuntimeError("mxfp4_linear: scale repack needed during CUDA graph capture; "
+                           "run one eager call first")
+    xc = x.contiguous().to(torch.bfloat16)
+    out = torch.empty((M, N), device=x.device, dtype=torch.bfloat16)
+    for m0 in range(0, M, h4mv.MAX_M):
+        h4mv.mxfp4_gemv(xc[m0:m0 + h4mv.MAX_M], weight, st, out=out[m0:m0 + h4mv.MAX_M])
+    return out
+
+
+def _define_op_if_missing(m_limit):
+    """Define radiance::mxfp4_linear when the fork is absent, with the patched
+    implementation over the chunked body as its CUDA kernel.  Returns False
+    when the op already exists."""
+    import torch
+    try:
+        torch.ops.radiance.mxfp4_linear
+        return False
+    except (AttributeError, RuntimeError):
+        pass
+    lib = torch.library.Library("radiance", "DEF")
+    lib.define(SCHEMA)
+    lib.impl("mxfp4_linear", make_patched(mxfp4_linear_chunked, m_limit), "CUDA")
+
+    def _meta(x, weight, weight_scale, wref):
+        return x.new_empty((x.shape[0], weight.shape[0]), dtype=torch.bfloat16)
+    lib.impl("mxfp4_linear", _meta, "Meta")
+    _state["lib"] = lib
+    _state["installed"] = True
+    return True
+
+
+def make_patched(body, m_limit):
+    import torch
+
+    import h4mv
+
+    def _patched(x, weight, weight_scale, wref):
+        try:
+            if _state["calls"] < 3:
+                _state["calls"] += 1
+                sys.stderr.write(f"[hipw4] call#{_state['calls']} x={tuple(x.shape)}/{x.dtype}"
+                                 f"/c={x.is_contiguous()} w={tuple(weight.shape)}/{weight.dtype}"
+                                 f" s={tuple(weight_scale.shape)}"
+                                 f" cap={_capturing(x)}\n")
+            if eligible(x, weight, weight_scale, m_limit):
+                st = scale_t_for(weight_scale)
+                if st is not None:
+                    out = h4mv.mxfp4_gemv(x, weight, st)
+                    _state["fast"] += 1
+                    if not _state["logged"]:
+                        _state["logged"] = True
+                        sys.stderr.write(f"[hipw4] ENGAGED N={weight.shape[0]} K={weight.shape[1] * 2} "
+                                         f"M={x.shape[0]}\n")
+                    return out
+        except Exception as e:
+            sys.stderr.write(f"[hipw4] fast path failed ({e!r}), falling back\n")
+        _state["slow"] += 1
+        return body(x, weight, weight_scale, wref)
+
+    return _patched
+
+
+def _override(body):
+    import torch
+    patched = make_patched(body, max_m())
+    lib = torch.library.Library("radiance", "IMPL")
+    lib.impl("mxfp4_linear", patched, "CUDA")
+    _state["impl_lib"] = lib
+    _state["installed"] = True
+    sys.stderr.write("[hipw4] op impl overridden\n")
+
+
+def _install():
+    if os.environ.get("FP8KV_HIPW4", "0") != "1":
+        return False
+    if _state["installed"]:
+        return True
+    try:
+        import torch  # noqa: F401
+
+        import h4mv  # noqa: F401  (loads libb200kv.so: fail here, not on the first call)
+    except Exception as e:
+        sys.stderr.write(f"[hipw4] lib load fail: {e}\n")
+        return False
+    try:
+        import radiance_mxfp4 as rm  # noqa: F401
+        have_fork = True
+    except Exception:
+        have_fork = False
+    if not have_fork:
+        if _define_op_if_missing(max_m()):
+            sys.stderr.write("[hipw4] installed (radiance op defined here)\n")
+        else:
+            _override(mxfp4_linear_chunked)
+            sys.stderr.write("[hipw4] installed\n")
+        return True
+
+    def _poll():
+        body = None
+        for _ in range(1500):
+            try:
+                import radiance_mxfp4 as rm
+                if getattr(rm, "WPERM", False):
+                    sys.stderr.write("[hipw4] WPERM=1, standing down\n")
+                    return
+                f = rm.mxfp4_linear
+                body = f._backend_fns.get("cuda") or f._init_fn
+                break
+            except Exception:
+                import time
+                time.sleep(0.2)
+        if body is None:
+            sys.stderr.write("[hipw4] radiance module never appeared\n")
+            return
+        _override(body)
+
+    threading.Thread(target=_poll, daemon=True).start()
+    sys.stderr.write("[hipw4] installed\n")
+    return True
+
+
+_install()

@@ -2,8 +2,9 @@
 vllm-fp8kv/fp8kv_prefill.py: `run` (:124-144) with the same signature, backed
 by the tcgen05 kernel in csrc/prefill_attn.cu, plus `prefill_attention`, the
 varlen generalisation (several sequences packed with cu_seqlens, each with
-its own block-table row and kv length), and `_install`, the vLLM
-TritonAttentionImpl.forward patch gated by FP8KV_PREFILL=1 (:147-198).
+its own block-table row and kv length), and `_install`, which with
+FP8KV_PREFILL=1 (:147-198) makes the TritonAttentionImpl.forward patch of
+fp8kv_override route prefill batches here as well.
 
 BM / BN / warps / stages tuned the Triton tile and are accepted and ignored:
 the B200 kernel always uses 128-row query tiles (GQA heads packed with
@@ -70,5 +71,25 @@ def prefill_attention(q, k_cache, v_cache, out, cu_seqlens_q, seq_lens, block_ta
         raise TypeError("cu_seqlens_q and seq_lens must be int32")
     if max_qlen is None:  # host sync; callers on the hot path pass it
         max_qlen = int((cu_seqlens_q[1:] - cu_seqlens_q[:-1]).max().item())
+    num_seqs = cu_seqlens_q.shape[0] - 1
+    if seq_lens.shape[0] < num_seqs or block_table.shape[0] < num_seqs:
+        raise ValueError("seq_lens and block_table need a row per sequence of cu_seqlens_q")
     return _launch(q, k_cache, v_cache, out, cu_seqlens_q, seq_lens, block_table, k_scale,
-                   v_scale, sm_scale, block_table.shape[0], int(max_qlen), 0, 0)
+                   v_scale, sm_scale, num_seqs, int(max_qlen), 0, 0)
+
+
+def _install():
+    """FP8KV_PREFILL=1: prefill batches (max_query_len > 1) go to this kernel
+    through the fp8kv_override patch of TritonAttentionImpl.forward; the gate
+    and the fallback to vLLM's own forward are that module's."""
+    if os.environ.get("FP8KV_PREFILL", "0") != "1":
+        return False
+    import fp8kv_override
+    fp8kv_override.enable_prefill()
+    ok = fp8kv_override._install()
+    if ok:
+        sys.stderr.write("[fp8kv-prefill] installed\n")
+    return ok
+
+
+_install()
