@@ -209,6 +209,58 @@ def time_graph(graph, steps, warmup, barrier=None):
     return e0.elapsed_time(e1) / steps
 
 
+PREFILL_LENS = (512, 1024, 1536, 2048)
+
+
+def prefill_flops(lens, hq=HQ, d=D):
+    """Causal attention FLOPs: 4 * D * HQ * sum L(L+1)/2 (QK^T and PV)."""
+    return 4 * d * hq * sum(L * (L + 1) // 2 for L in lens)
+
+
+def prefill_part(dev, steps, warmup, barrier=None):
+    """Config 3: four sequences {512, 1024, 1536, 2048} packed with cu_seqlens,
+    bf16 K/V ~ N(0,1) written into a paged fp8 pool (block 16, random block
+    permutation, per-tensor amax/448 scales) by the KV-write kernel, then one
+    varlen causal prefill call.  Returns (us per call, FLOPs per call)."""
+    import fp8kv_prefill
+    import kv_cache
+    lens = PREFILL_LENS
+    T = sum(lens)
+    g = torch.Generator(device=dev).manual_seed(3)
+    q = torch.randn(T, HQ, D, device=dev, generator=g).to(torch.bfloat16)
+    key = torch.randn(T, HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    val = torch.randn(T, HKV, D, device=dev, generator=g).to(torch.bfloat16)
+    nblk = [L // PBLK for L in lens]
+    nb = sum(nblk)
+    perm = torch.randperm(nb, device=dev, generator=g).to(torch.int32)
+    bt = torch.zeros(len(lens), max(nblk), dtype=torch.int32, device=dev)
+    slots, pos = [], 0
+    for s, L in enumerate(lens):
+        bt[s, :nblk[s]] = perm[pos:pos + nblk[s]]
+        pos += nblk[s]
+        t = torch.arange(L, device=dev)
+        slots.append(bt[s, t // PBLK].long() * PBLK + t % PBLK)
+    slots = torch.cat(slots)
+    ks = (key.float().abs().max() / 448.0).reshape(1)
+    vs = (val.float().abs().max() / 448.0).reshape(1)
+    kc = torch.zeros(nb, PBLK, HKV, D, dtype=torch.uint8, device=dev).view(torch.float8_e4m3fn)
+    vc = torch.zeros_like(kc)
+    kv_cache.reshape_and_cache_flash(key, val, kc, vc, slots, "fp8", ks, vs)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32, device=dev)
+    seq_lens = torch.tensor(lens, dtype=torch.int32, device=dev)
+    out = torch.empty(T, HQ, D, dtype=torch.bfloat16, device=dev)
+    reps = 10
+
+    def call():
+        for _ in range(reps):
+            fp8kv_prefill.prefill_attention(q, kc, vc, out, cu, seq_lens, bt, ks, vs, D ** -0.5,
+                                            max_qlen=max(lens))
+    graph = capture(call)
+    ms = time_graph(graph, max(steps // 2, 3), warmup, barrier) / reps
+    del graph
+    return ms * 1e3, prefill_flops(lens)
+
+
 def max_over_ranks(x, dist_on, dev):
     if not dist_on:
         return x
@@ -312,6 +364,8 @@ def run_b200(args):
     # ---- per-kernel breakdown (same graphs, kernel class alone) ------------
     ms_gemv = max_over_ranks(time_graph(g_gemv, args.steps, 2, barrier), dist_on, dev)
     ms_attn = max_over_ranks(time_graph(g_attn, args.steps, 2, barrier), dist_on, dev)
+    us_pre, flops_pre = prefill_part(dev, args.steps, 2, barrier)
+    us_pre = max_over_ranks(us_pre, dist_on, dev)
     gemv_bytes_step = args.layers * sum(gemv_bytes(N, K, args.batch) for _, N, K in SHAPES)
     attn_bytes_step = args.layers * decode_bytes(args.batch, args.ctx)
 
@@ -377,6 +431,14 @@ def run_b200(args):
                                "gbs": gemv_gbs},
                 "decode_attn": {"us_per_step": ms_attn * 1e3, "launches_per_step": args.layers,
                                 "gbs": attn_bytes_step / (ms_attn * 1e-3) / 1e9},
+                "prefill_attn": {"workload": "config 3: varlen causal prefill, 4 seqs "
+                                             f"{list(PREFILL_LENS)}, GQA 32/8, D 128, fp8 paged KV",
+                                 "us_per_call": us_pre, "gflop_per_call": flops_pre / 1e9,
+                                 "tflops": flops_pre / (us_pre * 1e-6) / 1e12,
+                                 "bound": "tensor", "peak_tflops": peaks.get("bf16_tflops", 1590.0),
+                                 "frac": flops_pre / (us_pre * 1e-6) / 1e12
+                                 / peaks.get("bf16_tflops", 1590.0),
+                                 "note": "timed outside the decode step (not part of value)"},
             },
             "roofline": {"bound": "hbm", "kernel": "mxfp4_gemv_kernel",
                          "achieved": gemv_gbs, "peak": hbm_peak, "unit": "GB/s",

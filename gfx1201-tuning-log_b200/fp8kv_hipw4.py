@@ -45,18 +45,19 @@ def _capturing(t):
 
 def scale_t_for(s):
     """weight_scale [K/32, N] -> [N, K/32] contiguous, cached by (data_ptr, shape);
-    None while capturing a CUDA graph (no allocations or side launches then)."""
-    import torch
+    None while capturing a CUDA graph (no allocations or side launches then).
+    The cache entry holds the source tensor too, so its address cannot be
+    freed and handed to another tensor while the entry exists."""
     key = (s.data_ptr(), tuple(s.shape), s.device)
     ent = _repack_cache.get(key)
     if ent is not None:
-        return ent
+        return ent[1]
     if _capturing(s):
         return None
     st = s.t().contiguous()
     if len(_repack_cache) > 512:
         _repack_cache.clear()
-    _repack_cache[key] = st
+    _repack_cache[key] = (s, st)
     return st
 
 
