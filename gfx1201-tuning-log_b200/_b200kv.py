@@ -64,7 +64,8 @@ lib.b200kv_prefill_attn.argtypes = (
      _vp, _vp, _vp, _i64,             # cu_seqlens_q, seq_lens, block_table, bt stride
      _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
      _i32, _i32, _i32, _i32,          # num_seqs, max_qlen, q0_single, qlen_single
-     _i32, _i32, _i32, _i32, _i32,    # hq, hkv, head_dim, block_size, kv_dtype
+     _i32, _i32, _i32, _i32,          # hq, hkv, head_dim, block_size
+     _i32, _i32,                      # num_blocks, kv_dtype
      _vp])
 
 lib.b200kv_kv_write.restype = _i32

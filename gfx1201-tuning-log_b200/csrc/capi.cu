@@ -70,7 +70,7 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int hq, int hkv, int head_dim,
-                        int block_size, int kv_dtype, void* stream);
+                        int block_size, int num_blocks, int kv_dtype, void* stream);
 
 void set_last_error(int e) { t_last_error = e; }
 
@@ -154,12 +154,13 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int num_q_heads, int num_kv_heads,
-                        int head_dim, int block_size, int kv_dtype, void* stream) {
+                        int head_dim, int block_size, int num_blocks, int kv_dtype,
+                        void* stream) {
   return b200kv::prefill_attn_launch(
       q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
       out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
       v_scale, sm_scale, num_seqs, max_qlen, q0_single, qlen_single, num_q_heads, num_kv_heads,
-      head_dim, block_size, kv_dtype, stream);
+      head_dim, block_size, num_blocks, kv_dtype, stream);
 }
 
 int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_head,

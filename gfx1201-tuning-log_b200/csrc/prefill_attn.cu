@@ -367,6 +367,15 @@ cudaError_t launch_prefill(const PrefillParams& p, int qtiles, int hkv, int ns, 
 
 }  // namespace
 
+int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
+                       const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
+                       int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
+                       const int32_t* cu_seqlens_q, const int32_t* seq_lens,
+                       const int32_t* block_table, int64_t bt_stride, const float* k_scale,
+                       const float* v_scale, float sm_scale, int num_seqs, int qmax,
+                       int q0_single, int qlen_single, int gqa, int hkv, int block_size,
+                       int num_blocks, void* stream);
+
 int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                         const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
                         int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
@@ -374,9 +383,10 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int hq, int hkv, int head_dim,
-                        int block_size, int kv_dtype, void* stream) {
+                        int block_size, int num_blocks, int kv_dtype, void* stream) {
   if (!q || !k_cache || !v_cache || !out || !block_table) return B200KV_ERR_INVALID_ARG;
-  if (num_seqs <= 0 || hq <= 0 || hkv <= 0 || block_size <= 0 || hq % hkv) return B200KV_ERR_INVALID_ARG;
+  if (num_seqs <= 0 || hq <= 0 || hkv <= 0 || block_size <= 0 || num_blocks < 0 || hq % hkv)
+    return B200KV_ERR_INVALID_ARG;
   if ((cu_seqlens_q == nullptr) != (seq_lens == nullptr)) return B200KV_ERR_INVALID_ARG;
   if (!cu_seqlens_q && (num_seqs != 1 || qlen_single < 0 || q0_single < 0)) return B200KV_ERR_INVALID_ARG;
   if (head_dim != kD) return B200KV_ERR_UNSUPPORTED;
@@ -396,6 +406,14 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
   if (sm_major_current_device() < 10) return B200KV_ERR_NO_DEVICE;
   const int qmax = cu_seqlens_q ? max_qlen : qlen_single;
   if (qmax <= 0) return B200KV_OK;
+  if (fp8) {  // 8-bit tensor-core path with TMA page gathers (csrc/prefill_fp8.cu)
+    const int r = prefill_fp8_launch(q, q_st, q_sh, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2,
+                                     out, o_st, o_sh, cu_seqlens_q, seq_lens, block_table,
+                                     bt_stride, k_scale, v_scale, sm_scale, num_seqs, qmax,
+                                     q0_single, qlen_single, gqa, hkv, block_size, num_blocks,
+                                     stream);
+    if (r >= 0) return r;
+  }
   PrefillParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_st = q_st;

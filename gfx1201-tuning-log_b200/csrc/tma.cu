@@ -40,4 +40,21 @@ bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64
   return r == CUDA_SUCCESS;
 }
 
+bool encode_paged_kv(CUtensorMap* map, const void* base, uint32_t row_bytes, uint32_t heads,
+                     uint32_t tokens, uint64_t blocks, uint64_t s_head, uint64_t s_tok,
+                     uint64_t s_blk) {
+  PFN_cuTensorMapEncodeTiled enc = get_encode();
+  if (!enc || row_bytes != 128 || tokens == 0 || tokens > 256 || blocks == 0) return false;
+  if ((s_head | s_tok | s_blk) & 15) return false;
+  const cuuint64_t dims[4] = {row_bytes, heads, tokens, blocks};
+  const cuuint64_t strides[3] = {s_head, s_tok, s_blk};
+  const cuuint32_t box[4] = {row_bytes, 1, tokens, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace b200kv

@@ -28,6 +28,28 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
+// Encodes a 4-D uint8 tensor map over a paged KV cache [blocks][tokens][heads][row]
+// (row = one head's `row_bytes`, byte strides s_head < s_tok < s_blk) with box
+// [row_bytes, 1 head, `tokens` tokens, 1 block] and 128-byte swizzle, so one
+// load brings one head's rows of one page into shared memory as a swizzled
+// [tokens][row_bytes] tile.  row_bytes must be 128.  Out-of-range block ids
+// read as zeros.
+bool encode_paged_kv(CUtensorMap* map, const void* base, uint32_t row_bytes, uint32_t heads,
+                     uint32_t tokens, uint64_t blocks, uint64_t s_head, uint64_t s_tok,
+                     uint64_t s_blk);
+
+// 4-D tiled TMA load of the box at (c0 bytes, c1, c2, c3), completion counted on
+// `bar`.  c0 must be a multiple of 16.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

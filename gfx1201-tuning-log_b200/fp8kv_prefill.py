@@ -50,7 +50,8 @@ def _launch(q, k_cache, v_cache, out, cu, lens, bt, kscale, vscale, sm_scale, nu
         lens.data_ptr() if lens is not None else None,
         bt.data_ptr(), bt.stride(0), ks.data_ptr(), vs.data_ptr(), float(sm_scale),
         num_seqs, max_qlen, q0_single, qlen_single, q.shape[1], k_cache.shape[2], q.shape[2],
-        k_cache.shape[1], _kv_dtype(k_cache), torch.cuda.current_stream(dev).cuda_stream),
+        k_cache.shape[1], k_cache.shape[0], _kv_dtype(k_cache),
+        torch.cuda.current_stream(dev).cuda_stream),
         "b200kv_prefill_attn")
     return out
 

@@ -143,10 +143,16 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
  * num_seqs must be 1, rows 0 .. qlen_single-1, q0 = q0_single, table row 0.
  *
  * Replaces the reference's Triton kernel vllm-fp8kv/fp8kv_prefill.py:32-121,
- * generalised to varlen batches.  Runs on tcgen05 tensor cores (f16 operands,
- * fp32 accumulation in tensor memory).  head_dim 128, GQA 1/2/4/8.
+ * generalised to varlen batches.  Runs on tcgen05 tensor cores with fp32
+ * accumulation in tensor memory: fp8 caches with block_size 16/32/64/128 take
+ * the fp8 MMA path (pages gathered by TMA straight from the cache, query and
+ * probabilities split into two e4m3 terms each, so both products keep a
+ * bf16-sized significand); other caches take an f16 path.  head_dim 128,
+ * GQA 1/2/4/8.
  *   max_qlen   upper bound of the per-sequence query lengths (grid size);
  *              ignored in the single-sequence form.
+ *   num_blocks number of blocks in the cache (its first dimension): block
+ *              ids outside [0, num_blocks) read as zeros on the fp8 path.
  */
 int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                         const void* k_cache, const void* v_cache,
@@ -158,7 +164,7 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         const float* k_scale, const float* v_scale, float sm_scale,
                         int num_seqs, int max_qlen, int q0_single, int qlen_single,
                         int num_q_heads, int num_kv_heads, int head_dim, int block_size,
-                        int kv_dtype, void* stream);
+                        int num_blocks, int kv_dtype, void* stream);
 
 /* ---- paged KV-cache write ------------------------------------------------------
  *

@@ -146,3 +146,67 @@ def test_bf16_cache(cuda):
     ref = FO.prefill_reference(q, k, v, torch.tensor([0, ctx], dtype=torch.int32),
                                torch.tensor([ctx], dtype=torch.int32), bt, 1.0, 1.0, D ** -0.5)
     _check(out, ref)
+
+
+def _paged_case(lens_q, lens_kv, pblk, seed, hkv=HKV, hq=HQ, unused_bt=0):
+    g = torch.Generator().manual_seed(seed)
+    nblk = [math.ceil(L / pblk) for L in lens_kv]
+    nb = sum(nblk) + 3
+    k = (torch.randn(nb, pblk, hkv, D, generator=g) * 2).to(torch.float8_e4m3fn)
+    v = (torch.randn(nb, pblk, hkv, D, generator=g) * 2).to(torch.float8_e4m3fn)
+    perm = torch.randperm(nb, generator=g).to(torch.int32)
+    bt = torch.full((len(lens_kv), max(nblk) + 2), unused_bt, dtype=torch.int32)
+    pos = 0
+    for s, n in enumerate(nblk):
+        bt[s, :n] = perm[pos:pos + n]
+        pos += n
+    T = sum(lens_q)
+    q = torch.randn(T, hq, D, generator=g).to(torch.bfloat16)
+    cu = torch.tensor([0] + torch.tensor(lens_q).cumsum(0).tolist(), dtype=torch.int32)
+    return q, k, v, bt, cu, torch.tensor(lens_kv, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("pblk", [16, 32, 64, 128])
+def test_block_sizes(cuda, pblk):
+    """Every block size the TMA page gather takes (one load per page and head)."""
+    import fp8kv_prefill
+    lens_q, lens_kv = [300, 1, 129], [300, 200, 400]
+    q, k, v, bt, cu, lens = _paged_case(lens_q, lens_kv, pblk, seed=pblk)
+    out = torch.zeros_like(q, device=cuda)
+    fp8kv_prefill.prefill_attention(q.to(cuda), k.to(cuda), v.to(cuda), out, cu.to(cuda),
+                                    lens.to(cuda), bt.to(cuda), 0.8, 1.1, D ** -0.5, max_qlen=300)
+    _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 0.8, 1.1, D ** -0.5))
+
+
+def test_non_finite_bytes_past_the_sequence(cuda):
+    """Cache slots past seq_len hold NaN codes and the unused block-table entries
+    point outside the cache: neither may reach the output."""
+    import fp8kv_prefill
+    lens_q, lens_kv = [37, 90], [37, 250]
+    q, k, v, bt, cu, lens = _paged_case(lens_q, lens_kv, PBLK, seed=77, unused_bt=1 << 30)
+    kb, vb = k.view(torch.uint8), v.view(torch.uint8)
+    for s, L in enumerate(lens_kv):
+        last = int(bt[s, (L - 1) // PBLK])
+        kb[last, L % PBLK or PBLK:] = 0x7F
+        vb[last, L % PBLK or PBLK:] = 0x7F
+    out = torch.zeros_like(q, device=cuda)
+    fp8kv_prefill.prefill_attention(q.to(cuda), k.to(cuda), v.to(cuda), out, cu.to(cuda),
+                                    lens.to(cuda), bt.to(cuda), 1.0, 1.0, D ** -0.5, max_qlen=90)
+    assert torch.isfinite(out.float()).all()
+    _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 1.0, 1.0, D ** -0.5))
+
+
+def test_large_dynamic_range_rows(cuda):
+    """Query rows spanning 2^-20 .. 2^20 and a peaked softmax: the split
+    e4m3 terms of q and p keep the reference's bf16 precision."""
+    import fp8kv_prefill
+    lens_q, lens_kv = [256], [700]
+    q, k, v, bt, cu, lens = _paged_case(lens_q, lens_kv, PBLK, seed=5)
+    g = torch.Generator().manual_seed(6)
+    scale = torch.exp2(torch.randint(-20, 21, (q.shape[0], q.shape[1], 1), generator=g).float())
+    q = (q.float() * scale * 0.05).to(torch.bfloat16)
+    q[::7] = (q[::7].float() * 0 + torch.randn(q[::7].shape, generator=g) * 3).to(torch.bfloat16)
+    out = torch.zeros_like(q, device=cuda)
+    fp8kv_prefill.prefill_attention(q.to(cuda), k.to(cuda), v.to(cuda), out, cu.to(cuda),
+                                    lens.to(cuda), bt.to(cuda), 1.0, 1.0, D ** -0.5, max_qlen=256)
+    _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 1.0, 1.0, D ** -0.5))
