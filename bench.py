@@ -56,6 +56,8 @@ def workload_config(args):
                         f"qkv/o/gate_up/down at M={args.batch} + fp8 paged decode attention "
                         f"{args.batch} seq x {args.ctx} ctx, GQA 32/8, D 128, block 16]",
             "batch": args.batch, "ctx": args.ctx, "layers": args.layers,
+            "mxfp4_kernel": ("block-scaled tcgen05 (kind::mxf4), scales packed at load"
+                             if args.gemv == "tc" else "CUDA-core mma.sync"),
             "l2": "inputs larger than L2 (distinct weights/KV per layer), no flush",
             "parallelism": f"replicas x{args.gpus}"}
 
@@ -129,7 +131,13 @@ def build_model(args, dev):
         for name, N, K in SHAPES:
             W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
             St = torch.randint(119, 126, (N, K // 32), dtype=torch.uint8, device=dev, generator=g)
-            lay[name] = (W, St)
+            if args.gemv == "tc":  # load-time repack of the scales into tensor-core atoms
+                import h4mv
+                packed, edge = h4mv.pack_scales(St, N, K)
+                assert not edge
+                lay[name] = (W, packed)
+            else:
+                lay[name] = (W, St)
         nb = B * nblk
         kf = torch.randn(nb, PBLK, HKV, D, device=dev, generator=g)
         ks = kf.abs().max() / 448.0
@@ -158,23 +166,25 @@ def build_model(args, dev):
 
 
 def run_step(layers, bufs, args, which=("gemv", "attn")):
-    """One hot-path step through the public API (h4mv.mxfp4_gemv, fp8kv_v3.run)."""
+    """One hot-path step through the public API (h4mv.mxfp4_gemm or
+    h4mv.mxfp4_gemv, fp8kv_v3.run)."""
     import fp8kv_v3
     import h4mv
     B = args.batch
     sm = D ** -0.5
+    gemv = h4mv.mxfp4_gemm if args.gemv == "tc" else h4mv.mxfp4_gemv
     do_g, do_a = "gemv" in which, "attn" in which
     for lay in layers:
         if do_g:
-            h4mv.mxfp4_gemv(lay["x"], *lay["qkv"], out=bufs["qkv"])
+            gemv(lay["x"], *lay["qkv"], out=bufs["qkv"])
         if do_a:
             q = bufs["qkv"][:, :HQ * D].unflatten(1, (HQ, D))
             fp8kv_v3.run(q, lay["k"], lay["v"], bufs["attn"], bufs["qsl"], bufs["slens"], lay["bt"],
                          lay["ks"], lay["vs"], sm, max_seq_len=args.ctx)
         if do_g:
-            h4mv.mxfp4_gemv(bufs["attn"].view(B, HQ * D), *lay["o"], out=bufs["o"])
-            h4mv.mxfp4_gemv(bufs["o"], *lay["gate_up"], out=bufs["gate_up"])
-            h4mv.mxfp4_gemv(lay["act"], *lay["down"], out=bufs["down"])
+            gemv(bufs["attn"].view(B, HQ * D), *lay["o"], out=bufs["o"])
+            gemv(bufs["o"], *lay["gate_up"], out=bufs["gate_up"])
+            gemv(lay["act"], *lay["down"], out=bufs["down"])
 
 
 def capture(fn):
@@ -428,7 +438,7 @@ def run_b200(args):
             "tok_s_hot_path_only": world * args.batch / (ms * 1e-3),
             "parts": {
                 "mxfp4_gemv": {"us_per_step": ms_gemv * 1e3, "launches_per_step": n_gemv,
-                               "gbs": gemv_gbs},
+                               "gbs": gemv_gbs, "kernel": args.gemv},
                 "decode_attn": {"us_per_step": ms_attn * 1e3, "launches_per_step": args.layers,
                                 "gbs": attn_bytes_step / (ms_attn * 1e-3) / 1e9},
                 "prefill_attn": {"workload": "config 3: varlen causal prefill, 4 seqs "
@@ -440,7 +450,8 @@ def run_b200(args):
                                  / peaks.get("bf16_tflops", 1590.0),
                                  "note": "timed outside the decode step (not part of value)"},
             },
-            "roofline": {"bound": "hbm", "kernel": "mxfp4_gemv_kernel",
+            "roofline": {"bound": "hbm",
+                         "kernel": "mxfp4_mma_kernel" if args.gemv == "tc" else "mxfp4_gemv_kernel",
                          "achieved": gemv_gbs, "peak": hbm_peak, "unit": "GB/s",
                          "frac": gemv_gbs / hbm_peak, "peak_source": peak_src,
                          "bytes_per_launch_avg": gemv_bytes_step / n_gemv,
@@ -472,6 +483,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
+                    help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
     args.rank = int(os.environ.get("RANK", "0"))

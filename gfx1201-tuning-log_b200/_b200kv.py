@@ -68,6 +68,13 @@ lib.b200kv_prefill_attn.argtypes = (
      _i32, _i32,                      # num_blocks, kv_dtype
      _vp])
 
+lib.b200kv_mxfp4_packed_scales_bytes.restype = ctypes.c_size_t
+lib.b200kv_mxfp4_packed_scales_bytes.argtypes = [_i32, _i32]
+lib.b200kv_mxfp4_pack_scales.restype = _i32
+lib.b200kv_mxfp4_pack_scales.argtypes = [_vp, _i32, _vp, _i32, _i32, _vp, _vp]
+lib.b200kv_mxfp4_gemm.restype = _i32
+lib.b200kv_mxfp4_gemm.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]
+
 lib.b200kv_kv_write.restype = _i32
 lib.b200kv_kv_write.argtypes = ([_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp] + [_i64] * 6 +
                                 [_vp, _vp, _vp] + [_i32] * 5 + [_vp])

@@ -63,6 +63,12 @@ int kv_write_launch(const void* key, int64_t k_st, int64_t k_sh, const void* val
                     const float* k_scale, const float* v_scale, int num_tokens, int hkv,
                     int head_dim, int block_size, int kv_dtype, void* stream);
 
+size_t mxfp4_packed_scales_bytes(int N, int K);
+int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, int* edge_flag,
+                             void* stream);
+int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
+                     void* stream);
+
 int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                         const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
                         int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
@@ -161,6 +167,20 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
       out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
       v_scale, sm_scale, num_seqs, max_qlen, q0_single, qlen_single, num_q_heads, num_kv_heads,
       head_dim, block_size, num_blocks, kv_dtype, stream);
+}
+
+size_t b200kv_mxfp4_packed_scales_bytes(int N, int K) {
+  return b200kv::mxfp4_packed_scales_bytes(N, K);
+}
+
+int b200kv_mxfp4_pack_scales(const void* scales, int layout, void* packed, int N, int K,
+                             int* edge_flag, void* stream) {
+  return b200kv::mxfp4_pack_scales_launch(scales, layout, packed, N, K, edge_flag, stream);
+}
+
+int b200kv_mxfp4_gemm(const void* W, const void* packed_scales, const void* X, void* out, int N,
+                      int K, int M, void* stream) {
+  return b200kv::mxfp4_mma_launch(W, packed_scales, X, out, N, K, M, stream);
 }
 
 int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_head,

@@ -1,0 +1,551 @@
+// MXFP4 (e2m1 + e8m0) W4A16 matvec / skinny GEMM on block-scaled tcgen05 MMAs,
+// sm_100a, 1 <= M <= 8.
+//
+// Same product as mxfp4_gemv.cu (the reference kernel h4mv/h4mv.cu:43-104):
+//   out[m, n] = bf16_rn( sum_g 2^(S[n,g]-127) * sum_{j<32} e2m1(W[n,32g+j]) * x[m,32g+j] )
+// with fp32 accumulation, computed by tcgen05.mma.kind::mxf4.block_scale.block32:
+//  * A = a 128-row weight tile in packed e2m1 straight from memory: plain TMA
+//    boxes of 128 rows x 128 bytes (256 k) land in the tensor core's 128-byte-
+//    swizzled K-major layout unchanged (the checkpoint's low-nibble-first order
+//    is the tensor core's), and the MMA applies the e8m0 group scales itself.
+//    A stage issues 4 K-adjacent boxes back to back, so DRAM sees 512
+//    contiguous bytes per row per stage: measured on this part, that streams at
+//    6.3 TB/s where one 128-byte box per row and stage stays near 3.6 TB/s;
+//  * B = the activations written as four e2m1 terms with their own e8m0
+//    scales per 32-element block, x ~= t0 + t1 + t2 + t3, each term taking the
+//    top 2-3 bits of what the previous ones left (greedy, round to nearest).
+//    They sit in the N dimension (B row 8p + m = term p of activation row m),
+//    so one MMA computes all four products and the epilogue adds them.  About
+//    95 % of bf16 values come out exact; the worst case is 5e-4 of the block
+//    maximum (modelled on config-2 data, where it moves the result by 1.4e-4 of
+//    its maximum against the 5e-3 tolerance);
+//  * the weight scales come pre-packed (b200kv_mxfp4_pack_scales) in the
+//    tensor core's scale-factor atom: 512 bytes per (128 rows x 4 groups), byte
+//    16*(row % 32) + 4*(row / 32) + group, copied to tensor memory with
+//    tcgen05.cp 32x128b.warpx4 -- a load-time repack, like the reference's
+//    scale transpose (fp8kv_hipw4.py:32-43).
+// Packed 4-bit operands keep every TMA request at a full 128-byte row and every
+// in-flight weight byte at one byte of shared memory (an unpacked 8-bit-container
+// operand would halve both).  Work split: a thread-block cluster of ks CTAs
+// splits K; clusters take 128-row tiles round-robin; partial tiles are reduced
+// through distributed shared memory.  Warp 0 streams (W box, 2 scale atoms)
+// stages through an mbarrier ring, warp 1 issues the MMAs from one thread,
+// warps 2-5 turn x into its four terms at the start and drain the accumulators.
+//
+// Scale semantics are the MMA's (OCP MX: 2^(s-127)); the reference kernel
+// differs for the bytes 0 (it gives 0.0) and 255 (inf), so weights holding those
+// bytes stay on mxfp4_gemv.cu -- the packer reports them.
+
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "b200kv.h"
+#include "b200kv_common.cuh"
+#include "tcgen05.cuh"
+#include "tma.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace b200kv {
+namespace {
+
+constexpr int kTile = 128;             // weight rows per tile (MMA M)
+constexpr int kAtomK = 128;            // K covered by one scale atom (4 groups)
+constexpr int kStep = 256;             // K per W box (128 B rows): 2 atoms, 4 MMAs
+constexpr int kBoxesPerStage = 4;      // a stage reads 512 contiguous bytes of each row
+constexpr int kTerms = 4;              // e2m1 terms of x
+constexpr int kNmma = 32;              // B rows: term p of activation row m at 8p + m
+constexpr int kMaxM = 8;
+constexpr int kBox = kTile * 128;      // W box: 16 KB
+constexpr int kAtom = 512;
+constexpr int kStageBytes = kBoxesPerStage * (kBox + 2 * kAtom);  // 68 KB
+constexpr int kBStep = kNmma * 128;        // B rows of one W box: 4 KB
+constexpr int kMaxStages = 3;
+constexpr int kThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 x + epilogue
+constexpr uint32_t kTmemCols = 256;    // D[2][32] 0..63, SFA 64 + 32*(s&1), SFB 128 + 8*box
+constexpr int kMaxSliceBoxes = 16;     // SFB of a K-slice stays in tensor memory: 8 columns a box
+
+struct MmaArgs {
+  const uint8_t* Sp;         // packed scale atoms [ntiles][K/128][512]
+  const __nv_bfloat16* X;    // [M, K]
+  __nv_bfloat16* Out;        // [M, N]
+  int N, K, M;
+  int nsteps;                // W boxes along K: K / 256
+  int sps;                   // W boxes per K-slice
+  int ntiles, nclusters, tmax, nstages;
+};
+
+struct MmaLayout {
+  int sps, tmax, nstages;
+  __host__ __device__ size_t xb() const { return (size_t)nstages * kStageBytes; }
+  __host__ __device__ size_t sfb() const { return xb() + (size_t)sps * kBStep; }
+  __host__ __device__ size_t part() const { return sfb() + (size_t)sps * 2 * kAtom; }
+  __host__ __device__ size_t bytes(int m) const { return part() + (size_t)tmax * m * kTile * 4 + 1024; }
+};
+
+// instruction descriptor, kind::mxf4 block-scaled: A, B e2m1 (format 1 of this
+// kind), both K-major, e8m0 scales, scale-factor byte ids (0 or 2: two bytes per MMA)
+__host__ __device__ constexpr uint32_t idesc_mxf4(int M, int N, uint32_t sf_id) {
+  return (sf_id << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
+         ((uint32_t)(M >> 4) << 24) | (sf_id << 29);
+}
+
+// shared-memory descriptor of a 512-byte scale atom (32 rows x 16 B, no swizzle)
+__device__ __forceinline__ uint64_t sdesc_atom(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(16 >> 4) << 16;
+  d |= (uint64_t)(128 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
+__device__ __forceinline__ void tmem_cp_atom(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ void mma_mxf4(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t acc, uint32_t sfa, uint32_t sfb) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+// (a, b) -> one byte of two e2m1 codes, a in the low nibble
+__device__ __forceinline__ uint32_t e2m1x2(float a, float b) {
+  uint16_t r;
+  asm("{\n .reg .b8 t;\n cvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n cvt.u16.u8 %0, t;\n}" : "=h"(r) : "f"(a), "f"(b));
+  return (uint32_t)r;
+}
+// one byte of two e2m1 codes -> (low, high) values
+__device__ __forceinline__ float2 e2m1x2_val(uint32_t byte) {
+  uint32_t h;
+  asm("{\n .reg .b8 t;\n cvt.u8.u32 t, %1;\n cvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(h) : "r"(byte));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+template <int MAXM>
+__global__ void __launch_bounds__(kThreads, 1)
+    mxfp4_mma_kernel(const __grid_constant__ CUtensorMap wmap, const MmaArgs a) {
+  extern __shared__ uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages], d_full[2], d_free[2], x_ready;
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rank = blockIdx.x;  // K-slice
+  const int cid = blockIdx.y;
+  const int s_begin = rank * a.sps;
+  const int ns = max(0, min(a.nsteps, s_begin + a.sps) - s_begin);  // steps in this slice
+  const int my_tiles = cid < a.ntiles ? (a.ntiles - cid + a.nclusters - 1) / a.nclusters : 0;
+  const MmaLayout L{a.sps, a.tmax, a.nstages};
+  uint8_t* xb = dsm + L.xb();
+  uint8_t* sfb = dsm + L.sfb();
+  float* part = reinterpret_cast<float*>(dsm + L.part());  // [tmax][M][128]
+
+  if (tid == 0) {
+    for (int i = 0; i < a.nstages; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&d_full[b], 1);
+      mbar_init(&d_free[b], 4);
+    }
+    mbar_init(&x_ready, 4);
+    fence_mbar_init();
+  }
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, kTmemCols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tbase = tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- producer: (4 W boxes, 8 scale atoms) per stage ---------------
+    if (lane == 0 && ns > 0) {
+      tma_prefetch_desc(&wmap);
+      bool failed = false;
+      int s = 0;
+      const int atoms_per_tile = a.nsteps * 2;
+      const int spt = (ns + kBoxesPerStage - 1) / kBoxesPerStage;  // stages per tile
+      for (int i = 0; i < my_tiles && !failed; ++i) {
+        const int tile = cid + i * a.nclusters;
+        for (int t = 0; t < spt; ++t, ++s) {
+          const int slot = s % a.nstages;
+          if (s >= a.nstages && !mbar_wait_bounded(&empty_bar[slot], ((s / a.nstages) - 1) & 1)) {
+            failed = true;  // stop issuing; drain what is in flight
+            break;
+          }
+          uint8_t* st = dsm + (size_t)slot * kStageBytes;
+          const int b0 = t * kBoxesPerStage;
+          const int nb = min(kBoxesPerStage, ns - b0);
+          mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(nb * (kBox + 2 * kAtom)));
+          const int g = s_begin + b0;  // first W box (along K) of this stage
+          for (int q = 0; q < nb; ++q)  // adjacent K boxes back to back: 512 B per row
+            tma_load_2d(st + q * kBox, &wmap, (g + q) * (kStep / 2), tile * kTile, &full_bar[slot]);
+          bulk_g2s(st + kBoxesPerStage * kBox, a.Sp + ((size_t)tile * atoms_per_tile + 2 * g) * kAtom,
+                   (uint32_t)(nb * 2 * kAtom), &full_bar[slot]);
+        }
+      }
+      // drain: every copy issued has landed before the CTA may exit
+      for (int t = max(0, s - a.nstages); t < s; ++t)
+        mbar_wait_bounded(&full_bar[t % a.nstages], (t / a.nstages) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------------------------------------------
+    if (lane == 0 && ns > 0) {
+      bool failed = !mbar_wait_bounded(&x_ready, 0);
+      tc::fence_after_sync();
+      const uint32_t a_ring = smem_u32(dsm), a_xb = smem_u32(xb), a_sfb = smem_u32(sfb);
+      const int spt = (ns + kBoxesPerStage - 1) / kBoxesPerStage;
+      const uint32_t tsfb = tbase + 128;  // the activation scales: all boxes of the slice, once
+      for (int q = 0; q < 2 * ns; ++q) tmem_cp_atom(tsfb + 4 * q, sdesc_atom(a_sfb + (uint32_t)q * kAtom));
+      int s = 0;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !failed) failed = !mbar_wait_bounded(&d_free[b], ((i - 2) >> 1) & 1);
+        tc::fence_after_sync();
+        const uint32_t tD = tbase + 32 * b;
+        for (int t = 0; t < spt; ++t, ++s) {
+          const int slot = s % a.nstages;
+          if (failed || !mbar_wait_bounded(&full_bar[slot], (s / a.nstages) & 1)) {
+            failed = true;  // issue nothing more
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t tsfa = tbase + 64 + 32 * (s & 1);
+          const uint32_t st = a_ring + (uint32_t)slot * kStageBytes;
+          const int b0 = t * kBoxesPerStage;
+          const int nb = min(kBoxesPerStage, ns - b0);
+          for (int q = 0; q < 2 * nb; ++q)
+            tmem_cp_atom(tsfa + 4 * q, sdesc_atom(st + kBoxesPerStage * kBox + (uint32_t)q * kAtom));
+          for (int q = 0; q < nb; ++q) {
+            const uint32_t abox = st + (uint32_t)q * kBox;
+            const uint32_t bbox = a_xb + (uint32_t)(b0 + q) * kBStep;
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) {  // K = 64 each; scale bytes 2(kq&1).. of atom kq/2
+              const uint32_t sf = 2u * (uint32_t)(kq & 1);
+              mma_mxf4(tD, tc::sdesc_sw128(abox + kq * 32, 16, 1024),
+                       tc::sdesc_sw128(bbox + kq * 32, 16, 1024), idesc_mxf4(kTile, kNmma, sf),
+                       (t > 0 || q > 0 || kq > 0) ? 1u : 0u,
+                       (tsfa + 8 * q + 4 * (kq >> 1)) | (sf << 30),
+                       (tsfb + 8 * (b0 + q) + 4 * (kq >> 1)) | (sf << 30));
+            }
+          }
+          tc::commit(&empty_bar[slot]);
+        }
+        tc::commit(&d_full[b]);
+      }
+    }
+  } else {
+    // ---------------- warps 2-5: x -> 4 e2m1 terms + scale atoms; epilogue ----------
+    const int et = tid - 64;                      // 0..127
+    const int row = 32 * (warp & 3) + lane;       // TMEM lane of this thread
+    // zero the B rows (rows of absent activation rows stay zero); scales 2^0
+    for (int i = et; i < ns * kBStep / 16; i += 128)
+      reinterpret_cast<uint4*>(xb)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = et; i < ns * 2 * kAtom / 4; i += 128)
+      reinterpret_cast<uint32_t*>(sfb)[i] = 0x7F7F7F7Fu;
+    named_bar_sync(1, 128);
+    // one 32-element block of one activation row per work item
+    const int nblk = ns * 8;
+    for (int w = et; w < a.M * nblk; w += 128) {
+      const int m = w / nblk, blk = w % nblk;
+      const int j = blk >> 3, kb8 = blk & 7;
+      const __nv_bfloat16* xr = a.X + (size_t)m * a.K + (size_t)(s_begin * kStep + blk * 32);
+      float r[32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 r4 = __ldg(reinterpret_cast<const uint4*>(xr) + q);
+        const uint32_t u[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          r[8 * q + 2 * e] = __uint_as_float(u[e] << 16);
+          r[8 * q + 2 * e + 1] = __uint_as_float(u[e] & 0xFFFF0000u);
+        }
+      }
+      uint8_t* bj = xb + (size_t)j * kBStep;
+#pragma unroll 1
+      for (int t = 0; t < kTerms; ++t) {
+        float mx = 0.f;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fabsf(r[e]));
+        const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+        // term scale 2^(E-129): the block max maps into [4, 8) (6 is e2m1's top)
+        const int sb = (mx == 0.f || E == 0xFF) ? 127 : max(E - 2, 1);
+        const float inv = __uint_as_float((uint32_t)(254 - sb) << 23);  // 2^-(sb-127)
+        const float scl = __uint_as_float((uint32_t)sb << 23);          // 2^(sb-127)
+        uint32_t w4[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k = 8 * q + 2 * e;
+            const uint32_t code = e2m1x2(r[k] * inv, r[k + 1] * inv);
+            const float2 v = e2m1x2_val(code);
+            r[k] = fmaf(-v.x, scl, r[k]);
+            r[k + 1] = fmaf(-v.y, scl, r[k + 1]);
+            word |= code << (8 * e);
+          }
+          w4[q] = word;
+        }
+        const int n = 8 * t + m;  // B row
+        *reinterpret_cast<uint4*>(bj + n * 128 + ((kb8 ^ (n & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        sfb[(size_t)(2 * j + (kb8 >> 2)) * kAtom + 16 * n + (kb8 & 3)] = (uint8_t)sb;
+      }
+    }
+    tc::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&x_ready);
+
+    // per tile: sum the four term columns of each activation row -> partial
+    bool failed = false;
+    for (int i = 0; i < my_tiles && ns > 0; ++i) {
+      const int b = i & 1;
+      if (!failed) failed = !mbar_wait_bounded(&d_full[b], (i >> 1) & 1);
+      tc::fence_after_sync();
+      float d[32];
+      tc::ld32_wait(tbase + 32 * b + ((uint32_t)(32 * (warp & 3)) << 16), d);
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&d_free[b]);
+      float* pr = part + (size_t)i * a.M * kTile + row;
+#pragma unroll
+      for (int m = 0; m < kMaxM; ++m)
+        if (m < a.M) pr[m * kTile] = (d[m] + d[8 + m]) + (d[16 + m] + d[24 + m]);
+    }
+    if (ns == 0)
+      for (int i = 0; i < my_tiles; ++i)
+        for (int m = 0; m < a.M; ++m) part[((size_t)i * a.M + m) * kTile + row] = 0.f;
+  }
+
+  // ---- reduce the cluster's K-slices through distributed shared memory -----------
+  tc::fence_before_sync();
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  const int ksz = (int)cluster.num_blocks();
+  for (int i = rank; i < my_tiles; i += ksz) {
+    const int row0 = (cid + i * a.nclusters) * kTile;
+    for (int e = tid; e < kTile * a.M; e += kThreads) {
+      const int m = e / kTile, r = e % kTile;
+      float v = 0.f;
+      for (int q = 0; q < ksz; ++q) v += cluster.map_shared_rank(part, q)[((size_t)i * a.M + m) * kTile + r];
+      const int n = row0 + r;
+      if (n < a.N) a.Out[(size_t)m * a.N + n] = __float2bfloat16_rn(v);
+    }
+  }
+  cluster.sync();
+  if (warp == 0) tc::tmem_dealloc(tbase, kTmemCols);
+}
+
+// Scale packer: S (layout 0: [N, K/32] transposed, 1: [K/32, N] checkpoint) ->
+// atoms [ntiles][nsteps][512]; rows past N and groups past K/32 get 127 (2^0).
+// *edge is set to 1 when any byte is 0 or 255.
+__global__ void pack_scales_kernel(const uint8_t* __restrict__ S, int layout, uint8_t* __restrict__ Sp,
+                                   int N, int K, int ntiles, int nsteps, int* edge) {
+  const int ngroups = K >> 5;
+  const size_t total = (size_t)ntiles * nsteps * kAtom;
+  bool e = false;
+  for (size_t o = (size_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
+    const int byte = (int)(o % kAtom);
+    const size_t ts = o / kAtom;
+    const int step = (int)(ts % nsteps), tile = (int)(ts / nsteps);
+    const int dp = byte >> 4, jj = (byte >> 2) & 3, kb = byte & 3;
+    const int n = tile * kTile + dp + 32 * jj;
+    const int g = step * 4 + kb;
+    uint8_t v = 127;
+    if (n < N && g < ngroups) {
+      v = layout == 0 ? S[(size_t)n * ngroups + g] : S[(size_t)g * N + n];
+      e |= (v == 0 || v == 255);
+    }
+    Sp[o] = v;
+  }
+  if (e) atomicExch(edge, 1);
+}
+
+// The kernel's dynamic shared-memory limit, raised on demand (per process; the
+// attribute is per function, the same value on every device).
+cudaError_t raise_smem_limit(size_t smem) {
+  static std::mutex mu;
+  static size_t limit = 0;
+  std::lock_guard<std::mutex> g(mu);
+  if (smem <= limit) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(mxfp4_mma_kernel<kMaxM>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) limit = smem;
+  return e;
+}
+
+template <int MAXM>
+cudaError_t launch_mma(const CUtensorMap& wm, const MmaArgs& a, int ks, cudaStream_t st) {
+  const MmaLayout L{a.sps, a.tmax, a.nstages};
+  const size_t smem = L.bytes(a.M);
+  const cudaError_t e = raise_smem_limit(smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ks, a.nclusters, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = ks;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mxfp4_mma_kernel<MAXM>, wm, a);
+}
+
+int max_active_clusters(int ks, size_t smem);
+
+int env_or(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
+}
+
+// Clusters of ks CTAs with `smem` bytes each that the device can hold at once
+// (cached per device, size and smem).
+int max_active_clusters(int ks, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, ks, smem);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  if (raise_smem_limit(smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ks, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = ks;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, mxfp4_mma_kernel<kMaxM>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n;
+  return n;
+}
+
+}  // namespace
+
+size_t mxfp4_packed_scales_bytes(int N, int K) {
+  if (N <= 0 || K <= 0 || K % kAtomK) return 0;
+  return (size_t)cdiv(N, kTile) * (K / kAtomK) * kAtom;
+}
+
+int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, int* edge_flag,
+                             void* stream) {
+  if (!S || !Sp || !edge_flag || N <= 0 || K <= 0) return B200KV_ERR_INVALID_ARG;
+  if (K % kAtomK) return B200KV_ERR_UNSUPPORTED;
+  if (layout != 0 && layout != 1) return B200KV_ERR_INVALID_ARG;
+  if (sm_major_current_device() < 10) return B200KV_ERR_NO_DEVICE;
+  const int ntiles = cdiv(N, kTile), nsteps = K / kAtomK;
+  const size_t total = (size_t)ntiles * nsteps * kAtom;
+  const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  pack_scales_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(S), layout, static_cast<uint8_t*>(Sp), N, K, ntiles, nsteps, edge_flag);
+  return cudaGetLastError() == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;
+}
+
+int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
+                     void* stream) {
+  if (!W || !Sp || !X || !Out) return B200KV_ERR_INVALID_ARG;
+  if (N <= 0 || K <= 0 || M <= 0) return B200KV_ERR_INVALID_ARG;
+  if (M > kMaxM || K % kStep) return B200KV_ERR_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(Sp) & 15) ||
+      (reinterpret_cast<uintptr_t>(X) & 15))
+    return B200KV_ERR_MISALIGNED;
+  const int sms = num_sms_current_device();
+  if (sms <= 0 || sm_major_current_device() < 10) return B200KV_ERR_NO_DEVICE;
+
+  MmaArgs a;
+  a.Sp = static_cast<const uint8_t*>(Sp);
+  a.X = static_cast<const __nv_bfloat16*>(X);
+  a.Out = static_cast<__nv_bfloat16*>(Out);
+  a.N = N;
+  a.K = K;
+  a.M = M;
+  a.nsteps = K / kStep;
+  a.ntiles = cdiv(N, kTile);
+  // K-split ks (cluster size), ring depth and cluster count.  The clusters are
+  // persistent: no more than can be resident at once (a cluster's CTAs must
+  // share a GPC, so fewer clusters than SMs / ks fit when a CTA fills an SM),
+  // and the plan minimises the per-cluster work, tiles x steps per slice.
+  const int force_ks = env_or("B200KV_MMA_KSPLIT", 0);
+  const int force_st = env_or("B200KV_MMA_STAGES", 0);
+  int best_ks = 1, best_st = 4, best_nc = 1;
+  double best_cost = 1e30;
+  for (int ks = 1; ks <= 8; ++ks) {
+    if (force_ks && ks != force_ks) continue;
+    if (ks > a.nsteps) break;
+    const int sps = cdiv(a.nsteps, ks);
+    for (int nst : {2, 3}) {
+      if (force_st && nst != force_st) continue;
+      const int nc0 = max(1, min(a.ntiles, sms / ks));
+      const int tslots = cdiv(a.ntiles, nc0) + 1;
+      if (sps > kMaxSliceBoxes) continue;
+      const size_t smem = MmaLayout{sps, tslots, nst}.bytes(M);
+      if (smem > 227 * 1024) continue;
+      const int nc = min(a.ntiles, min(nc0, max_active_clusters(ks, smem)));
+      if (nc <= 0) continue;
+      const int waves = cdiv(a.ntiles, nc);
+      if (waves > tslots) continue;
+      // per-cluster work, plus a small price per CTA sharing an SM and per rank
+      const int ctas = nc * ks;
+      const double share = ctas > sms ? (double)ctas / sms : 1.0;
+      const double cost = waves * sps * share + 0.25 * ks;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best_ks = ks;
+        best_st = nst;
+        best_nc = nc;
+      }
+    }
+  }
+  if (best_cost >= 1e30) return B200KV_ERR_UNSUPPORTED;
+  const int ks = best_ks;
+  a.nclusters = best_nc;
+  a.sps = cdiv(a.nsteps, ks);
+  a.tmax = cdiv(a.ntiles, a.nclusters);
+  a.nstages = best_st;
+  if (env_or("B200KV_MMA_PLAN", 0))
+    fprintf(stderr, "[b200kv] mxfp4_gemm N=%d K=%d M=%d: ks=%d clusters=%d stages=%d tiles/cluster=%d steps/slice=%d\n",
+            N, K, M, ks, a.nclusters, a.nstages, a.tmax, a.sps);
+
+  CUtensorMap wm;
+  if (!encode_u8_2d(&wm, W, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), 128, kTile, true))
+    return B200KV_ERR_UNSUPPORTED;
+  const cudaError_t e = launch_mma<kMaxM>(wm, a, ks, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;
+}
+
+}  // namespace b200kv

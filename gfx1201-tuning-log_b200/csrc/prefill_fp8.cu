@@ -237,9 +237,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pblk = 1 << p.pblk_shift;
       const int ppt = kBN >> p.pblk_shift;  // pages per tile
       bool failed = false;
+      int issued = nmax;
       for (int j = 0; j < nmax; ++j) {
         const int st = j % kStages;
-        if (j >= kStages && !failed) failed = !mbar_wait_bounded(&kv_empty[st], ((j / kStages) - 1) & 1);
+        if (j >= kStages && !mbar_wait_bounded(&kv_empty[st], ((j / kStages) - 1) & 1)) {
+          failed = true;  // stop issuing; drain what is in flight
+          issued = j;
+          break;
+        }
         const int keys = min(kBN, kv_hi - j * kBN);
         const int npages = (keys + pblk - 1) >> p.pblk_shift;
         mbar_arrive_expect_tx(&kv_full[st], (uint32_t)(npages * pblk * 128 * 2));
@@ -252,8 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // drain: every load issued has landed before the CTA may exit
-      for (int j = max(0, nmax - kStages); j < nmax; ++j)
-        if (!failed) failed = !mbar_wait_bounded(&kv_full[j % kStages], (j / kStages) & 1);
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        mbar_wait_bounded(&kv_full[j % kStages], (j / kStages) & 1);
     }
   } else if (warp == kSoftWarps + 1) {
     // ---------------- MMA issuer ------------------------------------------------
@@ -269,6 +274,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto qk = [&](int X, int j) {  // S_X = Q_X K(j)^T
         const int st = j % kStages;
         if (!failed) failed = !mbar_wait_bounded(&kv_full[st], (j / kStages) & 1);
+        if (failed) {  // issue nothing more; commit so the softmax warps do not wait
+          tc::commit(&s_full[X]);
+          return;
+        }
         tc::fence_after_sync();
 #pragma unroll
         for (int part = 0; part < 2; ++part)
@@ -283,6 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto pv = [&](int X, int j) {  // O_X += P_X V(j)
         const int st = j % kStages;
         if (!failed) failed = !mbar_wait_bounded(&p_full[X], j & 1);
+        if (failed) {
+          tc::commit(&pv_done[X]);
+          return;
+        }
         tc::fence_after_sync();
 #pragma unroll
         for (int part = 0; part < 2; ++part)

@@ -7,9 +7,11 @@ With FP8KV_HIPW4=1 the CUDA implementation of the op radiance::mxfp4_linear
 
   * gate (fp8kv_hipw4.py:70-76): x 2-D, contiguous, bf16, 1 <= M <= MAX_M;
     K % 32 == 0; N >= 8; weight_scale rows == K/32; weight 16-byte aligned;
-  * the checkpoint's scale layout [K/32, N] is repacked once to [N, K/32] and
-    cached by (data_ptr, shape), never while a CUDA graph is being captured
-    (fp8kv_hipw4.py:32-43);
+  * the checkpoint's scale layout [K/32, N] is repacked once and cached by
+    (data_ptr, shape), never while a CUDA graph is being captured
+    (fp8kv_hipw4.py:32-43): into tensor-core scale atoms for the block-scaled
+    tcgen05 kernel (h4mv.mxfp4_gemm) when K % 256 == 0 and no scale byte is
+    0 or 255, else into [N, K/32] for the CUDA-core kernel (h4mv.mxfp4_gemv);
   * out = torch.empty(M, N, bf16) and one launch on the current stream;
   * everything else goes to the op's original CUDA body.
 
@@ -48,7 +50,7 @@ def scale_t_for(s):
     None while capturing a CUDA graph (no allocations or side launches then).
     The cache entry holds the source tensor too, so its address cannot be
     freed and handed to another tensor while the entry exists."""
-    key = (s.data_ptr(), tuple(s.shape), s.device)
+    key = ("t", s.data_ptr(), tuple(s.shape), s.device)
     ent = _repack_cache.get(key)
     if ent is not None:
         return ent[1]
@@ -59,6 +61,27 @@ def scale_t_for(s):
         _repack_cache.clear()
     _repack_cache[key] = (s, st)
     return st
+
+
+def packed_scales_for(s, N, K):
+    """weight_scale [K/32, N] -> the tensor-core scale atoms (h4mv.pack_scales),
+    cached like scale_t_for; False when the weight cannot take the
+    tensor-core path (K % 256, or scale bytes 0 / 255), None during capture."""
+    import h4mv
+    key = ("p", s.data_ptr(), tuple(s.shape), s.device)
+    ent = _repack_cache.get(key)
+    if ent is not None:
+        return ent[1]
+    if _capturing(s):
+        return None
+    packed = False
+    if K % 256 == 0:
+        p, edge = h4mv.pack_scales(s.contiguous(), N, K, h4mv.SCALES_CHECKPOINT)
+        packed = False if edge else p
+    if len(_repack_cache) > 512:
+        _repack_cache.clear()
+    _repack_cache[key] = (s, packed)
+    return packed
 
 
 def eligible(x, weight, weight_scale, m_limit):
@@ -128,9 +151,14 @@ def make_patched(body, m_limit):
                                  f" s={tuple(weight_scale.shape)}"
                                  f" cap={_capturing(x)}\n")
             if eligible(x, weight, weight_scale, m_limit):
-                st = scale_t_for(weight_scale)
-                if st is not None:
-                    out = h4mv.mxfp4_gemv(x, weight, st)
+                N, K = weight.shape[0], weight.shape[1] * 2
+                packed = packed_scales_for(weight_scale, N, K) if weight.data_ptr() % 16 == 0 else False
+                if packed is not None and packed is not False:
+                    out = h4mv.mxfp4_gemm(x, weight, packed)
+                else:
+                    st = scale_t_for(weight_scale) if packed is False else None
+                    out = h4mv.mxfp4_gemv(x, weight, st) if st is not None else None
+                if out is not None:
                     _state["fast"] += 1
                     if not _state["logged"]:
                         _state["logged"] = True

@@ -43,3 +43,51 @@ def mxfp4_gemv(x, weight, scale_t, out=None):
                                 torch.cuda.current_stream(x.device).cuda_stream),
           "b200kv_mxfp4_gemv")
     return out
+
+
+# ---- block-scaled tensor-core path (load-time packed scales) -------------------
+SCALES_TRANSPOSED = 0   # St [N, K/32]
+SCALES_CHECKPOINT = 1   # S [K/32, N]
+
+
+def pack_scales(scales, N, K, layout=SCALES_TRANSPOSED):
+    """Pack e8m0 scales into the tensor core's scale-factor atoms (once per
+    weight).  Returns (packed uint8 tensor, has_edge) where has_edge reports
+    scale bytes 0 or 255, which the tensor-core MMA reads as 2^-127 / NaN but
+    the reference kernel as 0.0 / inf (keep such weights on mxfp4_gemv).
+    Synchronises once to read the flag: call at load time, not per step."""
+    nbytes = lib.b200kv_mxfp4_packed_scales_bytes(N, K)
+    if nbytes == 0:
+        raise ValueError(f"tensor-core path needs K % 128 == 0 (K={K})")
+    if scales.dtype != torch.uint8 or not scales.is_contiguous():
+        raise TypeError("scales must be a contiguous uint8 tensor")
+    want = (N, K // 32) if layout == SCALES_TRANSPOSED else (K // 32, N)
+    if tuple(scales.shape) != want:
+        raise ValueError(f"scales shape {tuple(scales.shape)} != {want}")
+    dev = scales.device
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    edge = torch.zeros(1, dtype=torch.int32, device=dev)
+    check(lib.b200kv_mxfp4_pack_scales(scales.data_ptr(), layout, packed.data_ptr(), N, K,
+                                       edge.data_ptr(), torch.cuda.current_stream(dev).cuda_stream),
+          "b200kv_mxfp4_pack_scales")
+    return packed, bool(edge.item())
+
+
+def mxfp4_gemm(x, weight, packed_scales, out=None):
+    """out[M, N] = x[M, K] @ dequant(weight, scales)^T on block-scaled tcgen05
+    MMAs, 1 <= M <= 8, K % 256 == 0, with scales packed by pack_scales()."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous 2-D bfloat16 tensor")
+    if weight.dtype != torch.uint8 or not weight.is_contiguous():
+        raise TypeError("weight must be a contiguous uint8 tensor")
+    M, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] * 2 != K:
+        raise ValueError(f"shape mismatch x={tuple(x.shape)} w={tuple(weight.shape)}")
+    if out is None:
+        out = torch.empty((M, N), device=x.device, dtype=torch.bfloat16)
+    check(lib.b200kv_mxfp4_gemm(weight.data_ptr(), packed_scales.data_ptr(), x.data_ptr(),
+                                out.data_ptr(), N, K, M,
+                                torch.cuda.current_stream(x.device).cuda_stream),
+          "b200kv_mxfp4_gemm")
+    return out

@@ -129,6 +129,32 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
                        int block_size, int max_blocks_per_seq, int max_seq_len_hint,
                        int kv_dtype, int out_by_qsl, int num_splits, void* stream);
 
+/* ---- MXFP4 on block-scaled tensor cores (load-time packed scales) -------------
+ *
+ * The same product as b200kv_mxfp4_gemv, computed by tcgen05
+ * kind::mxf4.block_scale MMAs: the packed e2m1 weights go to the tensor core
+ * straight from memory and the MMA applies the e8m0 scales itself.  The scales
+ * must first be packed once per weight (a load-time repack, as the reference
+ * transposes its scales once, h4mv/fp8kv_hipw4.py:32-43) into 512-byte atoms,
+ * one per (128 rows x 4 groups).  No counterpart call in the reference.
+ *
+ *   b200kv_mxfp4_packed_scales_bytes  size of the packed buffer (0 if K % 128).
+ *   b200kv_mxfp4_pack_scales  scales: layout 0 = St [N, K/32] (transposed, as
+ *       b200kv_mxfp4_gemv takes them), 1 = S [K/32, N] (checkpoint layout).
+ *       *edge_flag (device int, set to 1, never cleared) reports scale bytes 0
+ *       or 255, whose meaning differs between the MMA (2^-127, NaN) and the
+ *       reference kernel (0.0, inf): such weights belong on b200kv_mxfp4_gemv.
+ *   b200kv_mxfp4_gemm  out[M, N] bf16 for 1 <= M <= 8, K % 256 == 0, W 16-byte
+ *       aligned.  x enters as four e2m1 terms with per-32 block scales (about
+ *       95 % of bf16 values exact, the rest within 5e-4 of their block
+ *       maximum); fp32 accumulation.
+ */
+size_t b200kv_mxfp4_packed_scales_bytes(int N, int K);
+int b200kv_mxfp4_pack_scales(const void* scales, int layout, void* packed, int N, int K,
+                             int* edge_flag, void* stream);
+int b200kv_mxfp4_gemm(const void* W, const void* packed_scales, const void* X, void* out, int N,
+                      int K, int M, void* stream);
+
 /* ---- fp8 paged-KV causal prefill attention -----------------------------------
  *
  * For every sequence s with query rows cu_seqlens_q[s] .. cu_seqlens_q[s+1]-1

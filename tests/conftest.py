@@ -43,3 +43,26 @@ def cuda(libpath):
     major, _ = torch.cuda.get_device_capability()
     assert major >= 10, "GPU tests need an sm_100 device"
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """Every GPU test must leave the library's device status word at 0: a
+    kernel whose bounded wait ran out records a status there instead of
+    hanging, and its outputs may still look right."""
+    if request.node.get_closest_marker("gpu") is None:
+        yield
+        return
+    import torch
+    if not torch.cuda.is_available():
+        yield
+        return
+    _ensure_library()
+    import _b200kv
+    torch.cuda.synchronize()
+    _b200kv.reset_device_status()
+    yield
+    torch.cuda.synchronize()
+    st = _b200kv.device_status()
+    _b200kv.reset_device_status()
+    assert st == 0, f"a kernel reported device status {st:#x} (a bounded wait ran out)"

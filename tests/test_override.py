@@ -223,9 +223,12 @@ def test_hipw4_gate_and_repack(libpath):
 
 
 def test_hipw4_patched_routes(libpath, monkeypatch):
+    """Weights whose scales cannot take the tensor-core path (packed_scales_for
+    gives False) run the CUDA-core kernel with the transposed scales."""
     import fp8kv_hipw4 as hw
     import h4mv
     seen = {"fast": [], "body": 0}
+    monkeypatch.setattr(hw, "packed_scales_for", lambda s, N, K: False)
     monkeypatch.setattr(h4mv, "mxfp4_gemv", lambda x, w, st: seen["fast"].append((x.shape, st.shape)) or "fast")
 
     def body(x, w, s, wref):
@@ -244,6 +247,21 @@ def test_hipw4_patched_routes(libpath, monkeypatch):
     monkeypatch.setattr(h4mv, "mxfp4_gemv", boom)
     assert f(torch.zeros((1, K), dtype=torch.bfloat16), w, s, None) == "body"
     assert seen["body"] == 2
+
+
+def test_hipw4_prefers_tensor_core_path(libpath, monkeypatch):
+    import fp8kv_hipw4 as hw
+    import h4mv
+    seen = []
+    packed = torch.zeros(4, dtype=torch.uint8)
+    monkeypatch.setattr(hw, "packed_scales_for", lambda s, N, K: packed)
+    monkeypatch.setattr(h4mv, "mxfp4_gemm", lambda x, w, p: seen.append(p is packed) or "tc")
+    monkeypatch.setattr(h4mv, "mxfp4_gemv", lambda *a, **k: "cuda-core")
+    f = hw.make_patched(lambda *a: "body", 4)
+    N, K = 32, 256
+    out = f(torch.zeros((2, K), dtype=torch.bfloat16), torch.zeros((N, K // 2), dtype=torch.uint8),
+            torch.zeros((K // 32, N), dtype=torch.uint8), None)
+    assert out == "tc" and seen == [True]
 
 
 def test_hipw4_chunked_body_covers_any_m(libpath, monkeypatch):
