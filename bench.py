@@ -85,6 +85,10 @@ class ClockSampler:
             self.thread.start()
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()  # the timed region starts once the sampler answers
+        while not self.lines and self.proc.poll() is None and time.time() - t0 < 10:
+            time.sleep(0.02)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -328,7 +332,8 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "vs_baseline": None,
+            "dtype": "e2m1/e4m3 operands, f32 accumulate", "data": "synthetic",
             "config": workload_config(args),
             "cpu_baseline": {"value": val, "unit": "GB/s", "cores": torch.get_num_threads(),
                              "kind": "port",
@@ -426,6 +431,15 @@ def run_b200(args):
     gemv_gbs = gemv_bytes_step / (ms_gemv * 1e-3) / 1e9
     n_gemv = args.layers * 4
 
+    # DRAM bytes per launch of the dominant kernel from one ncu capture
+    # (dram__bytes_read.sum + dram__bytes_write.sum, cold cache) of the four
+    # 7B shapes at M = 1: 13.43, 8.97, 62.72 and 31.27 MB for qkv, o,
+    # gate_up and down.  Other configurations have no capture.
+    traffic, traffic_src = None, None
+    if args.gemv == "tc" and args.batch == 1:
+        traffic = (13.43 + 8.97 + 62.72 + 31.27) / 4 * 1e6
+        traffic_src = "ncu dram__bytes_read+write of the four shapes at M=1, averaged"
+
     result = None
     if rank == 0:
         cpu = cpu_baseline(args) if world == 1 else None
@@ -433,7 +447,8 @@ def run_b200(args):
         result = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e2m1/e4m3 operands, f32 accumulate",
             "data": "synthetic", "config": workload_config(args),
             "tok_s_hot_path_only": world * args.batch / (ms * 1e-3),
             "parts": {
@@ -456,12 +471,14 @@ def run_b200(args):
                          "frac": gemv_gbs / hbm_peak, "peak_source": peak_src,
                          "bytes_per_launch_avg": gemv_bytes_step / n_gemv,
                          "us_per_launch_avg": ms_gemv * 1e3 / n_gemv,
-                         "traffic": None},
+                         "traffic": traffic,
+                         "traffic_source": traffic_src},
             "cpu_baseline": cpu,
             "e2e": {"value": world * step_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "pinned host activations -> H2D, graph of public-API calls "
-                            "(h4mv.mxfp4_gemv, fp8kv_v3.run), D2H of outputs"},
+                            f"(h4mv.{'mxfp4_gemm' if args.gemv == 'tc' else 'mxfp4_gemv'}, "
+                            "fp8kv_v3.run), D2H of outputs"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
@@ -477,7 +494,9 @@ def run_b200(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default 300 graph replays, ~0.6 s of clocks samples; "
+                         "10 one-layer host samples for --impl reference)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--ctx", type=int, default=4096)
@@ -486,6 +505,8 @@ def main():
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
                     help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 300 if args.impl == "b200" else 10
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
     args.rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
