@@ -52,7 +52,8 @@ lib.b200kv_decode_attn.argtypes = (
      _vp, _i64, _i64,                 # out, strides
      _vp, _vp, _vp, _i64,             # qsl, seq_lens, block_table, bt stride
      _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
-     _i32, _i32, _i32, _i32, _i32, _i32, _i32,  # num_seqs .. max_seq_len_hint
+     _i32, _i32, _i32, _i32,          # num_seqs, hq, hkv, head_dim
+     _i32, _i32, _i32, _i32,          # block_size, num_blocks, max_blocks, max_seq_len_hint
      _i32, _i32, _i32,                # kv_dtype, out_by_qsl, num_splits
      _vp])                            # stream
 

@@ -60,6 +60,7 @@ def decode_attention(q, k_cache, v_cache, out, qsl, seq_lens, block_table,
         qsl.data_ptr(), seq_lens.data_ptr(), block_table.data_ptr(), block_table.stride(0),
         ks.data_ptr(), vs.data_ptr(), float(sm_scale),
         block_table.shape[0], q.shape[1], k_cache.shape[2], q.shape[2], k_cache.shape[1],
+        min(k_cache.shape[0], v_cache.shape[0]),
         block_table.shape[1], int(max_seq_len_hint),
         kv_dtype, 1 if out_by_qsl else 0, int(num_splits), stream), "b200kv_decode_attn")
     return out

@@ -19,6 +19,7 @@ extern __device__ int g_device_status;
 // ---- host helpers ------------------------------------------------------------
 int num_sms_current_device();     // cached per device; 0 when no device
 int sm_major_current_device();
+bool pdl_enabled();               // B200KV_PDL=0 turns programmatic launches off
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline int cdiv(int a, int b) { return (a + b - 1) / b; }
@@ -94,6 +95,22 @@ __device__ __forceinline__ void cp_async_commit() {
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---- programmatic dependent launch ---------------------------------------------
+// A kernel launched with programmatic stream serialization may start while the
+// kernel before it in the stream still runs (once every CTA of that kernel has
+// called griddep_launch_dependents or exited).  Whatever it reads that the
+// previous kernel may write, and everything it writes, comes after
+// griddep_wait(), which returns once the previous grid has completed and its
+// memory is visible.  Every CTA of every kernel here passes griddep_wait()
+// before it exits, so a grid's completion implies its predecessors'.  Both are
+// no-ops for a plain launch.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 }  // namespace b200kv

@@ -1,6 +1,7 @@
 // Exported C ABI of libb200kv.so (declared in include/b200kv.h).
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "b200kv.h"
 #include "b200kv_common.cuh"
@@ -46,6 +47,14 @@ int sm_major_current_device() {
   return d < 0 ? 0 : g_major[d];
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("B200KV_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 int mxfp4_gemv_launch(const void* W, const void* St, const void* X, void* out, int N, int K,
                       int M, void* stream);
 int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
@@ -54,8 +63,8 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        const int32_t* qsl, const int32_t* seq_lens, const int32_t* bt,
                        int64_t bt_stride, const float* k_scale, const float* v_scale,
                        float sm_scale, int num_seqs, int hq, int hkv, int head_dim,
-                       int block_size, int max_blocks, int hint, int kv_dtype, int out_by_qsl,
-                       int num_splits, void* stream);
+                       int block_size, int num_blocks, int max_blocks, int hint, int kv_dtype,
+                       int out_by_qsl, int num_splits, void* stream);
 
 int kv_write_launch(const void* key, int64_t k_st, int64_t k_sh, const void* value, int64_t v_st,
                     int64_t v_sh, void* k_cache, void* v_cache, int64_t sk0, int64_t sk1,
@@ -143,13 +152,13 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
                        const int32_t* seq_lens, const int32_t* block_table, int64_t bt_stride,
                        const float* k_scale, const float* v_scale, float sm_scale, int num_seqs,
                        int num_q_heads, int num_kv_heads, int head_dim, int block_size,
-                       int max_blocks_per_seq, int max_seq_len_hint, int kv_dtype, int out_by_qsl,
-                       int num_splits, void* stream) {
+                       int num_blocks, int max_blocks_per_seq, int max_seq_len_hint, int kv_dtype,
+                       int out_by_qsl, int num_splits, void* stream) {
   return b200kv::decode_attn_launch(
       q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
       out_stride_tok, out_stride_head, qsl, seq_lens, block_table, bt_stride, k_scale, v_scale,
-      sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, max_blocks_per_seq,
-      max_seq_len_hint, kv_dtype, out_by_qsl, num_splits, stream);
+      sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+      max_blocks_per_seq, max_seq_len_hint, kv_dtype, out_by_qsl, num_splits, stream);
 }
 
 int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,

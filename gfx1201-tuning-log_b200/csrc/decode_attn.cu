@@ -43,6 +43,7 @@
 
 #include "b200kv.h"
 #include "b200kv_common.cuh"
+#include "warp_mma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -75,41 +76,6 @@ struct DecodeParams {
 
 namespace {
 
-// ---- small PTX helpers -----------------------------------------------------
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
-  uint32_t r;
-  asm("{\n .reg .b16 t;\n cvt.u16.u32 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}" : "=r"(r) : "r"(two_bytes));
-  return r;
-}
-__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-template <bool F16>
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  if constexpr (F16) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  } else {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  }
-}
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(smem_u32(p)));
-}
-
 // Shared-memory layout of one CTA.  K rows are padded so the 8 tokens x 4
 // lanes of a B-fragment load hit distinct banks; V rows that ldmatrix reads are
 // padded to 272 bytes so its 8 row addresses hit distinct 16-byte groups.
@@ -125,10 +91,11 @@ struct Layout {
 
 template <int GQA>
 struct DecodeShared {
-  float wm[kWarps][8], wl[kWarps][8];     // per-warp softmax state at the end
-  float part_o[GQA][kHeadDim];            // this CTA's unnormalised o (read by peers)
-  float part_m[8], part_l[8];             // this CTA's max / sum (read by peers)
-  float comb_m[8], comb_l[8];
+  alignas(16) float part_o[GQA][kHeadDim];  // this CTA's unnormalised o (read by peers)
+  float wm[kWarps][8], wl[kWarps][8];       // per-warp softmax state at the end
+  float part_m[8], part_l[8];               // this CTA's max / sum (read by peers)
+  float rm[kMaxCluster][8], rl[kMaxCluster][8];  // every rank's (m, l)
+  float rw[kMaxCluster][8];                 // every rank's weight in the output
 };
 
 // One CTA = 4 warps = one share of a (sequence, kv head)'s context; cluster
@@ -155,6 +122,11 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeParam
   const int g = lane >> 2;   // fragment row group: head (S^T) / token (K^T)
   const int c = lane & 3;
 
+  // The next kernel may launch now.  Sequence metadata and block-table rows
+  // are read before this grid waits on the previous one (no kernel that
+  // triggers early writes them); q, K and V are read, and the output written,
+  // only after griddep_wait().
+  if (tid == 0) griddep_launch_dependents();
   const int seqlen = max(p.seq_lens[seq], 0);
   const int q_tok = p.qsl[seq];
   const int out_row = p.out_by_qsl ? q_tok : seq;
@@ -164,28 +136,34 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeParam
   const int nchunks = (hi - lo + kChunk - 1) / kChunk;
   const int32_t* bt_row = p.bt + (int64_t)seq * p.bt_stride;
 
-  // ---- chunk loader: one thread per row, 16-byte cp.async pieces ----------
-  auto issue_chunk = [&](int ch) {
+  // ---- chunk loader: one thread per row (kChunk == kThreads), 16-byte pieces --
+  auto row_block = [&](int ch) -> int64_t {  // block of this thread's row, or -1
+    const int tok = lo + ch * kChunk + tid;
+    if (ch >= nchunks || tok >= hi) return -1;
+    const int bi = p.bs_shift >= 0 ? tok >> p.bs_shift : tok / p.block_size;
+    return bt_row[bi];
+  };
+  auto issue_chunk = [&](int ch, int64_t blk) {
     uint8_t* ks = smem + (ch & 1) * L::STAGE;
     uint8_t* vs = ks + kChunk * L::KP;
-    const int t0 = lo + ch * kChunk;
-    const int nt = min(kChunk, hi - t0);
-    for (int r = tid; r < nt; r += kThreads) {
-      const int tok = t0 + r;
-      const int bi = p.bs_shift >= 0 ? tok >> p.bs_shift : tok / p.block_size;
+    const int tok = lo + ch * kChunk + tid;
+    if (blk >= 0) {
       const int64_t slot = p.bs_shift >= 0 ? tok & (p.block_size - 1) : tok % p.block_size;
-      const int64_t blk = bt_row[bi];
       const uint8_t* kg = p.k + blk * p.sk0 + slot * p.sk1 + kh * p.sk2;
       const uint8_t* vg = p.v + blk * p.sv0 + slot * p.sv1 + kh * p.sv2;
 #pragma unroll
       for (int j = 0; j < RB / 16; ++j) {
-        cp_async16(ks + r * L::KP + j * 16, kg + j * 16);
-        cp_async16(vs + r * L::VP + j * 16, vg + j * 16);
+        cp_async16(ks + tid * L::KP + j * 16, kg + j * 16);
+        cp_async16(vs + tid * L::VP + j * 16, vg + j * 16);
       }
     }
     cp_async_commit();
   };
-  if (nchunks > 0) issue_chunk(0);
+  // both stages' block-table entries before the wait, then both stages in flight
+  const int64_t blk0 = row_block(0), blk1 = row_block(1);
+  griddep_wait();
+  issue_chunk(0, blk0);
+  issue_chunk(1, blk1);
 
   // ---- q as the A operand: rows = heads (g < GQA), per-head exact prescale --
   // A fragment of 16 dims: a0 = (head g, dims 4c, 4c+1), a2 = (head g, dims
@@ -247,121 +225,120 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeParam
     for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
 
   for (int ch = 0; ch < nchunks; ++ch) {
-    __syncthreads();  // stage (ch+1)&1 is free (its last readers were chunk ch-1)
-    if (ch + 1 < nchunks) {
-      issue_chunk(ch + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    // chunks ch and ch+1 are in flight (an empty group stands in past the end)
+    cp_async_wait<1>();
     __syncthreads();
     const uint8_t* ks = smem + (ch & 1) * L::STAGE;
     const uint8_t* vs = ks + kChunk * L::KP;
     const int nt = min(kChunk, hi - (lo + ch * kChunk));
     const int w0 = warp * 32;                 // this warp's first token in the chunk
     const int ntw = max(0, min(32, nt - w0));  // its valid tokens
-    if (ntw == 0) continue;
+    if (ntw > 0) {  // this warp's tokens of the chunk
 
-    // V rows of this warp as f16 (fp8 path), zero past the valid tokens
-    const uint8_t* vrows;
-    int vpitch;
-    if constexpr (FP8) {
-      uint8_t* vc = smem + 2 * L::STAGE + warp * 32 * L::CP;
-      for (int i = lane; i < 32 * 16; i += 32) {
-        const int r = i >> 4, j = i & 15;  // row, 8-byte piece
-        uint4 h = make_uint4(0, 0, 0, 0);
-        if (r < ntw) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(vs + (w0 + r) * L::VP + j * 8);
-          h.x = e4m3x2_to_f16x2(raw.x & 0xFFFFu);
-          h.y = e4m3x2_to_f16x2(raw.x >> 16);
-          h.z = e4m3x2_to_f16x2(raw.y & 0xFFFFu);
-          h.w = e4m3x2_to_f16x2(raw.y >> 16);
+      // V rows of this warp as f16 (fp8 path), zero past the valid tokens
+      const uint8_t* vrows;
+      int vpitch;
+      if constexpr (FP8) {
+        uint8_t* vc = smem + 2 * L::STAGE + warp * 32 * L::CP;
+        for (int i = lane; i < 32 * 16; i += 32) {
+          const int r = i >> 4, j = i & 15;  // row, 8-byte piece
+          uint4 h = make_uint4(0, 0, 0, 0);
+          if (r < ntw) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(vs + (w0 + r) * L::VP + j * 8);
+            h.x = e4m3x2_to_f16x2(raw.x & 0xFFFFu);
+            h.y = e4m3x2_to_f16x2(raw.x >> 16);
+            h.z = e4m3x2_to_f16x2(raw.y & 0xFFFFu);
+            h.w = e4m3x2_to_f16x2(raw.y >> 16);
+          }
+          *reinterpret_cast<uint4*>(vc + r * L::CP + j * 16) = h;
         }
-        *reinterpret_cast<uint4*>(vc + r * L::CP + j * 16) = h;
+        __syncwarp();
+        vrows = vc;
+        vpitch = L::CP;
+      } else {
+        // rows past the valid tokens hold stale bytes: zero them so 0 * V stays 0
+        uint8_t* vw = const_cast<uint8_t*>(vs) + w0 * L::VP;
+        for (int i = ntw * 16 + lane; i < 32 * 16; i += 32)
+          *reinterpret_cast<uint4*>(vw + (i >> 4) * L::VP + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
+        __syncwarp();
+        vrows = vw;
+        vpitch = L::VP;
       }
-      __syncwarp();
-      vrows = vc;
-      vpitch = L::CP;
-    } else {
-      // rows past the valid tokens hold stale bytes: zero them so 0 * V stays 0
-      uint8_t* vw = const_cast<uint8_t*>(vs) + w0 * L::VP;
-      for (int i = ntw * 16 + lane; i < 32 * 16; i += 32)
-        *reinterpret_cast<uint4*>(vw + (i >> 4) * L::VP + (i & 15) * 16) = make_uint4(0, 0, 0, 0);
-      __syncwarp();
-      vrows = vw;
-      vpitch = L::VP;
-    }
 
-    // ---- S^T = q K^T over 4 token tiles of 8 --------------------------------
-    float sfr[4][4];
+      // ---- S^T = q K^T over 4 token tiles of 8 --------------------------------
+      float sfr[4][4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < 4; ++t) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) sfr[t][e] = 0.f;
-      const uint8_t* krow = ks + (w0 + 8 * t + g) * L::KP;
+        for (int e = 0; e < 4; ++e) sfr[t][e] = 0.f;
+        const uint8_t* krow = ks + (w0 + 8 * t + g) * L::KP;
 #pragma unroll
-      for (int ds = 0; ds < 8; ++ds) {
-        uint32_t b0, b1;
-        if constexpr (FP8) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(krow + 16 * ds + 4 * c);
-          b0 = e4m3x2_to_f16x2(w & 0xFFFFu);
-          b1 = e4m3x2_to_f16x2(w >> 16);
-        } else {
-          const uint2 w = *reinterpret_cast<const uint2*>(krow + 32 * ds + 8 * c);
-          b0 = w.x;
-          b1 = w.y;
+        for (int ds = 0; ds < 8; ++ds) {
+          uint32_t b0, b1;
+          if constexpr (FP8) {
+            const uint32_t w = *reinterpret_cast<const uint32_t*>(krow + 16 * ds + 4 * c);
+            b0 = e4m3x2_to_f16x2(w & 0xFFFFu);
+            b1 = e4m3x2_to_f16x2(w >> 16);
+          } else {
+            const uint2 w = *reinterpret_cast<const uint2*>(krow + 32 * ds + 8 * c);
+            b0 = w.x;
+            b1 = w.y;
+          }
+          mma16816<FP8>(sfr[t], qa[ds][0], 0u, qa[ds][1], 0u, b0, b1);
         }
-        mma16816<FP8>(sfr[t], qa[ds][0], 0u, qa[ds][1], 0u, b0, b1);
       }
-    }
 
-    // ---- online softmax for head g over this warp's tokens ------------------
-    float mx = -INFINITY;
+      // ---- online softmax for head g over this warp's tokens ------------------
+      float mx = -INFINITY;
 #pragma unroll
-    for (int t = 0; t < 4; ++t)
+      for (int t = 0; t < 4; ++t)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tok = 8 * t + 2 * c + e;
-        const float v = tok < ntw ? sfr[t][e] * score_scale : -INFINITY;
-        sfr[t][e] = v;
-        mx = fmaxf(mx, v);
+        for (int e = 0; e < 2; ++e) {
+          const int tok = 8 * t + 2 * c + e;
+          const float v = tok < ntw ? sfr[t][e] * score_scale : -INFINITY;
+          sfr[t][e] = v;
+          mx = fmaxf(mx, v);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);          // finite: ntw >= 1
+      const float alpha = exp2f(m_run - m_new);      // 0 on the first chunk
+      m_run = m_new;
+      float psum = 0.f;
+      uint32_t pb[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float p0 = exp2f(sfr[t][0] - m_new);
+        const float p1 = exp2f(sfr[t][1] - m_new);
+        psum += p0 + p1;
+        pb[t] = FP8 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
       }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m_run, mx);          // finite: ntw >= 1
-    const float alpha = exp2f(m_run - m_new);      // 0 on the first chunk
-    m_run = m_new;
-    float psum = 0.f;
-    uint32_t pb[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const float p0 = exp2f(sfr[t][0] - m_new);
-      const float p1 = exp2f(sfr[t][1] - m_new);
-      psum += p0 + p1;
-      pb[t] = FP8 ? pack_f16x2(p0, p1) : pack_bf16x2(p0, p1);
-    }
-    l_run = l_run * alpha + psum;
-    // rescale O^T: this thread holds heads 2c and 2c+1, whose alpha lives in
-    // the lanes with g == 2c / 2c+1
-    const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * c) * 4);
-    const float a1 = __shfl_sync(0xffffffffu, alpha, (2 * c + 1) * 4);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      o[i][0] *= a0; o[i][1] *= a1; o[i][2] *= a0; o[i][3] *= a1;
-    }
-
-    // ---- O^T += V^T P^T over 2 token slices of 16 ---------------------------
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int vtok = 16 * j + (lane & 7) + ((lane >> 4) << 3);
+      l_run = l_run * alpha + psum;
+      // rescale O^T: this thread holds heads 2c and 2c+1, whose alpha lives in
+      // the lanes with g == 2c / 2c+1
+      const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * c) * 4);
+      const float a1 = __shfl_sync(0xffffffffu, alpha, (2 * c + 1) * 4);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        uint32_t a[4];
-        ldsm_x4_trans(a, vrows + vtok * vpitch + (16 * i + ((lane >> 3) & 1) * 8) * 2);
-        mma16816<FP8>(o[i], a[0], a[1], a[2], a[3], pb[2 * j], pb[2 * j + 1]);
+        o[i][0] *= a0; o[i][1] *= a1; o[i][2] *= a0; o[i][3] *= a1;
+      }
+
+      // ---- O^T += V^T P^T over 2 token slices of 16 ---------------------------
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int vtok = 16 * j + (lane & 7) + ((lane >> 4) << 3);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t a[4];
+          ldsm_x4_trans(a, vrows + vtok * vpitch + (16 * i + ((lane >> 3) & 1) * 8) * 2);
+          mma16816<FP8>(o[i], a[0], a[1], a[2], a[3], pb[2 * j], pb[2 * j + 1]);
+        }
       }
     }
+    __syncthreads();  // stage ch&1 is free: chunk ch+2 goes there
+    issue_chunk(ch + 2, row_block(ch + 2));
   }
+  cp_async_wait<0>();  // only empty groups remain; the stages are reused below
 
   // ---- merge the 4 warps: per-warp state -> this CTA's partial --------------
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
@@ -419,34 +396,48 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeParam
   __nv_bfloat16* out_base = p.out + (int64_t)out_row * p.o_st + (int64_t)(kh * GQA) * p.o_sh;
 
   // ---- merge the cluster's partials through distributed shared memory -----
+  // Every remote read is issued independently of the others: one round of
+  // (m, l) loads, then one float4 of one rank's o per work item, so the merge
+  // costs two distributed-shared-memory round trips whatever the cluster size.
   cluster.sync();
-  if (tid < GQA) {
-    float mg = -INFINITY;
-    for (int r = 0; r < csize; ++r) mg = fmaxf(mg, cluster.map_shared_rank(&S.part_m[0], r)[tid]);
-    float lg = 0.f;
-    if (mg != -INFINITY)
-      for (int r = 0; r < csize; ++r) {
-        const float mr = cluster.map_shared_rank(&S.part_m[0], r)[tid];
-        if (mr != -INFINITY) lg += exp2f(mr - mg) * cluster.map_shared_rank(&S.part_l[0], r)[tid];
-      }
-    S.comb_m[tid] = mg;
-    S.comb_l[tid] = lg;
+  if (tid < csize * GQA) {
+    const int r = tid / GQA, h = tid % GQA;
+    S.rm[r][h] = cluster.map_shared_rank(&S.part_m[0], r)[h];
+    S.rl[r][h] = cluster.map_shared_rank(&S.part_l[0], r)[h];
   }
   __syncthreads();
-  constexpr int E = GQA * kHeadDim;
-  const int e0 = rank * E / csize, e1 = (rank + 1) * E / csize;
-  for (int e = e0 + tid; e < e1; e += kThreads) {
-    const int h = e / kHeadDim, d = e % kHeadDim;
-    const float mg = S.comb_m[h];
-    float acc = 0.f;
+  if (tid < GQA) {
+    float mg = -INFINITY;
+    for (int r = 0; r < csize; ++r) mg = fmaxf(mg, S.rm[r][tid]);
+    float lg = 0.f;
     if (mg != -INFINITY)
-      for (int r = 0; r < csize; ++r) {
-        const float mr = cluster.map_shared_rank(&S.part_m[0], r)[h];
-        if (mr != -INFINITY)
-          acc += exp2f(mr - mg) * cluster.map_shared_rank(&S.part_o[0][0], r)[h * kHeadDim + d];
-      }
-    const float lg = S.comb_l[h];
-    out_base[(int64_t)h * p.o_sh + d] = __float2bfloat16_rn(lg > 0.f ? acc * vsc / lg : 0.f);
+      for (int r = 0; r < csize; ++r)
+        if (S.rm[r][tid] != -INFINITY) lg += exp2f(S.rm[r][tid] - mg) * S.rl[r][tid];
+    const float inv = lg > 0.f ? vsc / lg : 0.f;
+    for (int r = 0; r < csize; ++r)
+      S.rw[r][tid] = (mg != -INFINITY && S.rm[r][tid] != -INFINITY) ? exp2f(S.rm[r][tid] - mg) * inv : 0.f;
+  }
+  __syncthreads();
+  // this CTA writes elements [e0, e0 + per_cta) of the (head, dim) block;
+  // contribution of rank r to element i lands in contrib[r * per_cta + i]
+  constexpr int E = GQA * kHeadDim;
+  const int per_cta = E / csize, nv = per_cta / 4, e0 = rank * per_cta;
+  float* contrib = reinterpret_cast<float*>(smem);  // the stages are free
+  for (int it = tid; it < csize * nv; it += kThreads) {
+    const int r = it / nv, v = it - r * nv;
+    const int e = e0 + 4 * v;
+    const float w = S.rw[r][e / kHeadDim];
+    float4 ov = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (w != 0.f) ov = *reinterpret_cast<const float4*>(cluster.map_shared_rank(&S.part_o[0][0], r) + e);
+    *reinterpret_cast<float4*>(contrib + r * per_cta + 4 * v) =
+        make_float4(w * ov.x, w * ov.y, w * ov.z, w * ov.w);
+  }
+  __syncthreads();
+  for (int i = tid; i < per_cta; i += kThreads) {
+    float acc = 0.f;
+    for (int r = 0; r < csize; ++r) acc += contrib[r * per_cta + i];
+    const int e = e0 + i, h = e / kHeadDim, d = e % kHeadDim;
+    out_base[(int64_t)h * p.o_sh + d] = __float2bfloat16_rn(acc);
   }
   cluster.sync();  // peers' shared memory stays alive until every rank is done
 }
@@ -469,17 +460,27 @@ cudaError_t launch_decode(const DecodeParams& p, int csize, int hkv, int num_seq
   lc.blockDim = dim3(kThreads, 1, 1);
   lc.dynamicSmemBytes = smem;
   lc.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = csize;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
-  lc.numAttrs = 1;
+  lc.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&lc, decode_attn_kernel<GQA, FP8>, p);
 }
 
 }  // namespace
+
+int decode_tma_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
+                      const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
+                      int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
+                      const int32_t* qsl, const int32_t* seq_lens, const int32_t* bt,
+                      int64_t bt_stride, const float* k_scale, const float* v_scale,
+                      float sm_scale, int num_seqs, int hkv, int gqa, int block_size,
+                      int num_blocks, int out_by_qsl, int csize, void* stream);
 
 // Cluster size (CTAs per (sequence, kv head)): the largest power of two <= 16
 // that keeps the grid within two CTAs per SM, but at least one CTA per 4096
@@ -509,8 +510,8 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        const int32_t* qsl, const int32_t* seq_lens, const int32_t* bt,
                        int64_t bt_stride, const float* k_scale, const float* v_scale,
                        float sm_scale, int num_seqs, int hq, int hkv, int head_dim,
-                       int block_size, int max_blocks, int hint, int kv_dtype, int out_by_qsl,
-                       int num_splits, void* stream) {
+                       int block_size, int num_blocks, int max_blocks, int hint, int kv_dtype,
+                       int out_by_qsl, int num_splits, void* stream) {
   if (!q || !k_cache || !v_cache || !out || !qsl || !seq_lens || !bt) return B200KV_ERR_INVALID_ARG;
   if (num_seqs <= 0 || hq <= 0 || hkv <= 0 || block_size <= 0 || max_blocks <= 0)
     return B200KV_ERR_INVALID_ARG;
@@ -530,6 +531,16 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
       (reinterpret_cast<uintptr_t>(q) & 15) || ((q_st % 8) != 0) || ((q_sh % 8) != 0))
     return B200KV_ERR_MISALIGNED;
   if (sm_major_current_device() < 10) return B200KV_ERR_NO_DEVICE;
+
+  const int ctx = hint > 0 ? hint : max_blocks * block_size;
+  const int cs = decode_cluster_size(num_seqs, hkv, ctx, num_splits);
+  if (fp8) {  // pages by TMA when the cache can be described by tensor maps
+    const int r = decode_tma_launch(q, q_st, q_sh, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2,
+                                    out, o_st, o_sh, qsl, seq_lens, bt, bt_stride, k_scale, v_scale,
+                                    sm_scale, num_seqs, hkv, gqa, block_size, num_blocks, out_by_qsl,
+                                    cs, stream);
+    if (r != B200KV_ERR_UNSUPPORTED) return r;
+  }
 
   DecodeParams p;
   p.q = static_cast<const __nv_bfloat16*>(q);
@@ -553,8 +564,6 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
   p.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz((unsigned)block_size) : -1;
   p.out_by_qsl = out_by_qsl;
 
-  const int ctx = hint > 0 ? hint : max_blocks * block_size;
-  const int cs = decode_cluster_size(num_seqs, hkv, ctx, num_splits);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (gqa * 2 + (fp8 ? 1 : 0)) {

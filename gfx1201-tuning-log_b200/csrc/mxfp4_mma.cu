@@ -171,6 +171,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_slot;
+  // The next kernel may launch now.  Weights and scale atoms are load-time
+  // data, so the producer streams them before this grid waits on the previous
+  // one; x is read, and the output written, only after griddep_wait().
+  if (tid == 0) griddep_launch_dependents();
 
   if (warp == 0) {
     // ---------------- producer: (4 W boxes, 8 scale atoms) per stage ---------------
@@ -259,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = et; i < ns * 2 * kAtom / 4; i += 128)
       reinterpret_cast<uint32_t*>(sfb)[i] = 0x7F7F7F7Fu;
     named_bar_sync(1, 128);
+    griddep_wait();  // x is the previous kernel's output
     // one 32-element block of one activation row per work item
     const int nblk = ns * 8;
     for (int w = et; w < a.M * nblk; w += 128) {
@@ -333,6 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---- reduce the cluster's K-slices through distributed shared memory -----------
+  griddep_wait();  // every thread, before any output store (and before exit)
   tc::fence_before_sync();
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
@@ -400,13 +406,15 @@ cudaError_t launch_mma(const CUtensorMap& wm, const MmaArgs& a, int ks, cudaStre
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = ks;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, mxfp4_mma_kernel<MAXM>, wm, a);
 }
 

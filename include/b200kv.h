@@ -111,6 +111,10 @@ void h4mv_launch(const void* W, const void* St, const void* Xb, void* Out,
  *   block_table  int32 [num_seqs, >= max_blocks_per_seq], row stride bt_stride
  *   k/v_scale    device fp32 scalars (ignored for bf16 KV)
  *   head_dim must be 128; GQA must be 1, 2, 4 or 8.
+ *   num_blocks   blocks in the cache (its first dimension), 0 if unknown.  fp8
+ *                caches with block_size 16/32/64/128 and num_blocks > 0 have their
+ *                pages loaded by TMA (block ids outside [0, num_blocks) read as
+ *                zeros); other caches take a per-row asynchronous-copy gather.
  *   num_splits   CTAs (a thread-block cluster) that share one (sequence, kv head):
  *                0 = choose from the SM count and the context bound (max_seq_len_hint,
  *                or max_blocks_per_seq*block_size when the hint is 0); otherwise a
@@ -126,8 +130,9 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
                        const int32_t* block_table, int64_t bt_stride,
                        const float* k_scale, const float* v_scale, float sm_scale,
                        int num_seqs, int num_q_heads, int num_kv_heads, int head_dim,
-                       int block_size, int max_blocks_per_seq, int max_seq_len_hint,
-                       int kv_dtype, int out_by_qsl, int num_splits, void* stream);
+                       int block_size, int num_blocks, int max_blocks_per_seq,
+                       int max_seq_len_hint, int kv_dtype, int out_by_qsl, int num_splits,
+                       void* stream);
 
 /* ---- MXFP4 on block-scaled tensor cores (load-time packed scales) -------------
  *

@@ -65,14 +65,14 @@ def _decode_call(lib, **over):
     args = dict(q=A, qst=32 * 128, qsh=128, k=A, v=A, sk0=16 * 8 * 128, sk1=8 * 128, sk2=128,
                 sv0=16 * 8 * 128, sv1=8 * 128, sv2=128, out=A, ost=32 * 128, osh=128,
                 qsl=A, sl=A, bt=A, bts=4, ks=A, vs=A, sm=0.088, ns=2, hq=32, hkv=8, d=128,
-                pblk=16, maxblk=4, hint=0, kvdt=0, obq=0, nsplit=0, st=None)
+                pblk=16, nblk=0, maxblk=4, hint=0, kvdt=0, obq=0, nsplit=0, st=None)
     args.update(over)
     a = args
     return lib.b200kv_decode_attn(a["q"], a["qst"], a["qsh"], a["k"], a["v"], a["sk0"], a["sk1"],
                                   a["sk2"], a["sv0"], a["sv1"], a["sv2"], a["out"], a["ost"],
                                   a["osh"], a["qsl"], a["sl"], a["bt"], a["bts"], a["ks"], a["vs"],
                                   a["sm"], a["ns"], a["hq"], a["hkv"], a["d"], a["pblk"],
-                                  a["maxblk"], a["hint"], a["kvdt"], a["obq"], a["nsplit"],
+                                  a["nblk"], a["maxblk"], a["hint"], a["kvdt"], a["obq"], a["nsplit"],
                                   a["st"])
 
 

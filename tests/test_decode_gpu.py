@@ -216,3 +216,53 @@ def test_cuda_graph_capture(cuda):
     ref = FO.decode_reference(c["q"], c["k_cache"], c["v_cache"], c["qsl"], c["seq_lens"],
                               c["block_table"], c["k_scale"], c["v_scale"], c["sm_scale"])
     _check(out, ref)
+
+
+# ---- the two page-load paths: TMA page tiles (fp8, block 16/32/64/128, pool
+# size known) and the per-row asynchronous-copy gather (everything else, or
+# B200KV_DECODE_TMA=0) -------------------------------------------------------
+def _oracle(c):
+    return FO.decode_reference(c["q"], c["k_cache"], c["v_cache"], c["qsl"], c["seq_lens"],
+                               c["block_table"], c["k_scale"], c["v_scale"], c["sm_scale"])
+
+
+@pytest.mark.parametrize("path", ["tma", "gather"])
+@pytest.mark.parametrize("pblk", [16, 32, 64, 128, 48])
+def test_block_sizes_both_paths(cuda, monkeypatch, path, pblk):
+    if path == "gather":
+        monkeypatch.setenv("B200KV_DECODE_TMA", "0")
+    lens = [1, 47, 129, 1000, 4096, 2500]
+    c = FO.make_decode_case(len(lens), lens, pblk=pblk, seed=100 + pblk)
+    _check(_run_v3(c, cuda), _oracle(c))
+
+
+def test_paths_agree_bit_for_bit(cuda, monkeypatch):
+    """Both paths take the same per-token products in the same order (the TMA
+    path only permutes MMA rows), so their outputs are identical."""
+    lens = [4096, 33, 2000, 700, 1, 4096, 3333, 129]
+    c = FO.make_decode_case(len(lens), lens, seed=110)
+    a = _run_v3(c, cuda)
+    monkeypatch.setenv("B200KV_DECODE_TMA", "0")
+    b = _run_v3(c, cuda)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("pblk", [16, 64])
+def test_nan_codes_past_the_sequence(cuda, pblk):
+    """Slots of the last page past seq_len, and every unused pool block, hold
+    0x7F (an fp8 NaN): they must not reach the output."""
+    lens = [5, 100, 1023, 4095]
+    c = FO.make_decode_case(len(lens), lens, pblk=pblk, seed=120)
+    kc = c["k_cache"].view(torch.uint8).clone()
+    vc = c["v_cache"].view(torch.uint8).clone()
+    used = torch.zeros(kc.shape[0], pblk, dtype=torch.bool)
+    for s, L in enumerate(lens):
+        for t in range(L):
+            used[int(c["block_table"][s, t // pblk]), t % pblk] = True
+    kc[~used] = 0x7F
+    vc[~used] = 0x7F
+    c["k_cache"], c["v_cache"] = kc.view(torch.float8_e4m3fn), vc.view(torch.float8_e4m3fn)
+    out = _run_v3(c, cuda)
+    assert torch.isfinite(out.float()).all()
+    _check(out, _oracle(c))
+
