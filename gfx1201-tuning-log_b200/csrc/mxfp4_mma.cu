@@ -27,8 +27,12 @@
 // Packed 4-bit operands keep every TMA request at a full 128-byte row and every
 // in-flight weight byte at one byte of shared memory (an unpacked 8-bit-container
 // operand would halve both).  Work split: a thread-block cluster of ks CTAs
-// splits K; clusters take 128-row tiles round-robin; partial tiles are reduced
-// through distributed shared memory.  Warp 0 streams (W box, 2 scale atoms)
+// splits K; clusters take 128-row tiles round-robin; each tile's partials are
+// pushed (st.async into distributed shared memory) to one rank of the cluster,
+// which adds them in a fixed order and stores the bf16 row, so no rank waits
+// on a cluster-wide barrier at the end.  The kernel is launched with
+// programmatic stream serialization: weights stream before it waits on the
+// kernel that produces x.  Warp 0 streams (W box, 2 scale atoms)
 // stages through an mbarrier ring, warp 1 issues the MMAs from one thread,
 // warps 2-5 turn x into its four terms at the start and drain the accumulators.
 //
@@ -36,7 +40,6 @@
 // differs for the bytes 0 (it gives 0.0) and 255 (inf), so weights holding those
 // bytes stay on mxfp4_gemv.cu -- the packer reports them.
 
-#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -54,8 +57,6 @@
 #include "tcgen05.cuh"
 #include "tma.cuh"
 
-namespace cg = cooperative_groups;
-
 namespace b200kv {
 namespace {
 
@@ -64,15 +65,15 @@ constexpr int kAtomK = 128;            // K covered by one scale atom (4 groups)
 constexpr int kStep = 256;             // K per W box (128 B rows): 2 atoms, 4 MMAs
 constexpr int kBoxesPerStage = 4;      // a stage reads 512 contiguous bytes of each row
 constexpr int kTerms = 4;              // e2m1 terms of x
-constexpr int kNmma = 32;              // B rows: term p of activation row m at 8p + m
-constexpr int kMaxM = 8;
+constexpr int kMaxM = 8;               // B rows (MMA N) = 4 * S: term p of row m at S*p + m
 constexpr int kBox = kTile * 128;      // W box: 16 KB
 constexpr int kAtom = 512;
 constexpr int kStageBytes = kBoxesPerStage * (kBox + 2 * kAtom);  // 68 KB
-constexpr int kBStep = kNmma * 128;        // B rows of one W box: 4 KB
 constexpr int kMaxStages = 3;
 constexpr int kThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 x + epilogue
-constexpr uint32_t kTmemCols = 256;    // D[2][32] 0..63, SFA 64 + 32*(s&1), SFB 128 + 8*box
+// tensor memory: D[2][32] at 0..63, A scales of ring slot r at 64 + 32 r, the
+// activation scales at 64 + 32 nstages + 8 box; 256 columns, or 512 when that
+// does not fit (such CTAs are too large to share an SM anyway)
 constexpr int kMaxSliceBoxes = 16;     // SFB of a K-slice stays in tensor memory: 8 columns a box
 
 struct MmaArgs {
@@ -85,13 +86,39 @@ struct MmaArgs {
   int ntiles, nclusters, tmax, nstages;
 };
 
+// Dynamic shared memory: the stage ring, x's four terms (B operand), their
+// scale atoms, and the receive area of the K-slice reduction: tile i of a
+// cluster is finished by rank i % ks, which receives every rank's partial of it
+// in recv[i / ks][rank][row][m].
 struct MmaLayout {
-  int sps, tmax, nstages;
+  int sps, tmax, nstages, ks, S;  // S: B-row stride of the terms (M <= S, N = 4 S)
+  __host__ __device__ int owned_max() const { return (tmax + ks - 1) / ks; }
   __host__ __device__ size_t xb() const { return (size_t)nstages * kStageBytes; }
-  __host__ __device__ size_t sfb() const { return xb() + (size_t)sps * kBStep; }
-  __host__ __device__ size_t part() const { return sfb() + (size_t)sps * 2 * kAtom; }
-  __host__ __device__ size_t bytes(int m) const { return part() + (size_t)tmax * m * kTile * 4 + 1024; }
+  __host__ __device__ size_t sfb() const { return xb() + (size_t)sps * 4 * S * 128; }
+  __host__ __device__ size_t recv() const { return sfb() + (size_t)sps * 2 * kAtom; }
+  __host__ __device__ size_t bytes(int m) const {
+    return recv() + (size_t)owned_max() * ks * kTile * m * 4 + 1024;
+  }
 };
+
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// 4-byte store into a peer CTA's shared memory, counted in bytes on the peer's
+// mbarrier (both addresses from map_to_rank)
+__device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+               "r"(__float_as_uint(v)), "r"(rbar)
+               : "memory");
+}
 
 // instruction descriptor, kind::mxf4 block-scaled: A, B e2m1 (format 1 of this
 // kind), both K-major, e8m0 scales, scale-factor byte ids (0 or 2: two bytes per MMA)
@@ -135,24 +162,127 @@ __device__ __forceinline__ float2 e2m1x2_val(uint32_t byte) {
   return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
-template <int MAXM>
+// x -> four e2m1 terms with e8m0 scales per 32-element block, written as the
+// B operand (term t of activation row m is B row S*t + m, 128-byte-swizzled
+// K-major rows, one 16-byte chunk per block) and its scale atoms.  TPB threads
+// share a block, EPT = 32 / TPB elements each; the next item's elements are
+// loaded before the current one is converted.  Term t of a block: residual
+// maximum mx in [2^(E-127), 2^(E-126)) -> scale 2^(E-129), codes rounded to
+// nearest (ties to even) and saturated at 6, residual -= code * scale.
+template <int TPB, int S>
+__device__ __forceinline__ void split_terms(const MmaArgs& a, int et, int s_begin, int ns,
+                                            uint8_t* xb, uint8_t* sfb) {
+  constexpr int EPT = 32 / TPB;
+  constexpr int NV = EPT / 8;          // 16-byte loads per item
+  constexpr uint32_t kBBox = 4 * S * 128;
+  const int nblk = ns * 8;
+  const int total = a.M * nblk * TPB;
+  const int bound = (total + 31) & ~31;  // whole warps iterate together (shuffles)
+  auto load = [&](int w, uint4 (&v)[NV]) {
+    if (w < total) {
+      const int q = w % TPB, wb = w / TPB;
+      const int m = wb / nblk, blk = wb % nblk;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          a.X + (size_t)m * a.K + (size_t)(s_begin * kStep + blk * 32 + EPT * q));
+#pragma unroll
+      for (int i = 0; i < NV; ++i) v[i] = __ldg(src + i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) v[i] = make_uint4(0, 0, 0, 0);
+    }
+  };
+  uint4 cur[NV], nxt[NV];
+  load(et, cur);
+  for (int w = et; w < bound; w += 128) {
+    load(w + 128, nxt);
+    const bool live = w < total;
+    const int q = w % TPB, wb = live ? w / TPB : 0;
+    const int m = wb / nblk, blk = wb % nblk;
+    const int j = blk >> 3, kb8 = blk & 7;
+    float r[EPT];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t u[4] = {cur[i].x, cur[i].y, cur[i].z, cur[i].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        r[8 * i + 2 * e] = __uint_as_float(u[e] << 16);
+        r[8 * i + 2 * e + 1] = __uint_as_float(u[e] & 0xFFFF0000u);
+      }
+    }
+    uint8_t* bj = xb + (size_t)j * kBBox;
+#pragma unroll 1
+    for (int t = 0; t < kTerms; ++t) {
+      float mx = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) mx = fmaxf(mx, fabsf(r[e]));
+#pragma unroll
+      for (int o = 1; o < TPB; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+      // term scale 2^(E-129): the block max maps into [4, 8) (6 is e2m1's top)
+      const int sb = (mx == 0.f || E == 0xFF) ? 127 : max(E - 2, 1);
+      const float inv = __uint_as_float((uint32_t)(254 - sb) << 23);  // 2^-(sb-127)
+      const float scl = __uint_as_float((uint32_t)sb << 23);          // 2^(sb-127)
+      uint32_t words[EPT / 8];
+#pragma unroll
+      for (int k = 0; k < EPT / 8; ++k) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int i = 8 * k + 2 * e;
+          const uint32_t code = e2m1x2(r[i] * inv, r[i + 1] * inv);
+          const float2 v = e2m1x2_val(code);
+          r[i] = fmaf(-v.x, scl, r[i]);
+          r[i + 1] = fmaf(-v.y, scl, r[i + 1]);
+          word |= code << (8 * e);
+        }
+        words[k] = word;
+      }
+      if (live) {
+        const int n = S * t + m;  // B row
+        uint8_t* dst = bj + n * 128 + ((kb8 ^ (n & 7)) << 4) + (16 / TPB) * q;
+        if constexpr (TPB == 1)
+          *reinterpret_cast<uint4*>(dst) = make_uint4(words[0], words[1], words[2], words[3]);
+        else if constexpr (TPB == 2)
+          *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[1]);
+        else
+          *reinterpret_cast<uint32_t*>(dst) = words[0];
+        if (q == 0) sfb[(size_t)(2 * j + (kb8 >> 2)) * kAtom + 16 * n + (kb8 & 3)] = (uint8_t)sb;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+  }
+}
+
+// S = B-row stride of the activation terms: term p of activation row m is B
+// row S*p + m, so the MMA's N is 4 S (8, 16 or 32 for M <= 2, 4, 8).
+template <int S>
 __global__ void __launch_bounds__(kThreads, 1)
     mxfp4_mma_kernel(const __grid_constant__ CUtensorMap wmap, const MmaArgs a) {
+  constexpr int NB = 4 * S;                 // MMA N
+  constexpr uint32_t kBBox = NB * 128;      // B bytes per W box (K-major, 128-byte swizzle)
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages], d_full[2], d_free[2], x_ready;
+  __shared__ uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
+  __shared__ uint64_t d_full[2], d_free[2], x_ready, recv_bar;
   __shared__ uint32_t tmem_slot;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int rank = blockIdx.x;  // K-slice
+  const int rank = blockIdx.x;  // K-slice = rank in the cluster (cluster dims (ks, 1, 1))
+  const int ksz = gridDim.x;
   const int cid = blockIdx.y;
   const int s_begin = rank * a.sps;
-  const int ns = max(0, min(a.nsteps, s_begin + a.sps) - s_begin);  // steps in this slice
+  const int ns = max(0, min(a.nsteps, s_begin + a.sps) - s_begin);  // W boxes in this slice
+  const int spt = (ns + kBoxesPerStage - 1) / kBoxesPerStage;       // stages per tile
   const int my_tiles = cid < a.ntiles ? (a.ntiles - cid + a.nclusters - 1) / a.nclusters : 0;
-  const MmaLayout L{a.sps, a.tmax, a.nstages};
+  const int owned = my_tiles > rank ? (my_tiles - rank + ksz - 1) / ksz : 0;  // tiles i % ksz == rank
+  const MmaLayout L{a.sps, a.tmax, a.nstages, ksz, S};
   uint8_t* xb = dsm + L.xb();
   uint8_t* sfb = dsm + L.sfb();
-  float* part = reinterpret_cast<float*>(dsm + L.part());  // [tmax][M][128]
+  float* recv = reinterpret_cast<float*>(dsm + L.recv());  // [owned_max][ksz][128][M]
+  const uint32_t recv_bytes = (uint32_t)(owned * (ksz - 1) * kTile * a.M * 4);
+  const uint32_t tsfb_off = 64 + 32 * a.nstages;
+  const uint32_t tmem_cols = tsfb_off + 8 * a.sps <= 256 ? 256 : 512;
 
   if (tid == 0) {
     for (int i = 0; i < a.nstages; ++i) {
@@ -164,26 +294,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&d_free[b], 4);
     }
     mbar_init(&x_ready, 4);
+    mbar_init(&recv_bar, 1);
     fence_mbar_init();
+    if (recv_bytes) mbar_arrive_expect_tx(&recv_bar, recv_bytes);  // peers' pushes complete it
   }
-  if (warp == 0) tc::tmem_alloc(&tmem_slot, kTmemCols);
+  if (warp == 0) tc::tmem_alloc(&tmem_slot, tmem_cols);
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tbase = tmem_slot;
+  if (ksz > 1) cluster_arrive_relaxed();  // recv_bar is initialised (peers wait before pushing)
   // The next kernel may launch now.  Weights and scale atoms are load-time
   // data, so the producer streams them before this grid waits on the previous
   // one; x is read, and the output written, only after griddep_wait().
   if (tid == 0) griddep_launch_dependents();
 
   if (warp == 0) {
-    // ---------------- producer: (4 W boxes, 8 scale atoms) per stage ---------------
+    // ---------------- producer: per stage up to 4 (W box, its 2 scale atoms) -------------
     if (lane == 0 && ns > 0) {
       tma_prefetch_desc(&wmap);
       bool failed = false;
       int s = 0;
       const int atoms_per_tile = a.nsteps * 2;
-      const int spt = (ns + kBoxesPerStage - 1) / kBoxesPerStage;  // stages per tile
       for (int i = 0; i < my_tiles && !failed; ++i) {
         const int tile = cid + i * a.nclusters;
         for (int t = 0; t < spt; ++t, ++s) {
@@ -195,8 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = dsm + (size_t)slot * kStageBytes;
           const int b0 = t * kBoxesPerStage;
           const int nb = min(kBoxesPerStage, ns - b0);
-          mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(nb * (kBox + 2 * kAtom)));
           const int g = s_begin + b0;  // first W box (along K) of this stage
+          mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(nb * (kBox + 2 * kAtom)));
           for (int q = 0; q < nb; ++q)  // adjacent K boxes back to back: 512 B per row
             tma_load_2d(st + q * kBox, &wmap, (g + q) * (kStep / 2), tile * kTile, &full_bar[slot]);
           bulk_g2s(st + kBoxesPerStage * kBox, a.Sp + ((size_t)tile * atoms_per_tile + 2 * g) * kAtom,
@@ -209,48 +341,69 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------------------------------------------
+    // A stage is "in" once its bytes landed and its weight-scale atoms were copied
+    // to tensor memory.  Until x is ready the issuer brings in the stages issued
+    // before this grid waited on the previous kernel, so that afterwards only
+    // the MMAs of those stages remain (an mbarrier wait and the atom copies cost
+    // about as much issue time as the MMAs themselves).
     if (lane == 0 && ns > 0) {
-      bool failed = !mbar_wait_bounded(&x_ready, 0);
-      tc::fence_after_sync();
       const uint32_t a_ring = smem_u32(dsm), a_xb = smem_u32(xb), a_sfb = smem_u32(sfb);
-      const int spt = (ns + kBoxesPerStage - 1) / kBoxesPerStage;
-      const uint32_t tsfb = tbase + 128;  // the activation scales: all boxes of the slice, once
-      for (int q = 0; q < 2 * ns; ++q) tmem_cp_atom(tsfb + 4 * q, sdesc_atom(a_sfb + (uint32_t)q * kAtom));
-      int s = 0;
-      for (int i = 0; i < my_tiles; ++i) {
-        const int b = i & 1;
-        if (i >= 2 && !failed) failed = !mbar_wait_bounded(&d_free[b], ((i - 2) >> 1) & 1);
-        tc::fence_after_sync();
-        const uint32_t tD = tbase + 32 * b;
-        for (int t = 0; t < spt; ++t, ++s) {
-          const int slot = s % a.nstages;
-          if (failed || !mbar_wait_bounded(&full_bar[slot], (s / a.nstages) & 1)) {
-            failed = true;  // issue nothing more
+      const uint32_t tsfb = tbase + tsfb_off;  // the activation scales: all boxes of the slice
+      const int total = my_tiles * spt;       // stages of this CTA
+      bool failed = false;
+      int s_in = 0;
+      auto stage_in = [&](int s) {
+        const int slot = s % a.nstages;
+        if (!mbar_wait_bounded(&full_bar[slot], (s / a.nstages) & 1)) return false;
+        const int nb = min(kBoxesPerStage, ns - (s % spt) * kBoxesPerStage);
+        const uint32_t atoms = a_ring + (uint32_t)slot * kStageBytes + kBoxesPerStage * kBox;
+        const uint32_t tsfa = tbase + 64 + 32 * slot;
+        for (int q = 0; q < 2 * nb; ++q) tmem_cp_atom(tsfa + 4 * q, sdesc_atom(atoms + (uint32_t)q * kAtom));
+        return true;
+      };
+      bool xr = mbar_test(&x_ready, 0);
+      while (!xr && !failed && s_in < min(total, a.nstages)) {
+        failed = !stage_in(s_in++);
+        xr = mbar_test(&x_ready, 0);
+      }
+      if (!failed && !xr) failed = !mbar_wait_bounded(&x_ready, 0);
+      tc::fence_after_sync();
+      if (!failed)
+        for (int q = 0; q < 2 * ns; ++q) tmem_cp_atom(tsfb + 4 * q, sdesc_atom(a_sfb + (uint32_t)q * kAtom));
+      for (int s = 0; s < total && !failed; ++s) {
+        const int i = s / spt, t = s % spt, b = i & 1;
+        if (t == 0) {  // accumulator b is free once the epilogue drained tile i - 2
+          if (i >= 2 && !mbar_wait_bounded(&d_free[b], ((i - 2) >> 1) & 1)) {
+            failed = true;
             break;
           }
           tc::fence_after_sync();
-          const uint32_t tsfa = tbase + 64 + 32 * (s & 1);
-          const uint32_t st = a_ring + (uint32_t)slot * kStageBytes;
-          const int b0 = t * kBoxesPerStage;
-          const int nb = min(kBoxesPerStage, ns - b0);
-          for (int q = 0; q < 2 * nb; ++q)
-            tmem_cp_atom(tsfa + 4 * q, sdesc_atom(st + kBoxesPerStage * kBox + (uint32_t)q * kAtom));
-          for (int q = 0; q < nb; ++q) {
-            const uint32_t abox = st + (uint32_t)q * kBox;
-            const uint32_t bbox = a_xb + (uint32_t)(b0 + q) * kBStep;
-#pragma unroll
-            for (int kq = 0; kq < 4; ++kq) {  // K = 64 each; scale bytes 2(kq&1).. of atom kq/2
-              const uint32_t sf = 2u * (uint32_t)(kq & 1);
-              mma_mxf4(tD, tc::sdesc_sw128(abox + kq * 32, 16, 1024),
-                       tc::sdesc_sw128(bbox + kq * 32, 16, 1024), idesc_mxf4(kTile, kNmma, sf),
-                       (t > 0 || q > 0 || kq > 0) ? 1u : 0u,
-                       (tsfa + 8 * q + 4 * (kq >> 1)) | (sf << 30),
-                       (tsfb + 8 * (b0 + q) + 4 * (kq >> 1)) | (sf << 30));
-            }
-          }
-          tc::commit(&empty_bar[slot]);
         }
-        tc::commit(&d_full[b]);
+        if (s == s_in && !stage_in(s_in++)) {
+          failed = true;  // issue nothing more
+          break;
+        }
+        const int slot = s % a.nstages;
+        const uint32_t tsfa = tbase + 64 + 32 * slot;
+        const uint32_t st = a_ring + (uint32_t)slot * kStageBytes;
+        const uint32_t tD = tbase + 32 * b;
+        const int b0 = t * kBoxesPerStage;
+        const int nb = min(kBoxesPerStage, ns - b0);
+        for (int q = 0; q < nb; ++q) {
+          const uint32_t abox = st + (uint32_t)q * kBox;
+          const uint32_t bbox = a_xb + (uint32_t)(b0 + q) * kBBox;
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {  // K = 64 each; scale bytes 2(kq&1).. of atom kq/2
+            const uint32_t sf = 2u * (uint32_t)(kq & 1);
+            mma_mxf4(tD, tc::sdesc_sw128(abox + kq * 32, 16, 1024),
+                     tc::sdesc_sw128(bbox + kq * 32, 16, 1024), idesc_mxf4(kTile, NB, sf),
+                     (t > 0 || q > 0 || kq > 0) ? 1u : 0u,
+                     (tsfa + 8 * q + 4 * (kq >> 1)) | (sf << 30),
+                     (tsfb + 8 * (b0 + q) + 4 * (kq >> 1)) | (sf << 30));
+          }
+        }
+        tc::commit(&empty_bar[slot]);
+        if (t == spt - 1) tc::commit(&d_full[b]);
       }
     }
   } else {
@@ -258,103 +411,82 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int et = tid - 64;                      // 0..127
     const int row = 32 * (warp & 3) + lane;       // TMEM lane of this thread
     // zero the B rows (rows of absent activation rows stay zero); scales 2^0
-    for (int i = et; i < ns * kBStep / 16; i += 128)
+    for (int i = et; i < ns * (int)kBBox / 16; i += 128)
       reinterpret_cast<uint4*>(xb)[i] = make_uint4(0, 0, 0, 0);
     for (int i = et; i < ns * 2 * kAtom / 4; i += 128)
       reinterpret_cast<uint32_t*>(sfb)[i] = 0x7F7F7F7Fu;
     named_bar_sync(1, 128);
     griddep_wait();  // x is the previous kernel's output
-    // one 32-element block of one activation row per work item
-    const int nblk = ns * 8;
-    for (int w = et; w < a.M * nblk; w += 128) {
-      const int m = w / nblk, blk = w % nblk;
-      const int j = blk >> 3, kb8 = blk & 7;
-      const __nv_bfloat16* xr = a.X + (size_t)m * a.K + (size_t)(s_begin * kStep + blk * 32);
-      float r[32];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 r4 = __ldg(reinterpret_cast<const uint4*>(xr) + q);
-        const uint32_t u[4] = {r4.x, r4.y, r4.z, r4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          r[8 * q + 2 * e] = __uint_as_float(u[e] << 16);
-          r[8 * q + 2 * e + 1] = __uint_as_float(u[e] & 0xFFFF0000u);
-        }
-      }
-      uint8_t* bj = xb + (size_t)j * kBStep;
-#pragma unroll 1
-      for (int t = 0; t < kTerms; ++t) {
-        float mx = 0.f;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, fabsf(r[e]));
-        const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF);
-        // term scale 2^(E-129): the block max maps into [4, 8) (6 is e2m1's top)
-        const int sb = (mx == 0.f || E == 0xFF) ? 127 : max(E - 2, 1);
-        const float inv = __uint_as_float((uint32_t)(254 - sb) << 23);  // 2^-(sb-127)
-        const float scl = __uint_as_float((uint32_t)sb << 23);          // 2^(sb-127)
-        uint32_t w4[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint32_t word = 0;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int k = 8 * q + 2 * e;
-            const uint32_t code = e2m1x2(r[k] * inv, r[k + 1] * inv);
-            const float2 v = e2m1x2_val(code);
-            r[k] = fmaf(-v.x, scl, r[k]);
-            r[k + 1] = fmaf(-v.y, scl, r[k + 1]);
-            word |= code << (8 * e);
-          }
-          w4[q] = word;
-        }
-        const int n = 8 * t + m;  // B row
-        *reinterpret_cast<uint4*>(bj + n * 128 + ((kb8 ^ (n & 7)) << 4)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-        sfb[(size_t)(2 * j + (kb8 >> 2)) * kAtom + 16 * n + (kb8 & 3)] = (uint8_t)sb;
-      }
-    }
+    // 1, 2 or 4 threads per 32-element block of one activation row: enough
+    // independent blocks per thread when x is long, more threads per block
+    // (the block maximum reduced across them) when it is short
+    const int blocks = a.M * ns * 8;
+    if (blocks >= 128)
+      split_terms<1, S>(a, et, s_begin, ns, xb, sfb);
+    else if (blocks >= 64)
+      split_terms<2, S>(a, et, s_begin, ns, xb, sfb);
+    else
+      split_terms<4, S>(a, et, s_begin, ns, xb, sfb);
     tc::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&x_ready);
 
-    // per tile: sum the four term columns of each activation row -> partial
+    // per tile: sum the four term columns of each activation row and hand the
+    // partial to the tile's finishing rank (i % ksz): its own receive slot, or a
+    // peer's through st.async counted on the peer's recv_bar
+    if (ksz > 1) cluster_wait();  // every peer's recv_bar is initialised
+    const uint32_t rbar_local = smem_u32(&recv_bar);
     bool failed = false;
-    for (int i = 0; i < my_tiles && ns > 0; ++i) {
-      const int b = i & 1;
-      if (!failed) failed = !mbar_wait_bounded(&d_full[b], (i >> 1) & 1);
-      tc::fence_after_sync();
-      float d[32];
-      tc::ld32_wait(tbase + 32 * b + ((uint32_t)(32 * (warp & 3)) << 16), d);
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&d_free[b]);
-      float* pr = part + (size_t)i * a.M * kTile + row;
+    for (int i = 0; i < my_tiles; ++i) {
+      float v[S];
 #pragma unroll
-      for (int m = 0; m < kMaxM; ++m)
-        if (m < a.M) pr[m * kTile] = (d[m] + d[8 + m]) + (d[16 + m] + d[24 + m]);
+      for (int m = 0; m < S; ++m) v[m] = 0.f;
+      if (ns > 0) {
+        const int b = i & 1;
+        if (!failed) failed = !mbar_wait_bounded(&d_full[b], (i >> 1) & 1);
+        tc::fence_after_sync();
+        float d[32];
+        tc::ld32_wait(tbase + 32 * b + ((uint32_t)(32 * (warp & 3)) << 16), d);
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&d_free[b]);
+#pragma unroll
+        for (int m = 0; m < S; ++m) v[m] = (d[m] + d[S + m]) + (d[2 * S + m] + d[3 * S + m]);
+      }
+      const int owner = i % ksz;
+      float* slot = recv + (((size_t)(i / ksz) * ksz + rank) * kTile + row) * a.M;
+      if (owner == rank) {
+#pragma unroll
+        for (int m = 0; m < S; ++m)
+          if (m < a.M) slot[m] = v[m];
+      } else {
+        const uint32_t raddr = map_to_rank(smem_u32(slot), owner);
+        const uint32_t rbar = map_to_rank(rbar_local, owner);
+#pragma unroll
+        for (int m = 0; m < S; ++m)
+          if (m < a.M) st_async_f32(raddr + 4 * m, v[m], rbar);
+      }
     }
-    if (ns == 0)
-      for (int i = 0; i < my_tiles; ++i)
-        for (int m = 0; m < a.M; ++m) part[((size_t)i * a.M + m) * kTile + row] = 0.f;
+
+    // finish the owned tiles: fixed-order sum over the ranks' partials
+    griddep_wait();  // before any output store
+    if (owned > 0 && (recv_bytes == 0 || mbar_wait_bounded(&recv_bar, 0))) {
+      for (int t = 0; t < owned; ++t) {
+        const int n = (cid + (rank + t * ksz) * a.nclusters) * kTile + row;
+        const float* rs = recv + ((size_t)t * ksz * kTile + row) * a.M;
+        for (int m = 0; m < a.M; ++m) {
+          float acc = 0.f;
+          for (int q = 0; q < ksz; ++q) acc += rs[(size_t)q * kTile * a.M + m];
+          if (n < a.N) a.Out[(size_t)m * a.N + n] = __float2bfloat16_rn(acc);
+        }
+      }
+    }
   }
 
-  // ---- reduce the cluster's K-slices through distributed shared memory -----------
-  griddep_wait();  // every thread, before any output store (and before exit)
+  griddep_wait();  // every thread waits before exit
   tc::fence_before_sync();
-  cg::cluster_group cluster = cg::this_cluster();
-  cluster.sync();
-  const int ksz = (int)cluster.num_blocks();
-  for (int i = rank; i < my_tiles; i += ksz) {
-    const int row0 = (cid + i * a.nclusters) * kTile;
-    for (int e = tid; e < kTile * a.M; e += kThreads) {
-      const int m = e / kTile, r = e % kTile;
-      float v = 0.f;
-      for (int q = 0; q < ksz; ++q) v += cluster.map_shared_rank(part, q)[((size_t)i * a.M + m) * kTile + r];
-      const int n = row0 + r;
-      if (n < a.N) a.Out[(size_t)m * a.N + n] = __float2bfloat16_rn(v);
-    }
-  }
-  cluster.sync();
-  if (warp == 0) tc::tmem_dealloc(tbase, kTmemCols);
+  __syncthreads();  // all tensor-memory reads are done
+  if (warp == 0) tc::tmem_dealloc(tbase, tmem_cols);
 }
 
 // Scale packer: S (layout 0: [N, K/32] transposed, 1: [K/32, N] checkpoint) ->
@@ -382,24 +514,25 @@ __global__ void pack_scales_kernel(const uint8_t* __restrict__ S, int layout, ui
   if (e) atomicExch(edge, 1);
 }
 
-// The kernel's dynamic shared-memory limit, raised on demand (per process; the
-// attribute is per function, the same value on every device).
+// The kernel's dynamic shared-memory limit, raised on demand (per process and
+// instantiation; the attribute is per function, the same value on every device).
+template <int S>
 cudaError_t raise_smem_limit(size_t smem) {
   static std::mutex mu;
   static size_t limit = 0;
   std::lock_guard<std::mutex> g(mu);
   if (smem <= limit) return cudaSuccess;
-  const cudaError_t e = cudaFuncSetAttribute(mxfp4_mma_kernel<kMaxM>,
+  const cudaError_t e = cudaFuncSetAttribute(mxfp4_mma_kernel<S>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) limit = smem;
   return e;
 }
 
-template <int MAXM>
+template <int S>
 cudaError_t launch_mma(const CUtensorMap& wm, const MmaArgs& a, int ks, cudaStream_t st) {
-  const MmaLayout L{a.sps, a.tmax, a.nstages};
+  const MmaLayout L{a.sps, a.tmax, a.nstages, ks, S};
   const size_t smem = L.bytes(a.M);
-  const cudaError_t e = raise_smem_limit(smem);
+  const cudaError_t e = raise_smem_limit<S>(smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ks, a.nclusters, 1);
@@ -415,10 +548,8 @@ cudaError_t launch_mma(const CUtensorMap& wm, const MmaArgs& a, int ks, cudaStre
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, mxfp4_mma_kernel<MAXM>, wm, a);
+  return cudaLaunchKernelEx(&cfg, mxfp4_mma_kernel<S>, wm, a);
 }
-
-int max_active_clusters(int ks, size_t smem);
 
 int env_or(const char* name, int dflt) {
   const char* v = getenv(name);
@@ -438,7 +569,7 @@ int max_active_clusters(int ks, size_t smem) {
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  if (raise_smem_limit(smem) != cudaSuccess) {
+  if (raise_smem_limit<kMaxM>(smem) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
@@ -510,18 +641,22 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
   // and the plan minimises the per-cluster work, tiles x steps per slice.
   const int force_ks = env_or("B200KV_MMA_KSPLIT", 0);
   const int force_st = env_or("B200KV_MMA_STAGES", 0);
+  const int S = M <= 2 ? 2 : (M <= 4 ? 4 : 8);  // term stride: N = 4 S
   int best_ks = 1, best_st = 4, best_nc = 1;
   double best_cost = 1e30;
   for (int ks = 1; ks <= 8; ++ks) {
     if (force_ks && ks != force_ks) continue;
     if (ks > a.nsteps) break;
     const int sps = cdiv(a.nsteps, ks);
-    for (int nst : {2, 3}) {
-      if (force_st && nst != force_st) continue;
+    for (int nst0 : {2, 3}) {
+      if (force_st && nst0 != force_st) continue;
       const int nc0 = max(1, min(a.ntiles, sms / ks));
       const int tslots = cdiv(a.ntiles, nc0) + 1;
       if (sps > kMaxSliceBoxes) continue;
-      const size_t smem = MmaLayout{sps, tslots, nst}.bytes(M);
+      // no more ring stages than a CTA ever fills (a small footprint lets the
+      // next kernel's CTAs share the SM and start streaming early)
+      const int nst = min(nst0, cdiv(a.ntiles, nc0) * cdiv(sps, kBoxesPerStage));
+      const size_t smem = MmaLayout{sps, tslots, nst, ks, S}.bytes(M);
       if (smem > 227 * 1024) continue;
       const int nc = min(a.ntiles, min(nc0, max_active_clusters(ks, smem)));
       if (nc <= 0) continue;
@@ -552,7 +687,9 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
   CUtensorMap wm;
   if (!encode_u8_2d(&wm, W, (uint64_t)(K / 2), (uint64_t)N, (uint64_t)(K / 2), 128, kTile, true))
     return B200KV_ERR_UNSUPPORTED;
-  const cudaError_t e = launch_mma<kMaxM>(wm, a, ks, static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = S == 2 ? launch_mma<2>(wm, a, ks, st)
+                               : (S == 4 ? launch_mma<4>(wm, a, ks, st) : launch_mma<8>(wm, a, ks, st));
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;
 }
 
