@@ -42,13 +42,22 @@ def gemv_bytes(N, K, M):
     return N * K // 2 + N * K // 32 + 2 * M * K + 2 * M * N
 
 
-def decode_bytes(B, ctx):
-    """Algorithmic bytes of one decode-attention call: fp8 K+V, q, out, block table, lens."""
-    return B * (2 * ctx * HKV * D + HQ * D * 2 * 2 + (ctx // PBLK) * 4 + 8)
+def decode_bytes(B, ctx, tp=1):
+    """Algorithmic bytes of one decode-attention call (one rank's kv heads under
+    tensor parallelism): fp8 K+V, q, out, block table, lens."""
+    return B * (2 * ctx * (HKV // tp) * D + (HQ // tp) * D * 2 * 2 + (ctx // PBLK) * 4 + 8)
 
 
 def layer_bytes(B, ctx):
     return sum(gemv_bytes(N, K, B) for _, N, K in SHAPES) + decode_bytes(B, ctx)
+
+
+def rank_shapes(tp):
+    """(name, N, K) of one rank's MXFP4 linears under tensor parallelism over tp
+    ranks: qkv and gate_up column-parallel (N / tp), o and down row-parallel
+    (K / tp, followed by an allreduce of the [B, 4096] partials)."""
+    return tuple((name, N // tp if name in ("qkv", "gate_up") else N,
+                  K if name in ("qkv", "gate_up") else K // tp) for name, N, K in SHAPES)
 
 
 def workload_config(args):
@@ -59,7 +68,9 @@ def workload_config(args):
             "mxfp4_kernel": ("block-scaled tcgen05 (kind::mxf4), scales packed at load"
                              if args.gemv == "tc" else "CUDA-core mma.sync"),
             "l2": "inputs larger than L2 (distinct weights/KV per layer), no flush",
-            "parallelism": f"replicas x{args.gpus}"}
+            "parallelism": (f"tp{args.tp}: attention by kv head, qkv/gate_up column-parallel, "
+                            f"o/down row-parallel + {args.allreduce} allreduce (in the CUDA graph)"
+                            if args.tp > 1 else f"replicas x{args.gpus}")}
 
 
 # ---------------------------------------------------------------------------
@@ -126,13 +137,14 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 def build_model(args, dev):
     """Random-init weights and KV pools for `layers` layers on `dev`."""
-    B, ctx, L = args.batch, args.ctx, args.layers
+    B, ctx, L, tp = args.batch, args.ctx, args.layers, args.tp
+    hkv = HKV // tp  # this rank's kv heads
     g = torch.Generator(device=dev).manual_seed(1234 + args.rank)
     layers = []
     nblk = ctx // PBLK
     for _ in range(L):
         lay = {}
-        for name, N, K in SHAPES:
+        for name, N, K in rank_shapes(tp):
             W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
             St = torch.randint(119, 126, (N, K // 32), dtype=torch.uint8, device=dev, generator=g)
             if args.gemv == "tc":  # load-time repack of the scales into tensor-core atoms
@@ -143,11 +155,11 @@ def build_model(args, dev):
             else:
                 lay[name] = (W, St)
         nb = B * nblk
-        kf = torch.randn(nb, PBLK, HKV, D, device=dev, generator=g)
+        kf = torch.randn(nb, PBLK, hkv, D, device=dev, generator=g)
         ks = kf.abs().max() / 448.0
         lay["k"] = (kf / ks).to(torch.float8_e4m3fn)
         del kf
-        vf = torch.randn(nb, PBLK, HKV, D, device=dev, generator=g)
+        vf = torch.randn(nb, PBLK, hkv, D, device=dev, generator=g)
         vs = vf.abs().max() / 448.0
         lay["v"] = (vf / vs).to(torch.float8_e4m3fn)
         del vf
@@ -155,13 +167,13 @@ def build_model(args, dev):
         lay["vs"] = vs.reshape(1).float()
         lay["bt"] = torch.randperm(nb, device=dev, generator=g).to(torch.int32).view(B, nblk)
         lay["x"] = torch.randn(B, 4096, device=dev, generator=g).to(torch.bfloat16)
-        lay["act"] = torch.randn(B, 14336, device=dev, generator=g).to(torch.bfloat16)
+        lay["act"] = torch.randn(B, 14336 // tp, device=dev, generator=g).to(torch.bfloat16)
         layers.append(lay)
     bufs = {
-        "qkv": torch.empty(B, 6144, dtype=torch.bfloat16, device=dev),
-        "attn": torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev),
+        "qkv": torch.empty(B, 6144 // tp, dtype=torch.bfloat16, device=dev),
+        "attn": torch.empty(B, HQ // tp, D, dtype=torch.bfloat16, device=dev),
         "o": torch.empty(B, 4096, dtype=torch.bfloat16, device=dev),
-        "gate_up": torch.empty(B, 28672, dtype=torch.bfloat16, device=dev),
+        "gate_up": torch.empty(B, 28672 // tp, dtype=torch.bfloat16, device=dev),
         "down": torch.empty(B, 4096, dtype=torch.bfloat16, device=dev),
         "qsl": torch.arange(B + 1, dtype=torch.int32, device=dev),
         "slens": torch.full((B,), ctx, dtype=torch.int32, device=dev),
@@ -169,26 +181,34 @@ def build_model(args, dev):
     return layers, bufs
 
 
-def run_step(layers, bufs, args, which=("gemv", "attn")):
+def run_step(layers, bufs, args, which=("gemv", "attn", "comm")):
     """One hot-path step through the public API (h4mv.mxfp4_gemm or
-    h4mv.mxfp4_gemv, fp8kv_v3.run)."""
+    h4mv.mxfp4_gemv, fp8kv_v3.run); under tensor parallelism the o and down
+    partials are summed over the ranks (tp.allreduce_)."""
     import fp8kv_v3
     import h4mv
+    import tp
     B = args.batch
+    hq = HQ // args.tp
     sm = D ** -0.5
     gemv = h4mv.mxfp4_gemm if args.gemv == "tc" else h4mv.mxfp4_gemv
-    do_g, do_a = "gemv" in which, "attn" in which
+    do_g, do_a, do_c = "gemv" in which, "attn" in which, "comm" in which and args.tp > 1
     for lay in layers:
         if do_g:
             gemv(lay["x"], *lay["qkv"], out=bufs["qkv"])
         if do_a:
-            q = bufs["qkv"][:, :HQ * D].unflatten(1, (HQ, D))
+            q = bufs["qkv"][:, :hq * D].unflatten(1, (hq, D))
             fp8kv_v3.run(q, lay["k"], lay["v"], bufs["attn"], bufs["qsl"], bufs["slens"], lay["bt"],
                          lay["ks"], lay["vs"], sm, max_seq_len=args.ctx)
         if do_g:
-            gemv(bufs["attn"].view(B, HQ * D), *lay["o"], out=bufs["o"])
+            gemv(bufs["attn"].view(B, hq * D), *lay["o"], out=bufs["o"])
+        if do_c:
+            args.allreduce_fn(bufs["o"])
+        if do_g:
             gemv(bufs["o"], *lay["gate_up"], out=bufs["gate_up"])
             gemv(lay["act"], *lay["down"], out=bufs["down"])
+        if do_c:
+            args.allreduce_fn(bufs["down"])
 
 
 def capture(fn):
@@ -350,6 +370,7 @@ def run_b200(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     args.rank = rank
     dist_on = world > 1
+    args.tp = world if dist_on and args.parallel == "tp" else 1
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     barrier = None
@@ -362,12 +383,23 @@ def run_b200(args):
         barrier = dist.barrier
 
     layers, bufs = build_model(args, dev)
+    comm = None
+    if args.tp > 1:
+        import tp
+        if args.allreduce == "peer":
+            comm = tp.PeerAllreduce()
+            args.allreduce_fn = comm
+        else:
+            args.allreduce_fn = tp.allreduce_
+    # the model's algorithmic bytes per step (one GPU's worth under tp: the
+    # shards partition it; replicas each stream a full copy)
     step_bytes = args.layers * layer_bytes(args.batch, args.ctx)
     launches_per_step = args.layers * 5
 
     g_step = capture(lambda: run_step(layers, bufs, args))
     g_gemv = capture(lambda: run_step(layers, bufs, args, which=("gemv",)))
     g_attn = capture(lambda: run_step(layers, bufs, args, which=("attn",)))
+    g_comm = capture(lambda: run_step(layers, bufs, args, which=("comm",))) if args.tp > 1 else None
 
     # ---- timed region: whole steps (graph replay), clocks sampled meanwhile --
     clocks = ClockSampler(local)
@@ -379,15 +411,18 @@ def run_b200(args):
     # ---- per-kernel breakdown (same graphs, kernel class alone) ------------
     ms_gemv = max_over_ranks(time_graph(g_gemv, args.steps, 2, barrier), dist_on, dev)
     ms_attn = max_over_ranks(time_graph(g_attn, args.steps, 2, barrier), dist_on, dev)
+    ms_comm = (max_over_ranks(time_graph(g_comm, args.steps, 2, barrier), dist_on, dev)
+               if g_comm is not None else None)
     us_pre, flops_pre = prefill_part(dev, args.steps, 2, barrier)
     us_pre = max_over_ranks(us_pre, dist_on, dev)
-    gemv_bytes_step = args.layers * sum(gemv_bytes(N, K, args.batch) for _, N, K in SHAPES)
-    attn_bytes_step = args.layers * decode_bytes(args.batch, args.ctx)
+    # one rank's bytes (the per-GPU roofline)
+    gemv_bytes_step = args.layers * sum(gemv_bytes(N, K, args.batch) for _, N, K in rank_shapes(args.tp))
+    attn_bytes_step = args.layers * decode_bytes(args.batch, args.ctx, args.tp)
 
     # ---- e2e through the public API with host buffers ----------------------
     B = args.batch
     h_x = torch.randn(args.layers, B, 4096).to(torch.bfloat16).pin_memory()
-    h_act = torch.randn(args.layers, B, 14336).to(torch.bfloat16).pin_memory()
+    h_act = torch.randn(args.layers, B, 14336 // args.tp).to(torch.bfloat16).pin_memory()
     d_x = torch.stack([lay["x"] for lay in layers])  # staging views refreshed per step
     d_act = torch.stack([lay["act"] for lay in layers])
     for i, lay in enumerate(layers):
@@ -395,7 +430,7 @@ def run_b200(args):
         lay["act"] = d_act[i]
     g_e2e = capture(lambda: run_step(layers, bufs, args))
     h_out = torch.empty(B, 4096, dtype=torch.bfloat16).pin_memory()
-    h_attn = torch.empty(B, HQ, D, dtype=torch.bfloat16).pin_memory()
+    h_attn = torch.empty(B, HQ // args.tp, D, dtype=torch.bfloat16).pin_memory()
     h2d = h_x.numel() * 2 + h_act.numel() * 2
     d2h = h_out.numel() * 2 + h_attn.numel() * 2
 
@@ -436,21 +471,23 @@ def run_b200(args):
     # 7B shapes at M = 1: 13.43, 8.97, 62.72 and 31.27 MB for qkv, o,
     # gate_up and down.  Other configurations have no capture.
     traffic, traffic_src = None, None
-    if args.gemv == "tc" and args.batch == 1:
+    if args.gemv == "tc" and args.batch == 1 and args.tp == 1:
         traffic = (13.43 + 8.97 + 62.72 + 31.27) / 4 * 1e6
         traffic_src = "ncu dram__bytes_read+write of the four shapes at M=1, averaged"
 
     result = None
     if rank == 0:
         cpu = cpu_baseline(args) if world == 1 else None
-        value = world * step_bytes / (ms * 1e-3) / 1e9
+        copies = world // args.tp  # full model copies streamed per step
+        value = copies * step_bytes / (ms * 1e-3) / 1e9
         result = {
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if args.tp > 1 else "weak",
+            "vs_baseline": None,
             "dtype": "e2m1/e4m3 operands, f32 accumulate",
             "data": "synthetic", "config": workload_config(args),
-            "tok_s_hot_path_only": world * args.batch / (ms * 1e-3),
+            "tok_s_hot_path_only": copies * args.batch / (ms * 1e-3),
             "parts": {
                 "mxfp4_gemv": {"us_per_step": ms_gemv * 1e3, "launches_per_step": n_gemv,
                                "gbs": gemv_gbs, "kernel": args.gemv},
@@ -463,7 +500,8 @@ def run_b200(args):
                                  "bound": "tensor", "peak_tflops": peaks.get("bf16_tflops", 1590.0),
                                  "frac": flops_pre / (us_pre * 1e-6) / 1e12
                                  / peaks.get("bf16_tflops", 1590.0),
-                                 "note": "timed outside the decode step (not part of value)"},
+                                 "note": "timed outside the decode step (not part of value); "
+                                         "each rank runs the full call"},
             },
             "roofline": {"bound": "hbm",
                          "kernel": "mxfp4_mma_kernel" if args.gemv == "tc" else "mxfp4_gemv_kernel",
@@ -474,7 +512,7 @@ def run_b200(args):
                          "traffic": traffic,
                          "traffic_source": traffic_src},
             "cpu_baseline": cpu,
-            "e2e": {"value": world * step_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
+            "e2e": {"value": copies * step_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "pinned host activations -> H2D, graph of public-API calls "
                             f"(h4mv.{'mxfp4_gemm' if args.gemv == 'tc' else 'mxfp4_gemv'}, "
@@ -482,11 +520,23 @@ def run_b200(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if ms_comm is not None:
+            result["parts"]["allreduce"] = {
+                "us_per_step": ms_comm * 1e3, "calls_per_step": 2 * args.layers,
+                "us_per_call": ms_comm * 1e3 / (2 * args.layers),
+                "bytes_per_call": args.batch * 4096 * 2,
+                "impl": ("b200kv one-shot peer-memory allreduce (NVLink stores + flags)"
+                         if args.allreduce == "peer" else "NCCL all_reduce (torch.distributed)")}
+            result["parts"]["mxfp4_gemv"]["note"] = "one rank's shards; gbs is per GPU"
+            result["parts"]["decode_attn"]["note"] = "one rank's kv heads; gbs is per GPU"
         print(json.dumps(result), flush=True)
-    del g_step, g_gemv, g_attn, g_e2e
+    del g_step, g_gemv, g_attn, g_e2e, g_comm  # graphs holding NCCL calls go first
     if dist_on:
         import torch.distributed as dist
+        torch.cuda.synchronize()
         dist.barrier()
+        if comm is not None:
+            comm.close()
         dist.destroy_process_group()
     return result
 
@@ -502,11 +552,17 @@ def main():
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--parallel", choices=("tp", "replicas"), default="tp",
+                    help="N > 1: tensor parallelism over the N GPUs (default) or N full replicas")
+    ap.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
+                    help="tensor-parallel allreduce: b200kv's peer-memory kernel or NCCL")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
                     help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 300 if args.impl == "b200" else 10
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    args.tp = world if world > 1 and args.parallel == "tp" else 1
     args.warmup = max(args.warmup, 3) if args.impl == "b200" else args.warmup
     args.rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

@@ -57,6 +57,19 @@ lib.b200kv_decode_attn.argtypes = (
      _i32, _i32, _i32,                # kv_dtype, out_by_qsl, num_splits
      _vp])                            # stream
 
+lib.b200kv_comm_buffer_bytes.restype = ctypes.c_size_t
+lib.b200kv_comm_buffer_bytes.argtypes = []
+lib.b200kv_comm_alloc.restype = _i32
+lib.b200kv_comm_alloc.argtypes = [ctypes.POINTER(ctypes.c_void_p), _vp]
+lib.b200kv_comm_open.restype = _i32
+lib.b200kv_comm_open.argtypes = [_vp, ctypes.POINTER(ctypes.c_void_p)]
+lib.b200kv_comm_close.restype = _i32
+lib.b200kv_comm_close.argtypes = [_vp]
+lib.b200kv_comm_free.restype = _i32
+lib.b200kv_comm_free.argtypes = [_vp]
+lib.b200kv_allreduce_oneshot.restype = _i32
+lib.b200kv_allreduce_oneshot.argtypes = [_vp, _vp, _i32, ctypes.POINTER(ctypes.c_void_p), _i32, _i32, _vp]
+
 lib.b200kv_prefill_attn.restype = _i32
 lib.b200kv_prefill_attn.argtypes = (
     [_vp, _i64, _i64,                 # q, strides

@@ -13,6 +13,7 @@ enum DeviceStatus : int {
   kDevOk = 0,
   kDevMbarrierTimeout = 0x101,   // a bulk copy never completed on its mbarrier
   kDevSplitOverflow = 0x102,     // seq_len larger than the context bound given
+  kDevPeerTimeout = 0x103,       // a peer GPU's flag did not arrive in time
 };
 extern __device__ int g_device_status;
 

@@ -57,6 +57,13 @@ bool pdl_enabled() {
 
 int mxfp4_gemv_launch(const void* W, const void* St, const void* X, void* out, int N, int K,
                       int M, void* stream);
+size_t comm_buffer_bytes();
+int comm_alloc(void** buf, void* ipc_handle);
+int comm_open(const void* ipc_handle, void** peer);
+int comm_close(void* peer);
+int comm_free(void* buf);
+int allreduce_oneshot_launch(const void* in, void* out, int n, void* const* bufs, int rank, int tp,
+                             void* stream);
 int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                        const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
                        int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
@@ -205,3 +212,16 @@ int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_
 }
 
 }  // extern "C"
+
+// ---- tensor-parallel allreduce over peer memory ------------------------------------
+extern "C" size_t b200kv_comm_buffer_bytes(void) { return b200kv::comm_buffer_bytes(); }
+extern "C" int b200kv_comm_alloc(void** buf, void* ipc_handle) { return b200kv::comm_alloc(buf, ipc_handle); }
+extern "C" int b200kv_comm_open(const void* ipc_handle, void** peer_buf) {
+  return b200kv::comm_open(ipc_handle, peer_buf);
+}
+extern "C" int b200kv_comm_close(void* peer_buf) { return b200kv::comm_close(peer_buf); }
+extern "C" int b200kv_comm_free(void* buf) { return b200kv::comm_free(buf); }
+extern "C" int b200kv_allreduce_oneshot(const void* in, void* out, int n, void* const* bufs, int rank,
+                                        int tp, void* stream) {
+  return b200kv::allreduce_oneshot_launch(in, out, n, bufs, rank, tp, stream);
+}

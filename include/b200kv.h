@@ -53,10 +53,14 @@ const char* b200kv_status_string(int status);
 int b200kv_last_error(void);
 
 /*
- * Device-side status word written by kernels that hit a bounded wait limit
- * (an mbarrier that never completed).  0 = clean.  Reading it synchronises
- * the given stream.  b200kv_reset_device_status() clears it (async on stream).
+ * Device-side status word written by kernels that hit a bounded wait limit.
+ * 0 = clean; B200KV_DEV_MBARRIER_TIMEOUT: an mbarrier (a copy or a peer warp)
+ * never completed; B200KV_DEV_PEER_TIMEOUT: a peer GPU's allreduce flag did not
+ * arrive.  Reading it synchronises the given stream.
+ * b200kv_reset_device_status() clears it (async on stream).
  */
+#define B200KV_DEV_MBARRIER_TIMEOUT 0x101
+#define B200KV_DEV_PEER_TIMEOUT     0x103
 int b200kv_get_device_status(void* stream, int* status_out);
 int b200kv_reset_device_status(void* stream);
 
@@ -223,6 +227,28 @@ int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_
                     const int64_t* slot_mapping, const float* k_scale, const float* v_scale,
                     int num_tokens, int num_kv_heads, int head_dim, int block_size,
                     int kv_dtype, void* stream);
+
+/* ---- Tensor-parallel allreduce over peer memory ---------------------------------
+ *
+ * Sum of a bf16 vector of n elements (n % 8 == 0, n <= 32768: one [M <= 8, 4096]
+ * partial of the row-parallel o / down projections) over tp <= 8 GPUs of one
+ * node, one rank per GPU, through NVLink peer stores and flags -- the
+ * collective of the tensor-parallel layout (no counterpart in the reference,
+ * which runs on one GPU).  Each rank allocates one communication buffer
+ * (b200kv_comm_alloc, 64-byte CUDA IPC handle out), exchanges the handles over
+ * any host channel, opens the peers' (b200kv_comm_open; its own stays as
+ * allocated) and passes all tp buffer pointers, in rank order, to every call.
+ * All ranks must make the same sequence of calls; a call waits at most 200 ms
+ * for the peers and then reports B200KV_DEV_PEER_TIMEOUT through the device
+ * status word.  in == out is allowed.  Capturable in CUDA graphs.
+ */
+size_t b200kv_comm_buffer_bytes(void);
+int b200kv_comm_alloc(void** buf, void* ipc_handle64);
+int b200kv_comm_open(const void* ipc_handle64, void** peer_buf);
+int b200kv_comm_close(void* peer_buf);
+int b200kv_comm_free(void* buf);
+int b200kv_allreduce_oneshot(const void* in, void* out, int n, void* const* bufs, int rank, int tp,
+                             void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,95 @@
+"""The tensor-parallel one-shot allreduce (b200kv_allreduce_oneshot) on two
+B200s: two processes, one per GPU, exchange their IPC handles over an NCCL
+process group.  The result must equal, bit for bit on every rank, the rank-
+ordered fp32 sum of the bf16 partials rounded to bf16 -- over consecutive calls
+(both buffer parities), in place, for the decode sizes M = 1 and 8, and inside
+a replayed CUDA graph.  Skipped with fewer than two GPUs."""
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import PKG
+
+pytestmark = pytest.mark.gpu
+TP = 2
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _expected(parts):
+    acc = torch.zeros_like(parts[0], dtype=torch.float32)
+    for p in parts:
+        acc += p.float()
+    return acc.to(torch.bfloat16)
+
+
+def _rank_main(rank, port):
+    import sys
+    if PKG not in sys.path:
+        sys.path.insert(0, PKG)
+    import _b200kv
+    import tp
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=TP, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    ar = tp.PeerAllreduce()
+    try:
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        for n in (4096, 8 * 4096, 4096, 4096, 8 * 4096):  # both parities, two sizes
+            x = torch.randn(n, device=dev, generator=g).to(torch.bfloat16)
+            parts = [torch.empty_like(x) for _ in range(TP)]
+            dist.all_gather(parts, x)
+            want = _expected(parts)
+            y = ar(x.clone())
+            assert torch.equal(y, want), n
+        # captured in a CUDA graph, replayed: three calls per replay
+        bufs = [torch.empty(4096, dtype=torch.bfloat16, device=dev) for _ in range(3)]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for b in bufs:
+                ar(b.normal_())
+        torch.cuda.current_stream().wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for b in bufs:
+                ar(b)
+        for _ in range(2):
+            srcs = [torch.randn(4096, device=dev, generator=g).to(torch.bfloat16) for _ in bufs]
+            wants = []
+            for sbuf in srcs:
+                parts = [torch.empty_like(sbuf) for _ in range(TP)]
+                dist.all_gather(parts, sbuf)
+                wants.append(_expected(parts))
+            for b, sbuf in zip(bufs, srcs):
+                b.copy_(sbuf)
+            graph.replay()
+            torch.cuda.synchronize()
+            for b, w in zip(bufs, wants):
+                assert torch.equal(b, w)
+        del graph
+        torch.cuda.synchronize()
+        assert _b200kv.device_status() == 0
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        ar.close()
+        dist.destroy_process_group()
+
+
+def test_peer_allreduce_two_gpus():
+    if torch.cuda.device_count() < TP:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_rank_main, args=(_free_port(),), nprocs=TP, join=True)

@@ -113,3 +113,16 @@ def test_kv_write_argument_validation(b200):
     assert call(ks=None) == 1
     assert call(sk1=1000) == 3
     assert call(kst=1020) == 3
+
+
+def test_allreduce_argument_validation(b200):
+    lib = b200.lib
+    bufs = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+    A = 0x30000
+    assert lib.b200kv_allreduce_oneshot(None, A, 4096, bufs, 0, 2, None) == 1
+    assert lib.b200kv_allreduce_oneshot(A, A, 4096, bufs, 2, 2, None) == 1        # rank outside tp
+    assert lib.b200kv_allreduce_oneshot(A, A, 4096, bufs, 0, 9, None) == 1        # more than 8 ranks
+    assert lib.b200kv_allreduce_oneshot(A, A, 4100, bufs, 0, 2, None) == 2        # n % 8
+    assert lib.b200kv_allreduce_oneshot(A, A, 8 * 4096 + 8, bufs, 0, 2, None) == 2
+    assert lib.b200kv_allreduce_oneshot(A + 8, A, 4096, bufs, 0, 2, None) == 3    # 16-byte rule
+    assert lib.b200kv_comm_buffer_bytes() > 2 * 8 * 8 * 4096 * 2
