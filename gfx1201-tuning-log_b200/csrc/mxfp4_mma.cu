@@ -417,16 +417,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<uint32_t*>(sfb)[i] = 0x7F7F7F7Fu;
     named_bar_sync(1, 128);
     griddep_wait();  // x is the previous kernel's output
-    // 1, 2 or 4 threads per 32-element block of one activation row: enough
-    // independent blocks per thread when x is long, more threads per block
-    // (the block maximum reduced across them) when it is short
+    // 1, 2 or 4 threads per 32-element block of one activation row: the most
+    // threads per block (shorter dependency chains, the block maximum reduced
+    // across them) that still needs the fewest rounds of the 128 threads
     const int blocks = a.M * ns * 8;
-    if (blocks >= 128)
-      split_terms<1, S>(a, et, s_begin, ns, xb, sfb);
-    else if (blocks >= 64)
+    const int rounds1 = (blocks + 127) / 128;
+    if ((4 * blocks + 127) / 128 == rounds1)
+      split_terms<4, S>(a, et, s_begin, ns, xb, sfb);
+    else if ((2 * blocks + 127) / 128 == rounds1)
       split_terms<2, S>(a, et, s_begin, ns, xb, sfb);
     else
-      split_terms<4, S>(a, et, s_begin, ns, xb, sfb);
+      split_terms<1, S>(a, et, s_begin, ns, xb, sfb);
     tc::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(&x_ready);
