@@ -295,6 +295,44 @@ def prefill_part(dev, steps, warmup, barrier=None):
     return ms * 1e3, prefill_flops(lens)
 
 
+DECODE_PROMPT, DECODE_TOKENS = 4096, 256
+
+
+def decode_7b_part(args, dev, barrier, allreduce):
+    """Config 4: the full 7B MXFP4 decoder (decoder.py) decoding DECODE_TOKENS
+    greedy tokens per sequence after a DECODE_PROMPT-token prompt, batch
+    args.batch, one CUDA-graph replay per token.  The prompt's KV pages are
+    synthetic (random fp8 of the cache's scale), not computed: the decode cost
+    depends only on their length; the prefill kernel is timed as config 3.
+    Returns (ms per token step, tokens/s over the whole batch)."""
+    import decoder
+    cfg = decoder.SEVEN_B
+    B = args.batch
+    gather = None
+    if args.tp > 1:
+        import torch.distributed as dist
+
+        def gather(out, inp):
+            dist.all_gather_into_tensor(out.view(-1), inp.contiguous().view(-1))
+    dec = decoder.MXFP4Decoder(cfg, dev, B, DECODE_PROMPT + DECODE_TOKENS + 16, seed=7, tp=args.tp,
+                               rank=args.rank, allreduce=allreduce, gather=gather)
+    g = torch.Generator(device=dev).manual_seed(11 + args.rank)
+    npb = DECODE_PROMPT // cfg.block_size
+    for kv in dec.kv:  # prompt pages of every sequence
+        for name in ("k", "v"):
+            pages = kv[name].view(B, dec.maxblk, *kv[name].shape[1:])[:, :npb]
+            pages.copy_((torch.randn(pages.shape, device=dev, generator=g) * 4).to(torch.float8_e4m3fn))
+    dec.positions.fill_(DECODE_PROMPT)
+    dec.tokens.copy_(torch.randint(0, cfg.vocab, (B,), device=dev, generator=g))
+    dec.step()
+    dec.step()
+    graph = capture(dec.step)
+    steps = min(DECODE_TOKENS - 3, args.steps)
+    ms = time_graph(graph, steps, 1, barrier)
+    del graph
+    return ms, B / (ms * 1e-3)
+
+
 def max_over_ranks(x, dist_on, dev):
     if not dist_on:
         return x
@@ -415,6 +453,8 @@ def run_b200(args):
                if g_comm is not None else None)
     us_pre, flops_pre = prefill_part(dev, args.steps, 2, barrier)
     us_pre = max_over_ranks(us_pre, dist_on, dev)
+    ms_tok, _ = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None)
+    ms_tok = max_over_ranks(ms_tok, dist_on, dev)
     # one rank's bytes (the per-GPU roofline)
     gemv_bytes_step = args.layers * sum(gemv_bytes(N, K, args.batch) for _, N, K in rank_shapes(args.tp))
     attn_bytes_step = args.layers * decode_bytes(args.batch, args.ctx, args.tp)
@@ -502,6 +542,14 @@ def run_b200(args):
                                  / peaks.get("bf16_tflops", 1590.0),
                                  "note": "timed outside the decode step (not part of value); "
                                          "each rank runs the full call"},
+                "decode_7b": {"workload": f"config 4: full 7B MXFP4 decoder (RMSNorm, qkv, RoPE + fp8 "
+                                          f"KV write, decode attention, o, SwiGLU MLP, bf16 lm_head "
+                                          f"128256, greedy argmax), batch {args.batch}, "
+                                          f"{DECODE_PROMPT}-token prompt (synthetic KV pages), "
+                                          f"tokens {DECODE_PROMPT}+; one CUDA-graph replay per token",
+                              "ms_per_token_step": ms_tok,
+                              "tok_s": copies * args.batch / (ms_tok * 1e-3),
+                              "note": "timed outside the hot-path step (not part of value)"},
             },
             "roofline": {"bound": "hbm",
                          "kernel": "mxfp4_mma_kernel" if args.gemv == "tc" else "mxfp4_gemv_kernel",

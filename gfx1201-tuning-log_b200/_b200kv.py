@@ -57,6 +57,17 @@ lib.b200kv_decode_attn.argtypes = (
      _i32, _i32, _i32,                # kv_dtype, out_by_qsl, num_splits
      _vp])                            # stream
 
+lib.b200kv_rmsnorm_residual.restype = _i32
+lib.b200kv_rmsnorm_residual.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]
+lib.b200kv_rope_kv_write.restype = _i32
+lib.b200kv_rope_kv_write.argtypes = (
+    [_vp, _i64, _vp, _vp, _i32, _vp,  # qkv, stride, positions, cos_sin, max_pos, slots
+     _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,  # caches, strides (elements)
+     _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32,  # scales, tokens, hq, hkv, d, block, kv dtype
+     _vp])
+lib.b200kv_swiglu.restype = _i32
+lib.b200kv_swiglu.argtypes = [_vp, _vp, _i32, _i32, _vp]
+
 lib.b200kv_comm_buffer_bytes.restype = ctypes.c_size_t
 lib.b200kv_comm_buffer_bytes.argtypes = []
 lib.b200kv_comm_alloc.restype = _i32

@@ -57,6 +57,14 @@ bool pdl_enabled() {
 
 int mxfp4_gemv_launch(const void* W, const void* St, const void* X, void* out, int N, int K,
                       int M, void* stream);
+int rmsnorm_residual_launch(void* h, const void* delta, const void* weight, void* x, int rows,
+                            int hidden, float eps, void* stream);
+int rope_kv_write_launch(void* qkv, int64_t qkv_st, const int32_t* positions, const float* cos_sin,
+                         int max_pos, const int64_t* slots, void* k_cache, void* v_cache,
+                         int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0, int64_t sv1,
+                         int64_t sv2, const float* k_scale, const float* v_scale, int num_tokens,
+                         int hq, int hkv, int head_dim, int block_size, int kv_dtype, void* stream);
+int swiglu_launch(const void* gate_up, void* act, int rows, int inter, void* stream);
 size_t comm_buffer_bytes();
 int comm_alloc(void** buf, void* ipc_handle);
 int comm_open(const void* ipc_handle, void** peer);
@@ -224,4 +232,25 @@ extern "C" int b200kv_comm_free(void* buf) { return b200kv::comm_free(buf); }
 extern "C" int b200kv_allreduce_oneshot(const void* in, void* out, int n, void* const* bufs, int rank,
                                         int tp, void* stream) {
   return b200kv::allreduce_oneshot_launch(in, out, n, bufs, rank, tp, stream);
+}
+
+// ---- decoder-layer glue ------------------------------------------------------------
+extern "C" int b200kv_rmsnorm_residual(void* h, const void* delta, const void* weight, void* x,
+                                       int rows, int hidden, float eps, void* stream) {
+  return b200kv::rmsnorm_residual_launch(h, delta, weight, x, rows, hidden, eps, stream);
+}
+extern "C" int b200kv_rope_kv_write(void* qkv, int64_t qkv_stride_tok, const int32_t* positions,
+                                    const float* cos_sin, int max_pos, const int64_t* slot_mapping,
+                                    void* k_cache, void* v_cache, int64_t sk0, int64_t sk1,
+                                    int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2,
+                                    const float* k_scale, const float* v_scale, int num_tokens,
+                                    int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                                    int kv_dtype, void* stream) {
+  return b200kv::rope_kv_write_launch(qkv, qkv_stride_tok, positions, cos_sin, max_pos, slot_mapping,
+                                      k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, k_scale, v_scale,
+                                      num_tokens, num_q_heads, num_kv_heads, head_dim, block_size,
+                                      kv_dtype, stream);
+}
+extern "C" int b200kv_swiglu(const void* gate_up, void* act, int rows, int inter, void* stream) {
+  return b200kv::swiglu_launch(gate_up, act, rows, inter, stream);
 }

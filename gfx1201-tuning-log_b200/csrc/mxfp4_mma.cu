@@ -64,16 +64,20 @@ constexpr int kTile = 128;             // weight rows per tile (MMA M)
 constexpr int kAtomK = 128;            // K covered by one scale atom (4 groups)
 constexpr int kStep = 256;             // K per W box (128 B rows): 2 atoms, 4 MMAs
 constexpr int kBoxesPerStage = 4;      // a stage reads 512 contiguous bytes of each row
-constexpr int kTerms = 4;              // e2m1 terms of x
-constexpr int kMaxM = 8;               // B rows (MMA N) = 4 * S: term p of row m at S*p + m
+constexpr int kTerms = 6;              // e2m1 terms of x
+constexpr int kMaxM = 8;               // activation rows; term p of row m is B row S*p + m
+// B rows (MMA N) for term stride S: kTerms * S rounded up to a multiple of 8
+__host__ __device__ constexpr int nb_rows(int S) { return (kTerms * S + 7) / 8 * 8; }
+// tensor-memory columns of one accumulator
+__host__ __device__ constexpr int d_cols(int S) { return nb_rows(S) <= 32 ? 32 : 64; }
 constexpr int kBox = kTile * 128;      // W box: 16 KB
 constexpr int kAtom = 512;
 constexpr int kStageBytes = kBoxesPerStage * (kBox + 2 * kAtom);  // 68 KB
 constexpr int kMaxStages = 3;
 constexpr int kThreads = 192;          // warp 0 TMA, warp 1 MMA, warps 2-5 x + epilogue
-// tensor memory: D[2][32] at 0..63, A scales of ring slot r at 64 + 32 r, the
-// activation scales at 64 + 32 nstages + 8 box; 256 columns, or 512 when that
-// does not fit (such CTAs are too large to share an SM anyway)
+// tensor memory: D[2][DC] at 0 and DC (DC = d_cols(S)), A scales of ring slot r
+// at 2 DC + 32 r, the activation scales at 2 DC + 32 nstages + 8 box; 256
+// columns, or 512 when that does not fit (such CTAs no longer share an SM)
 constexpr int kMaxSliceBoxes = 16;     // SFB of a K-slice stays in tensor memory: 8 columns a box
 
 struct MmaArgs {
@@ -94,7 +98,7 @@ struct MmaLayout {
   int sps, tmax, nstages, ks, S;  // S: B-row stride of the terms (M <= S, N = 4 S)
   __host__ __device__ int owned_max() const { return (tmax + ks - 1) / ks; }
   __host__ __device__ size_t xb() const { return (size_t)nstages * kStageBytes; }
-  __host__ __device__ size_t sfb() const { return xb() + (size_t)sps * 4 * S * 128; }
+  __host__ __device__ size_t sfb() const { return xb() + (size_t)sps * nb_rows(S) * 128; }
   __host__ __device__ size_t recv() const { return sfb() + (size_t)sps * 2 * kAtom; }
   __host__ __device__ size_t bytes(int m) const {
     return recv() + (size_t)owned_max() * ks * kTile * m * 4 + 1024;
@@ -174,7 +178,7 @@ __device__ __forceinline__ void split_terms(const MmaArgs& a, int et, int s_begi
                                             uint8_t* xb, uint8_t* sfb) {
   constexpr int EPT = 32 / TPB;
   constexpr int NV = EPT / 8;          // 16-byte loads per item
-  constexpr uint32_t kBBox = 4 * S * 128;
+  constexpr uint32_t kBBox = nb_rows(S) * 128;
   const int nblk = ns * 8;
   const int total = a.M * nblk * TPB;
   const int bound = (total + 31) & ~31;  // whole warps iterate together (shuffles)
@@ -246,7 +250,8 @@ __device__ __forceinline__ void split_terms(const MmaArgs& a, int et, int s_begi
           *reinterpret_cast<uint2*>(dst) = make_uint2(words[0], words[1]);
         else
           *reinterpret_cast<uint32_t*>(dst) = words[0];
-        if (q == 0) sfb[(size_t)(2 * j + (kb8 >> 2)) * kAtom + 16 * n + (kb8 & 3)] = (uint8_t)sb;
+        if (q == 0)  // scale-factor atom: byte 16 (n % 32) + 4 (n / 32) + group
+          sfb[(size_t)(2 * j + (kb8 >> 2)) * kAtom + 16 * (n & 31) + 4 * (n >> 5) + (kb8 & 3)] = (uint8_t)sb;
       }
     }
 #pragma unroll
@@ -259,7 +264,8 @@ __device__ __forceinline__ void split_terms(const MmaArgs& a, int et, int s_begi
 template <int S>
 __global__ void __launch_bounds__(kThreads, 1)
     mxfp4_mma_kernel(const __grid_constant__ CUtensorMap wmap, const MmaArgs a) {
-  constexpr int NB = 4 * S;                 // MMA N
+  constexpr int NB = nb_rows(S);            // MMA N
+  constexpr int DC = d_cols(S);
   constexpr uint32_t kBBox = NB * 128;      // B bytes per W box (K-major, 128-byte swizzle)
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
@@ -281,7 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sfb = dsm + L.sfb();
   float* recv = reinterpret_cast<float*>(dsm + L.recv());  // [owned_max][ksz][128][M]
   const uint32_t recv_bytes = (uint32_t)(owned * (ksz - 1) * kTile * a.M * 4);
-  const uint32_t tsfb_off = 64 + 32 * a.nstages;
+  const uint32_t tsfa_off = 2 * DC;
+  const uint32_t tsfb_off = 2 * DC + 32 * a.nstages;
   const uint32_t tmem_cols = tsfb_off + 8 * a.sps <= 256 ? 256 : 512;
 
   if (tid == 0) {
@@ -357,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait_bounded(&full_bar[slot], (s / a.nstages) & 1)) return false;
         const int nb = min(kBoxesPerStage, ns - (s % spt) * kBoxesPerStage);
         const uint32_t atoms = a_ring + (uint32_t)slot * kStageBytes + kBoxesPerStage * kBox;
-        const uint32_t tsfa = tbase + 64 + 32 * slot;
+        const uint32_t tsfa = tbase + tsfa_off + 32 * slot;
         for (int q = 0; q < 2 * nb; ++q) tmem_cp_atom(tsfa + 4 * q, sdesc_atom(atoms + (uint32_t)q * kAtom));
         return true;
       };
@@ -384,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int slot = s % a.nstages;
-        const uint32_t tsfa = tbase + 64 + 32 * slot;
+        const uint32_t tsfa = tbase + tsfa_off + 32 * slot;
         const uint32_t st = a_ring + (uint32_t)slot * kStageBytes;
-        const uint32_t tD = tbase + 32 * b;
+        const uint32_t tD = tbase + DC * b;
         const int b0 = t * kBoxesPerStage;
         const int nb = min(kBoxesPerStage, ns - b0);
         for (int q = 0; q < nb; ++q) {
@@ -446,13 +453,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = i & 1;
         if (!failed) failed = !mbar_wait_bounded(&d_full[b], (i >> 1) & 1);
         tc::fence_after_sync();
-        float d[32];
-        tc::ld32_wait(tbase + 32 * b + ((uint32_t)(32 * (warp & 3)) << 16), d);
+        float d0[32], d1[32];
+        const uint32_t tl = tbase + DC * b + ((uint32_t)(32 * (warp & 3)) << 16);
+        tc::ld32_wait(tl, d0);
+        if constexpr (DC == 64) tc::ld32_wait(tl + 32, d1);
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(&d_free[b]);
 #pragma unroll
-        for (int m = 0; m < S; ++m) v[m] = (d[m] + d[S + m]) + (d[2 * S + m] + d[3 * S + m]);
+        for (int m = 0; m < S; ++m) {
+          float acc = 0.f;
+#pragma unroll
+          for (int t = 0; t < kTerms; ++t) acc += S * t + m < 32 ? d0[S * t + m] : d1[S * t + m - 32];
+          v[m] = acc;
+        }
       }
       const int owner = i % ksz;
       float* slot = recv + (((size_t)(i / ksz) * ksz + rank) * kTile + row) * a.M;

@@ -1,0 +1,243 @@
+"""The 7B-class MXFP4 decoder of the reference's benchmarks (config 4), decode
+loop on b200kv's kernels.
+
+HF Llama layout: per layer RMSNorm -> fused qkv (MXFP4) -> rotary embedding +
+paged fp8 KV write -> decode attention -> o (MXFP4) -> residual + RMSNorm ->
+gate_up (MXFP4) -> SwiGLU -> down (MXFP4) -> residual; final RMSNorm, bf16
+lm_head, greedy argmax.  Random-init weights (config 2's MXFP4 distribution:
+codes uniform over the 16 values, e8m0 scales uniform in 2^-8..2^-2), bf16
+embeddings and lm_head.  Tensor parallel over `tp` ranks as in tp.py, the
+lm_head vocab-parallel with a (max, index) gather for the argmax.
+
+A decode step reads tokens, positions and the block tables from device
+tensors and advances them on the device, so it can be captured once in a CUDA
+graph and replayed token after token.
+"""
+from dataclasses import dataclass
+
+import torch
+
+import fp8kv_v3
+import h4mv
+from _b200kv import KV_BF16, KV_FP8_E4M3, check, lib
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    layers: int = 32
+    hidden: int = 4096
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    inter: int = 14336
+    vocab: int = 128256
+    rope_theta: float = 1e6
+    eps: float = 1e-5
+    block_size: int = 16
+
+
+SEVEN_B = DecoderConfig()
+
+
+def rope_table(max_pos, head_dim, theta):
+    """fp32 [max_pos, head_dim]: cos of the head_dim/2 rotary frequencies
+    theta^(-2i/head_dim), then their sin; angles in float64, rounded once."""
+    inv = theta ** (-torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim)
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cat([torch.cos(ang), torch.sin(ang)], 1).float()
+
+
+def _mxfp4(g, n, k, device):
+    W = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=device, generator=g)
+    St = torch.randint(119, 126, (n, k // 32), dtype=torch.uint8, device=device, generator=g)
+    return W, St
+
+
+def random_layer(cfg, li, seed, device="cpu"):
+    """Full (unsharded) weights of layer li: MXFP4 (W [N, K/2], St [N, K/32])
+    for qkv ([q | k | v] rows), o, gate_up ([gate | up] rows), down; bf16 norms.
+    Every rank draws the same layer from the same seed and keeps its shard."""
+    g = torch.Generator(device=device).manual_seed(seed * 1000 + li)
+    H, d = cfg.hidden, cfg.head_dim
+    nqkv = (cfg.heads + 2 * cfg.kv_heads) * d
+    lay = {"qkv": _mxfp4(g, nqkv, H, device), "o": _mxfp4(g, H, cfg.heads * d, device),
+           "gate_up": _mxfp4(g, 2 * cfg.inter, H, device), "down": _mxfp4(g, H, cfg.inter, device)}
+    for name in ("in_norm", "post_norm"):
+        lay[name] = (1.0 + 0.1 * torch.randn(H, device=device, generator=g)).to(torch.bfloat16)
+    return lay
+
+
+def random_head(cfg, seed, device="cpu"):
+    """bf16 embeddings, lm_head ~ N(0, 1) * 0.02 and 1.0 scale, final norm."""
+    g = torch.Generator(device=device).manual_seed(seed * 1000 + 999)
+    emb = (torch.randn(cfg.vocab, cfg.hidden, device=device, generator=g)).to(torch.bfloat16)
+    head = (0.02 * torch.randn(cfg.vocab, cfg.hidden, device=device, generator=g)).to(torch.bfloat16)
+    fnorm = (1.0 + 0.1 * torch.randn(cfg.hidden, device=device, generator=g)).to(torch.bfloat16)
+    return {"embed": emb, "lm_head": head, "final_norm": fnorm}
+
+
+def shard_layer(lay, cfg, rank, tp):
+    """This rank's shard of a full layer (tp.py's layout)."""
+    import tp as tpm
+    if tp == 1:
+        return dict(lay)
+    inter = cfg.inter
+    gu_rows = torch.cat([torch.arange(rank * inter // tp, (rank + 1) * inter // tp),
+                         inter + torch.arange(rank * inter // tp, (rank + 1) * inter // tp)])
+    W, St = lay["gate_up"]
+    gu_rows = gu_rows.to(W.device)
+    return {
+        "qkv": tpm.qkv_shard(*lay["qkv"], cfg.heads, cfg.kv_heads, cfg.head_dim, rank, tp),
+        "o": tpm.row_shard(*lay["o"], rank, tp),
+        "gate_up": (W.index_select(0, gu_rows).contiguous(), St.index_select(0, gu_rows).contiguous()),
+        "down": tpm.row_shard(*lay["down"], rank, tp),
+        "in_norm": lay["in_norm"], "post_norm": lay["post_norm"],
+    }
+
+
+def _linear(W, St, device, kernel="auto"):
+    """Weights on the device with their scales in the layout of the faster
+    kernel: tensor-core atoms when K % 256 == 0 and no edge byte, else (or
+    with kernel="mma.sync") the transposed scales of the mma.sync kernel."""
+    W = W.to(device).contiguous()
+    St = St.to(device).contiguous()
+    N, K = W.shape[0], W.shape[1] * 2
+    if K % 256 == 0 and kernel == "auto":
+        packed, edge = h4mv.pack_scales(St, N, K)
+        if not edge:
+            return ("tc", W, packed)
+    return ("mv", W, St)
+
+
+def _gemm(x, lin, out):
+    kind, W, S = lin
+    if kind == "tc":
+        return h4mv.mxfp4_gemm(x, W, S, out=out)
+    return h4mv.mxfp4_gemv(x, W, S, out=out)
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+class MXFP4Decoder:
+    """Decode loop of `batch` sequences with room for `max_ctx` tokens each.
+
+    tp/rank/allreduce: this rank's part of a tensor-parallel group (allreduce
+    sums a bf16 tensor in place over the group, e.g. tp.PeerAllreduce;
+    gather(out, inp) all-gathers a float32 tensor, for the argmax).  Weights are
+    drawn on `gen_device` (CPU in tests, so the oracle sees the same numbers)."""
+
+    def __init__(self, cfg, device, batch, max_ctx, seed=0, tp=1, rank=0, allreduce=None,
+                 gather=None, kv_scale=1.0 / 8, gen_device=None, layers=None, mxfp4_kernel="auto"):
+        self.cfg, self.dev, self.B, self.tp, self.rank = cfg, device, batch, tp, rank
+        self.allreduce = allreduce if allreduce is not None else (lambda t: t)
+        self.gather = gather
+        if cfg.heads % tp or cfg.kv_heads % tp or cfg.inter % tp or cfg.vocab % tp:
+            raise ValueError("model does not divide over tp")
+        self.hq, self.hkv = cfg.heads // tp, cfg.kv_heads // tp
+        gdev = gen_device if gen_device is not None else device
+        d, bs = cfg.head_dim, cfg.block_size
+        nlayers = cfg.layers if layers is None else layers
+        self.layers = []
+        for li in range(nlayers):
+            sh = shard_layer(random_layer(cfg, li, seed, gdev), cfg, rank, tp)
+            lin = lambda name: _linear(*sh[name], device, mxfp4_kernel)  # noqa: E731
+            self.layers.append({
+                "qkv": lin("qkv"), "o": lin("o"), "gate_up": lin("gate_up"), "down": lin("down"),
+                "in_norm": sh["in_norm"].to(device), "post_norm": sh["post_norm"].to(device)})
+        head = random_head(cfg, seed, gdev)
+        vl = cfg.vocab // tp
+        self.embed = head["embed"].to(device)
+        self.lm_head = head["lm_head"][rank * vl:(rank + 1) * vl].to(device).contiguous()
+        self.final_norm = head["final_norm"].to(device)
+        del head
+        # paged fp8 KV: sequence b owns blocks [b * maxblk, (b + 1) * maxblk)
+        self.maxblk = -(-max_ctx // bs)
+        nb = batch * self.maxblk
+        self.block_table = torch.arange(nb, dtype=torch.int32, device=device).view(batch, self.maxblk)
+        self.kv = []
+        for _ in range(nlayers):
+            self.kv.append({
+                "k": torch.zeros(nb, bs, self.hkv, d, dtype=torch.uint8, device=device).view(torch.float8_e4m3fn),
+                "v": torch.zeros(nb, bs, self.hkv, d, dtype=torch.uint8, device=device).view(torch.float8_e4m3fn),
+                "ks": torch.full((1,), kv_scale, dtype=torch.float32, device=device),
+                "vs": torch.full((1,), kv_scale, dtype=torch.float32, device=device)})
+        self.rope = rope_table(max_ctx, d, cfg.rope_theta).to(device)
+        self.max_ctx = max_ctx
+        # per-step state (device): next input tokens and their positions
+        self.tokens = torch.zeros(batch, dtype=torch.int64, device=device)
+        self.positions = torch.zeros(batch, dtype=torch.int32, device=device)
+        H, nqkv = cfg.hidden, (self.hq + 2 * self.hkv) * d
+        z = lambda *s: torch.zeros(*s, dtype=torch.bfloat16, device=device)  # noqa: E731
+        self.buf = {"h": z(batch, H), "x": z(batch, H), "qkv": z(batch, nqkv), "attn": z(batch, self.hq, d),
+                    "o": z(batch, H), "gu": z(batch, 2 * cfg.inter // tp), "act": z(batch, cfg.inter // tp),
+                    "dn": z(batch, H)}
+        self.qsl = torch.arange(batch + 1, dtype=torch.int32, device=device)
+        self.seq_lens = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.slots = torch.zeros(batch, dtype=torch.int64, device=device)
+        self.logits = torch.zeros(batch, vl, dtype=torch.float32, device=device)
+
+    # ---- glue kernels ---------------------------------------------------------
+    def _rmsnorm(self, delta, w):
+        b = self.buf
+        check(lib.b200kv_rmsnorm_residual(b["h"].data_ptr(), delta.data_ptr() if delta is not None else None,
+                                          w.data_ptr(), b["x"].data_ptr(), self.B, self.cfg.hidden,
+                                          float(self.cfg.eps), _stream(b["h"])), "b200kv_rmsnorm_residual")
+
+    def _rope_kv(self, kv):
+        b, k, v = self.buf, kv["k"], kv["v"]
+        check(lib.b200kv_rope_kv_write(
+            b["qkv"].data_ptr(), b["qkv"].stride(0), self.positions.data_ptr(), self.rope.data_ptr(),
+            self.max_ctx, self.slots.data_ptr(), k.data_ptr(), v.data_ptr(),
+            k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2),
+            kv["ks"].data_ptr(), kv["vs"].data_ptr(), self.B, self.hq, self.hkv, self.cfg.head_dim,
+            self.cfg.block_size, KV_FP8_E4M3 if k.dtype == torch.float8_e4m3fn else KV_BF16,
+            _stream(b["qkv"])), "b200kv_rope_kv_write")
+
+    def _swiglu(self):
+        b = self.buf
+        check(lib.b200kv_swiglu(b["gu"].data_ptr(), b["act"].data_ptr(), self.B, self.cfg.inter // self.tp,
+                                _stream(b["gu"])), "b200kv_swiglu")
+
+    # ---- one decode step --------------------------------------------------------
+    def step(self):
+        """Embed self.tokens at self.positions, run the layers, write this
+        rank's logits and return the greedy next tokens (device int64 [B]);
+        tokens and positions advance in place."""
+        cfg, b, B, d, bs = self.cfg, self.buf, self.B, self.cfg.head_dim, self.cfg.block_size
+        pos = self.positions
+        self.seq_lens.copy_(pos + 1)
+        self.slots.copy_(self.block_table.gather(1, (pos // bs).long().unsqueeze(1)).squeeze(1).long() * bs
+                         + (pos % bs).long())
+        torch.index_select(self.embed, 0, self.tokens, out=b["h"])
+        self._rmsnorm(None, self.layers[0]["in_norm"] if self.layers else self.final_norm)
+        for li, lay in enumerate(self.layers):
+            kv = self.kv[li]
+            _gemm(b["x"], lay["qkv"], b["qkv"])
+            self._rope_kv(kv)
+            q = b["qkv"][:, :self.hq * d].unflatten(1, (self.hq, d))
+            fp8kv_v3.run(q, kv["k"], kv["v"], b["attn"], self.qsl, self.seq_lens, self.block_table,
+                         kv["ks"], kv["vs"], d ** -0.5, max_seq_len=self.max_ctx)
+            _gemm(b["attn"].view(B, self.hq * d), lay["o"], b["o"])
+            self.allreduce(b["o"])
+            self._rmsnorm(b["o"], lay["post_norm"])
+            _gemm(b["x"], lay["gate_up"], b["gu"])
+            self._swiglu()
+            _gemm(b["act"], lay["down"], b["dn"])
+            self.allreduce(b["dn"])
+            nxt = self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm
+            self._rmsnorm(b["dn"], nxt)
+        # bf16 lm_head on cuBLAS (a plain library GEMM), fp32 logits
+        self.logits.copy_(torch.mm(b["x"], self.lm_head.t(), out_dtype=torch.float32))
+        val, idx = self.logits.max(dim=1)
+        if self.tp > 1:
+            vl = self.cfg.vocab // self.tp
+            mine = torch.stack([val, (idx + self.rank * vl).float()], 1)  # exact below 2^24
+            allv = torch.empty(self.tp, B, 2, dtype=torch.float32, device=self.dev)
+            self.gather(allv, mine)
+            best = allv[:, :, 0].argmax(0)  # first maximum = lowest vocab index on ties
+            idx = allv[:, :, 1].gather(0, best.unsqueeze(0)).squeeze(0).long()
+        self.tokens.copy_(idx)
+        self.positions.add_(1)
+        return self.tokens

@@ -228,6 +228,34 @@ int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_
                     int num_tokens, int num_kv_heads, int head_dim, int block_size,
                     int kv_dtype, void* stream);
 
+/* ---- Decoder-layer glue for the 7B decode loop --------------------------------------
+ *
+ * The element-wise steps around the hot path (HF Llama semantics; the
+ * reference left them to vLLM's own kernels, profiling/prof_h4mv.txt:11-15).
+ * All bf16, launched on `stream`, no synchronisation.
+ *
+ * b200kv_rmsnorm_residual: per row, h <- bf16(h + delta) when delta != NULL
+ *   (in place), then x = weight * bf16(h * rsqrt(mean(h^2) + eps)) with fp32
+ *   statistics.  hidden % 8 == 0, <= 16384; 16-byte aligned rows.
+ * b200kv_rope_kv_write: per token t (row stride qkv_stride_tok of the fused
+ *   [q | k | v] projection, heads of head_dim), rotary embedding at
+ *   positions[t] (neox halves; cos_sin = fp32 [max_pos][head_dim], the cos of
+ *   the head_dim/2 frequencies then their sin) of the q heads in place and of
+ *   the k heads, which go with v to the paged cache slot slot_mapping[t]
+ *   (< 0: skipped) exactly as b200kv_kv_write stores them.
+ * b200kv_swiglu: act[r, i] = bf16(bf16(silu(g)) * u), g = gate_up[r, i],
+ *   u = gate_up[r, inter + i]; inter even.
+ */
+int b200kv_rmsnorm_residual(void* h, const void* delta, const void* weight, void* x, int rows,
+                            int hidden, float eps, void* stream);
+int b200kv_rope_kv_write(void* qkv, int64_t qkv_stride_tok, const int32_t* positions,
+                         const float* cos_sin, int max_pos, const int64_t* slot_mapping,
+                         void* k_cache, void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2,
+                         int64_t sv0, int64_t sv1, int64_t sv2, const float* k_scale,
+                         const float* v_scale, int num_tokens, int num_q_heads, int num_kv_heads,
+                         int head_dim, int block_size, int kv_dtype, void* stream);
+int b200kv_swiglu(const void* gate_up, void* act, int rows, int inter, void* stream);
+
 /* ---- Tensor-parallel allreduce over peer memory ---------------------------------
  *
  * Sum of a bf16 vector of n elements (n % 8 == 0, n <= 32768: one [M <= 8, 4096]

@@ -84,14 +84,17 @@ def test_every_code_and_scale(cuda):
 _E2M1 = torch.tensor([0, .5, 1, 1.5, 2, 3, 4, 6], dtype=torch.float64)
 
 
-def _terms_reference(x):
-    """CPU restatement of the kernel's activation split: per 32-block, four
+TERMS = 6  # e2m1 terms per activation (the kernel's kTerms)
+
+
+def _terms_reference(x, terms=TERMS):
+    """CPU restatement of the kernel's activation split: per 32-block, `terms`
     greedy e2m1 terms, term scale 2^(E-129) for a residual maximum in
     [2^(E-127), 2^(E-126)), round to nearest (ties to the even code), saturate
     at 6."""
     r = x.double().view(x.shape[0], -1, 32).clone()
     total = torch.zeros_like(r)
-    for _ in range(4):
+    for _ in range(terms):
         mx = r.abs().amax(-1, keepdim=True)
         E = torch.floor(torch.log2(mx.clamp(min=1e-300)))
         s = torch.exp2(E - 2)
@@ -108,7 +111,7 @@ def _terms_reference(x):
 
 
 def test_activation_terms(cuda):
-    """x is written as four block-scaled e2m1 terms: w = one-hot 1.0 picks one x
+    """x is written as six block-scaled e2m1 terms: w = one-hot 1.0 picks one x
     element per row, so out = that representation of x, bit for bit; on values
     spanning 11 binades inside each 32-block it stays within 5e-4 of the block
     maximum."""
@@ -177,3 +180,18 @@ def test_rejects_bad_arguments(cuda):
         h4mv.mxfp4_gemm(torch.zeros(9, 256, dtype=torch.bfloat16, device=cuda), W.to(cuda), packed)
     with pytest.raises(ValueError):
         h4mv.pack_scales(torch.zeros(256, 3, dtype=torch.uint8, device=cuda), 256, 96)
+
+
+@pytest.mark.parametrize("N,K,M", [(1024, 512, 1), (512, 1024, 2), (2048, 512, 1), (6144, 4096, 1),
+                                   (4096, 14336, 3), (28672, 4096, 8), (512, 512, 5)])
+def test_exact_against_term_restatement(cuda, N, K, M):
+    """With x replaced by its six-term representation the product is exact up
+    to fp32 summation order and the final bf16 rounding: every output within
+    one bf16 rounding (plus 1e-6 of the maximum) of the fp32 reference."""
+    W, S, St, X = MO.make_case(N, K, M, seed=N + K + M)
+    g = torch.Generator().manual_seed(M)
+    X = (X.float() * (1 + 3 * torch.rand(X.shape, generator=g))).to(torch.bfloat16)  # wider blocks
+    ref = MO.mxfp4_linear_reference(W, S, _terms_reference(X.float()))
+    Y = _run(W, St, X, cuda)
+    tol = ref.abs() * 2.0 ** -8 + 1e-6 * ref.abs().max()
+    assert bool(((Y - ref).abs() <= tol).all()), float(((Y - ref).abs() - tol).max())
