@@ -5,10 +5,13 @@
 //
 // Every rank owns a communication buffer (cudaMalloc, shared with the peers
 // through CUDA IPC handles):
-//   [0, 64)        call counter (read and advanced only by the owner)
+//   [0, 256)       call counters, one per CTA (read and advanced only by it)
 //   [256, ...)     lines[2][8][kMaxElems / 2] of 8 bytes: {4 data bytes, flag}
-// Call k (counter value k, parity p = k & 1) on rank r: one CTA writes its
-// partial into lines[p][r] of every rank, two bf16 and the flag k + 1 per
+// The vector is split into chunks of kLinesPerCta lines, one CTA each (the
+// grid depends only on n, so every call of a size uses the same chunks and
+// counters).  Call k of a chunk (its counter value k, parity p = k & 1) on
+// rank r: the CTA writes its chunk into lines[p][r] of every rank, two bf16
+// and the flag k + 1 per
 // 8-byte store (one NVLink transaction, so a reader that sees the flag sees the
 // data: no fence and no separate flag round trip -- the "low-latency" line
 // format), then polls its own lines[p][*] until every flag reads k + 1
@@ -32,10 +35,13 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 constexpr int kMaxElems = 8 * 4096;     // bf16 elements per partial
-constexpr int kArThreads = 512;
+constexpr int kArThreads = 256;
+constexpr int kLinesPerCta = 256;        // one line per thread
+constexpr int kMaxCtas = kMaxElems / 2 / kLinesPerCta;
 constexpr size_t kCtrlBytes = 256;
 constexpr size_t kLines = kMaxElems / 2;  // 8-byte lines per rank slot
 constexpr size_t kBufBytes = kCtrlBytes + (size_t)2 * kMaxRanks * kLines * 8;
+static_assert(kMaxCtas * 4 <= (int)kCtrlBytes, "one counter per CTA in the control block");
 constexpr unsigned long long kTimeoutNs = 200ull * 1000 * 1000;  // 200 ms
 
 struct PeerBufs {
@@ -67,25 +73,27 @@ __global__ void __launch_bounds__(kArThreads, 1)
   const int tid = threadIdx.x;
   if (tid == 0) griddep_launch_dependents();
   uint8_t* mine = peers.p[rank];
+  volatile uint32_t* counter = reinterpret_cast<volatile uint32_t*>(mine) + blockIdx.x;
   // `in` is the previous kernel's output, and the counter was advanced by the
   // previous call, which may still have been running when this grid started
   griddep_wait();
-  if (tid == 0) call = *reinterpret_cast<volatile uint32_t*>(mine);
+  if (tid == 0) call = *counter;
   __syncthreads();
   const uint32_t flag = call + 1;
   const int par = (int)(call & 1u);
-  const int nl = n / 2;  // lines (2 bf16 each)
+  const int nl = min(n / 2, (int)(blockIdx.x + 1) * kLinesPerCta);  // lines (2 bf16 each)
+  const int i0 = blockIdx.x * kLinesPerCta;
   const uint32_t* src = reinterpret_cast<const uint32_t*>(in);
 
-  // push: this rank's partial into slot `rank` of every rank's buffer
-  for (int i = tid; i < nl; i += kArThreads) {
+  // push: this rank's chunk into slot `rank` of every rank's buffer
+  for (int i = i0 + tid; i < nl; i += kArThreads) {
     const uint32_t d = src[i];
     for (int r = 0; r < tp; ++r) st_line(lines(peers.p[r], par, rank) + i, d, flag);
   }
 
   // poll the local slots, fixed-order sum (identical on every rank)
   bool late = false;
-  for (int i = tid; i < nl; i += kArThreads) {
+  for (int i = i0 + tid; i < nl; i += kArThreads) {
     float a0 = 0.f, a1 = 0.f;
     for (int r = 0; r < tp; ++r) {
       const uint2* l = lines(mine, par, r) + i;
@@ -107,7 +115,7 @@ __global__ void __launch_bounds__(kArThreads, 1)
     reinterpret_cast<uint32_t*>(out)[i] = *reinterpret_cast<const uint32_t*>(&h);
   }
   __syncthreads();
-  if (tid == 0) *reinterpret_cast<volatile uint32_t*>(mine) = flag;
+  if (tid == 0) *counter = flag;
 }
 
 }  // namespace
@@ -154,7 +162,7 @@ int allreduce_oneshot_launch(const void* in, void* out, int n, void* const* bufs
     pb.p[r] = static_cast<uint8_t*>(bufs[r]);
   }
   cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(1, 1, 1);
+  lc.gridDim = dim3((n / 2 + kLinesPerCta - 1) / kLinesPerCta, 1, 1);
   lc.blockDim = dim3(kArThreads, 1, 1);
   lc.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[1];
