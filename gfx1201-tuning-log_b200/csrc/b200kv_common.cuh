@@ -111,6 +111,31 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// ---- thread-block clusters: push into a peer's shared memory -----------------------
+// A rank that pushes with st.async must know the target's mbarrier is
+// initialised: every thread calls cluster_arrive_relaxed() after the barriers
+// are set up and the pushing threads call cluster_wait() before their first
+// push.  The target waits on its mbarrier for the bytes it expects, so no rank
+// reads another's shared memory and none waits on a cluster barrier at the end.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// 4-byte store into a peer CTA's shared memory, counted in bytes on the peer's
+// mbarrier (both addresses from map_to_rank)
+__device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
+               "r"(__float_as_uint(v)), "r"(rbar)
+               : "memory");
+}
+
 // ---- programmatic dependent launch ---------------------------------------------
 // A kernel launched with programmatic stream serialization may start while the
 // kernel before it in the stream still runs (once every CTA of that kernel has

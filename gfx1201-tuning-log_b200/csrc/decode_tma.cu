@@ -77,8 +77,10 @@ struct TmaShared {
   alignas(16) float part_o[GQA][kHD];  // this CTA's unnormalised o (read by peers)
   float wm[kCWarps][8], wl[kCWarps][8];
   float part_m[8], part_l[8];
-  float rm[kMaxCS][8], rl[kMaxCS][8], rw[kMaxCS][8];
-  uint64_t full_bar[kStages], empty_bar[kStages];
+  alignas(16) float inbox_o[GQA * kHD];     // [source rank][the elements this rank finishes]
+  float inbox_ml[kMaxCS][2][8];             // every rank's (m, l) per head
+  float rw[kMaxCS][8];                      // every rank's weight in the output
+  uint64_t full_bar[kStages], empty_bar[kStages], inbox_bar;
 };
 
 // byte offset of (row, byte b) in a 128-byte-swizzled tile (1024-byte aligned)
@@ -110,7 +112,10 @@ __global__ void __launch_bounds__(kThreadsT)
       mbar_init(&S.full_bar[s], 1);
       mbar_init(&S.empty_bar[s], kCWarps);
     }
+    mbar_init(&S.inbox_bar, 1);
     fence_mbar_init();
+    if (csize > 1)  // the peers' pushes: their o elements of this rank plus their (m, l)
+      mbar_arrive_expect_tx(&S.inbox_bar, (uint32_t)((csize - 1) * (GQA * kHD / csize + 2 * GQA) * 4));
     // The next kernel may launch now.  Sequence metadata and block-table rows
     // are read, and pages prefetched into L2, before this grid waits on the
     // previous one; q, the shared-memory loads of K and V and the output come
@@ -127,6 +132,7 @@ __global__ void __launch_bounds__(kThreadsT)
   const int hi = min(seqlen, lo + per);
   const int nchunks = (hi - lo + kStageTok - 1) / kStageTok;
   __syncthreads();  // barrier init visible
+  if (csize > 1) cluster_arrive_relaxed();  // the inbox barrier is initialised
 
   float m_run = -INFINITY, l_run = 0.f;
   float o[8][4];
@@ -362,31 +368,53 @@ __global__ void __launch_bounds__(kThreadsT)
     S.part_m[tid] = mc;
     S.part_l[tid] = lc;
   }
+  // ---- merge the cluster's partials: push, then reduce locally ----------------------
+  // Rank r finishes elements [r per_cta, (r + 1) per_cta) of the (head, dim)
+  // block.  Every rank pushes its (m, l) of every head and its o of those
+  // elements into rank r's inbox (st.async, counted on r's inbox barrier), so the
+  // merge costs one one-way trip and no rank waits on a cluster barrier.
+  constexpr int E = GQA * kHD;
+  const int per_cta = E / csize, e0 = rank * per_cta;
+  __syncthreads();  // part_o, part_m, part_l complete
+  if (csize > 1) cluster_wait();
+  const uint32_t bar_local = smem_u32(&S.inbox_bar);
+  for (int it = tid; it < E + csize * 2 * GQA; it += kThreadsT) {
+    int r;
+    float v;
+    float* dst;
+    if (it < E) {
+      r = it / per_cta;
+      v = (&S.part_o[0][0])[it];
+      dst = &S.inbox_o[rank * per_cta + (it - r * per_cta)];
+    } else {
+      const int j = it - E, k = j % (2 * GQA);
+      r = j / (2 * GQA);
+      v = k < GQA ? S.part_m[k] : S.part_l[k - GQA];
+      dst = &S.inbox_ml[rank][k / GQA][k % GQA];
+    }
+    if (r == rank)
+      *dst = v;
+    else
+      st_async_f32(map_to_rank(smem_u32(dst), r), v, map_to_rank(bar_local, r));
+  }
+  if (csize > 1) mbar_wait_bounded(&S.inbox_bar, 0);
+  __syncthreads();  // this rank's own inbox entries are visible too
+
   griddep_wait();  // every thread, before the output store (and before exit)
   const float vsc = __ldg(p.v_scale);
   __nv_bfloat16* out_base = p.out + (int64_t)out_row * p.o_st + (int64_t)(kh * GQA) * p.o_sh;
-
-  // ---- merge the cluster's partials through distributed shared memory -------------
-  // one round of (m, l) loads, then one float4 of one rank's o per work item
-  cluster.sync();
-  if (tid < csize * GQA) {
-    const int r = tid / GQA, h = tid % GQA;
-    S.rm[r][h] = cluster.map_shared_rank(&S.part_m[0], r)[h];
-    S.rl[r][h] = cluster.map_shared_rank(&S.part_l[0], r)[h];
-  }
-  __syncthreads();
   if (tid < GQA) {
     float mg = -INFINITY;
 #pragma unroll
     for (int r = 0; r < kMaxCS; ++r)
-      if (r < csize) mg = fmaxf(mg, S.rm[r][tid]);
+      if (r < csize) mg = fmaxf(mg, S.inbox_ml[r][0][tid]);
     float wr[kMaxCS];
     float lg = 0.f;
 #pragma unroll
     for (int r = 0; r < kMaxCS; ++r) {
-      const float mr = r < csize ? S.rm[r][tid] : -INFINITY;
+      const float mr = r < csize ? S.inbox_ml[r][0][tid] : -INFINITY;
       wr[r] = (mr == -INFINITY) ? 0.f : exp2f(mr - mg);
-      if (r < csize) lg += wr[r] * S.rl[r][tid];
+      if (r < csize) lg += wr[r] * S.inbox_ml[r][1][tid];
     }
     const float inv = lg > 0.f ? vsc / lg : 0.f;
 #pragma unroll
@@ -394,27 +422,14 @@ __global__ void __launch_bounds__(kThreadsT)
       if (r < csize) S.rw[r][tid] = wr[r] * inv;
   }
   __syncthreads();
-  constexpr int E = GQA * kHD;
-  const int per_cta = E / csize, nv = per_cta / 4, e0 = rank * per_cta;
-  float* contrib = reinterpret_cast<float*>(smem);
-  for (int it = tid; it < csize * nv; it += kThreadsT) {
-    const int r = it / nv, v = it - r * nv;
-    const int e = e0 + 4 * v;
-    const float w = S.rw[r][e / kHD];
-    float4 ov = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (w != 0.f) ov = *reinterpret_cast<const float4*>(cluster.map_shared_rank(&S.part_o[0][0], r) + e);
-    *reinterpret_cast<float4*>(contrib + r * per_cta + 4 * v) = make_float4(w * ov.x, w * ov.y, w * ov.z, w * ov.w);
-  }
-  __syncthreads();
   for (int i = tid; i < per_cta; i += kThreadsT) {
+    const int e = e0 + i, h = e / kHD, d = e % kHD;
     float acc = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxCS; ++r)
-      if (r < csize) acc += contrib[r * per_cta + i];
-    const int e = e0 + i, h = e / kHD, d = e % kHD;
+    for (int r = 0; r < kMaxCS; ++r)  // the products rounded before the sum, as the gather path
+      if (r < csize) acc = __fadd_rn(acc, __fmul_rn(S.rw[r][h], S.inbox_o[r * per_cta + i]));
     out_base[(int64_t)h * p.o_sh + d] = __float2bfloat16_rn(acc);
   }
-  cluster.sync();  // peers' shared memory stays alive until every rank is done
 }
 
 template <int GQA>

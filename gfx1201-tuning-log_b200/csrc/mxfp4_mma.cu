@@ -105,24 +105,7 @@ struct MmaLayout {
   }
 };
 
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, int rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-// 4-byte store into a peer CTA's shared memory, counted in bytes on the peer's
-// mbarrier (both addresses from map_to_rank)
-__device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr),
-               "r"(__float_as_uint(v)), "r"(rbar)
-               : "memory");
-}
+
 
 // instruction descriptor, kind::mxf4 block-scaled: A, B e2m1 (format 1 of this
 // kind), both K-major, e8m0 scales, scale-factor byte ids (0 or 2: two bytes per MMA)
