@@ -38,13 +38,6 @@ bool encode_paged_kv(CUtensorMap* map, const void* base, uint32_t row_bytes, uin
                      uint32_t tokens, uint64_t blocks, uint64_t s_head, uint64_t s_tok,
                      uint64_t s_blk);
 
-// Encodes a 2-D tensor map over packed e2m1 data [rows][row_elems / 2 bytes]
-// (pitch bytes per row) as 16U4_ALIGN16B: a load unpacks every 16 nibbles
-// into a 16-byte chunk (8 data bytes + 8 pad bytes), the layout the tensor
-// core reads 4-bit operands of kind::f8f6f4 from.  Box [box_elems (128), box_rows],
-// 128-byte swizzle.  Needs base 32-byte aligned and pitch a multiple of 32.
-bool encode_e2m1_unpacked_2d(CUtensorMap* map, const void* base, uint64_t row_elems, uint64_t rows,
-                             uint64_t pitch, uint32_t box_elems, uint32_t box_rows);
 
 // 4-D tiled TMA load of the box at (c0 bytes, c1, c2, c3), completion counted on
 // `bar`.  c0 must be a multiple of 16.

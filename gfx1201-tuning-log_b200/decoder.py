@@ -47,21 +47,25 @@ def rope_table(max_pos, head_dim, theta):
     return torch.cat([torch.cos(ang), torch.sin(ang)], 1).float()
 
 
-def _mxfp4(g, n, k, device):
+CONFIG2_SCALES = (119, 126)  # e8m0 bytes drawn from [lo, hi): 2^-8 .. 2^-2
+
+
+def _mxfp4(g, n, k, device, scales):
     W = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=device, generator=g)
-    St = torch.randint(119, 126, (n, k // 32), dtype=torch.uint8, device=device, generator=g)
+    St = torch.randint(scales[0], scales[1], (n, k // 32), dtype=torch.uint8, device=device, generator=g)
     return W, St
 
 
-def random_layer(cfg, li, seed, device="cpu"):
+def random_layer(cfg, li, seed, device="cpu", scales=CONFIG2_SCALES):
     """Full (unsharded) weights of layer li: MXFP4 (W [N, K/2], St [N, K/32])
     for qkv ([q | k | v] rows), o, gate_up ([gate | up] rows), down; bf16 norms.
     Every rank draws the same layer from the same seed and keeps its shard."""
     g = torch.Generator(device=device).manual_seed(seed * 1000 + li)
     H, d = cfg.hidden, cfg.head_dim
     nqkv = (cfg.heads + 2 * cfg.kv_heads) * d
-    lay = {"qkv": _mxfp4(g, nqkv, H, device), "o": _mxfp4(g, H, cfg.heads * d, device),
-           "gate_up": _mxfp4(g, 2 * cfg.inter, H, device), "down": _mxfp4(g, H, cfg.inter, device)}
+    lay = {"qkv": _mxfp4(g, nqkv, H, device, scales), "o": _mxfp4(g, H, cfg.heads * d, device, scales),
+           "gate_up": _mxfp4(g, 2 * cfg.inter, H, device, scales),
+           "down": _mxfp4(g, H, cfg.inter, device, scales)}
     for name in ("in_norm", "post_norm"):
         lay[name] = (1.0 + 0.1 * torch.randn(H, device=device, generator=g)).to(torch.bfloat16)
     return lay
@@ -129,7 +133,8 @@ class MXFP4Decoder:
     drawn on `gen_device` (CPU in tests, so the oracle sees the same numbers)."""
 
     def __init__(self, cfg, device, batch, max_ctx, seed=0, tp=1, rank=0, allreduce=None,
-                 gather=None, kv_scale=1.0 / 8, gen_device=None, layers=None, mxfp4_kernel="auto"):
+                 gather=None, kv_scale=1.0 / 8, gen_device=None, layers=None, mxfp4_kernel="auto",
+                 scales=CONFIG2_SCALES):
         self.cfg, self.dev, self.B, self.tp, self.rank = cfg, device, batch, tp, rank
         self.allreduce = allreduce if allreduce is not None else (lambda t: t)
         self.gather = gather
@@ -141,7 +146,7 @@ class MXFP4Decoder:
         nlayers = cfg.layers if layers is None else layers
         self.layers = []
         for li in range(nlayers):
-            sh = shard_layer(random_layer(cfg, li, seed, gdev), cfg, rank, tp)
+            sh = shard_layer(random_layer(cfg, li, seed, gdev, scales), cfg, rank, tp)
             lin = lambda name: _linear(*sh[name], device, mxfp4_kernel)  # noqa: E731
             self.layers.append({
                 "qkv": lin("qkv"), "o": lin("o"), "gate_up": lin("gate_up"), "down": lin("down"),

@@ -62,9 +62,27 @@ def linear(x, W, S):
     return MO.mxfp4_linear_reference(W, S, x).to(torch.bfloat16)
 
 
-def decode_step(cfg, weights, caches, tokens, positions, block_table, table):
+def linear_rowpar(x, W, S, tp):
+    """Row-parallel MXFP4 linear over tp ranks, as tensor parallelism computes
+    it: each rank's K slice gives an fp32 partial rounded to bf16, the partials
+    are summed in rank order in fp32 and rounded to bf16 (the allreduce)."""
+    if tp == 1:
+        return linear(x, W, S)
+    K = x.shape[1]
+    k = K // tp
+    acc = None
+    for r in range(tp):
+        part = MO.mxfp4_linear_reference(W[:, r * k // 2:(r + 1) * k // 2],
+                                         S[r * k // 32:(r + 1) * k // 32], x[:, r * k:(r + 1) * k])
+        part = part.to(torch.bfloat16).float()
+        acc = part if acc is None else acc + part
+    return acc.to(torch.bfloat16)
+
+
+def decode_step(cfg, weights, caches, tokens, positions, block_table, table, tp=1):
     """One decode step for B sequences; caches (per layer dict k, v, ks, vs) are
-    updated in place with the new tokens' K/V.  Returns fp32 logits [B, V]."""
+    updated in place with the new tokens' K/V.  tp > 1 rounds the row-parallel
+    o and down partials as tensor parallelism does.  Returns fp32 logits [B, V]."""
     B = tokens.shape[0]
     H, hq, hkv, d, inter = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.inter
     bs = cfg.block_size
@@ -86,11 +104,11 @@ def decode_step(cfg, weights, caches, tokens, positions, block_table, table):
         qsl = torch.arange(B + 1, dtype=torch.int32)
         attn = FO.decode_reference(q, c["k"], c["v"], qsl, seq_lens, block_table, c["ks"], c["vs"],
                                    d ** -0.5).to(torch.bfloat16)
-        o = linear(attn.reshape(B, hq * d), *lw["o"])
+        o = linear_rowpar(attn.reshape(B, hq * d), *lw["o"], tp)
         h = (h.float() + o.float()).to(torch.bfloat16)
         x = rmsnorm(h, lw["post_norm"], cfg.eps)
         act = swiglu(linear(x, *lw["gate_up"]), inter)
-        dn = linear(act, *lw["down"])
+        dn = linear_rowpar(act, *lw["down"], tp)
         h = (h.float() + dn.float()).to(torch.bfloat16)
     x = rmsnorm(h, weights["final_norm"], cfg.eps)
     return x.float() @ weights["lm_head"].float().t()

@@ -93,3 +93,80 @@ def test_peer_allreduce_two_gpus():
     if torch.cuda.device_count() < TP:
         pytest.skip("needs two GPUs")
     mp.spawn(_rank_main, args=(_free_port(),), nprocs=TP, join=True)
+
+
+def _decoder_rank(rank, port):
+    """The tensor-parallel decoder (2 ranks) against the CPU oracle of the whole
+    model with the row-parallel partials rounded to bf16 before their sum (the
+    numerics of tensor parallelism): each rank's logits are its vocab slice of
+    the oracle's, the greedy tokens agree where the oracle's top two are
+    separated."""
+    import sys
+    from conftest import ORACLE
+    for p in (PKG, ORACLE):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import decoder
+    import decoder_oracle as DO
+    import tp
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=TP, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    ar = tp.PeerAllreduce()
+    try:
+        cfg = decoder.DecoderConfig(layers=2, hidden=512, heads=4, kv_heads=2, head_dim=128,
+                                    inter=1024, vocab=1000)
+        seed, B, max_ctx = 5, 2, 64
+
+        def gather(out, inp):
+            dist.all_gather_into_tensor(out.view(-1), inp.contiguous().view(-1))
+        # e8m0 scales 2^-9..2^-6: attention scores of order one, so the model is not
+        # so sensitive that one bf16 rounding of a partial changes later tokens
+        scales = (118, 122)
+        dec = decoder.MXFP4Decoder(cfg, dev, B, max_ctx, seed=seed, tp=TP, rank=rank, allreduce=ar,
+                                   gather=gather, gen_device="cpu", scales=scales)
+        layers = []
+        for li in range(cfg.layers):
+            lay = decoder.random_layer(cfg, li, seed, "cpu", scales)
+            layers.append({k: ((v[0], v[1].t().contiguous()) if isinstance(v, tuple) else v)
+                           for k, v in lay.items()})
+        weights = dict(decoder.random_head(cfg, seed, "cpu"), layers=layers)
+        nb = B * dec.maxblk
+        caches = [{"k": torch.zeros(nb, 16, cfg.kv_heads, 128, dtype=torch.float8_e4m3fn),
+                   "v": torch.zeros(nb, 16, cfg.kv_heads, 128, dtype=torch.float8_e4m3fn),
+                   "ks": 1 / 8, "vs": 1 / 8} for _ in range(cfg.layers)]
+        table = DO.rope_table(max_ctx, 128, cfg.rope_theta)
+        bt = dec.block_table.cpu()
+        tokens = torch.tensor([3, 7], dtype=torch.int64)
+        dec.tokens.copy_(tokens)
+        positions = torch.zeros(B, dtype=torch.int32)
+        vl = cfg.vocab // TP
+        for step in range(5):
+            want = DO.decode_step(cfg, weights, caches, tokens, positions, bt, table, tp=TP)
+            nxt = dec.step().cpu()
+            got = dec.logits.cpu()
+            mine = want[:, rank * vl:(rank + 1) * vl]
+            err = float((got - mine).abs().max() / want.abs().max())
+            assert err < 2e-2, (rank, step, err)
+            top2 = want.topk(2, dim=1).values
+            sep = (top2[:, 0] - top2[:, 1]) > 4 * float((got - mine).abs().max())
+            assert torch.equal(nxt[sep], want.argmax(1)[sep]), (rank, step)
+            tokens = nxt.clone()
+            positions = positions + 1
+        torch.cuda.synchronize()
+        import _b200kv
+        assert _b200kv.device_status() == 0
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        ar.close()
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_decoder_two_gpus():
+    if torch.cuda.device_count() < TP:
+        pytest.skip("needs two GPUs")
+    mp.spawn(_decoder_rank, args=(_free_port(),), nprocs=TP, join=True)
