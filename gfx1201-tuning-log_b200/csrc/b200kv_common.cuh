@@ -136,6 +136,16 @@ __device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t r
                : "memory");
 }
 
+// 16-byte store (four floats) into a peer CTA's shared memory, counted on the
+// peer's mbarrier; raddr 16-byte aligned
+__device__ __forceinline__ void st_async_v4_f32(uint32_t raddr, float4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   raddr),
+               "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)), "r"(__float_as_uint(v.z)),
+               "r"(__float_as_uint(v.w)), "r"(rbar)
+               : "memory");
+}
+
 // ---- programmatic dependent launch ---------------------------------------------
 // A kernel launched with programmatic stream serialization may start while the
 // kernel before it in the stream still runs (once every CTA of that kernel has

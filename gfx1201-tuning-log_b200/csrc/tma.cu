@@ -40,6 +40,20 @@ bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64
   return r == CUDA_SUCCESS;
 }
 
+bool encode_e2m1_unpacked_2d(CUtensorMap* map, const void* base, uint64_t row_elems, uint64_t rows,
+                             uint64_t pitch, uint32_t box_rows) {
+  PFN_cuTensorMapEncodeTiled enc = get_encode();
+  if (!enc || row_elems % 128 || (pitch & 15) || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const cuuint64_t dims[2] = {row_elems, rows};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool encode_paged_kv(CUtensorMap* map, const void* base, uint32_t row_bytes, uint32_t heads,
                      uint32_t tokens, uint64_t blocks, uint64_t s_head, uint64_t s_tok,
                      uint64_t s_blk) {

@@ -17,6 +17,15 @@ namespace b200kv {
 bool encode_u8_2d(CUtensorMap* map, const void* base, uint64_t row_bytes, uint64_t rows,
                   uint64_t pitch, uint32_t box_x, uint32_t box_y, bool swizzle128);
 
+// Encodes a 2-D tensor map over packed e2m1 codes [rows, row_elems] (two codes
+// a byte, row pitch `pitch` bytes) that the TMA unpacks on the way into shared
+// memory: every 8 bytes (16 codes) land in a 16-byte chunk, the operand layout
+// of 4-bit types in tcgen05 kind::f8f6f4 / mxf8f6f4 MMAs.  Box [128 codes, box_rows
+// rows] with 128-byte swizzle: 128 bytes of shared memory per row, of which the
+// TMA signals the 64 packed bytes on the mbarrier.  x coordinates count codes.
+bool encode_e2m1_unpacked_2d(CUtensorMap* map, const void* base, uint64_t row_elems, uint64_t rows,
+                             uint64_t pitch, uint32_t box_rows);
+
 // 2-D tiled TMA load of the box at (x bytes, y rows) into shared memory,
 // completion counted on `bar`.  x must be a multiple of 16.
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,

@@ -75,7 +75,8 @@ def pack_scales(scales, N, K, layout=SCALES_TRANSPOSED):
 
 def mxfp4_gemm(x, weight, packed_scales, out=None):
     """out[M, N] = x[M, K] @ dequant(weight, scales)^T on block-scaled tcgen05
-    MMAs, 1 <= M <= 8, K % 256 == 0, with scales packed by pack_scales()."""
+    MMAs with scales packed by pack_scales(): 1 <= M <= 8 (K % 256 == 0) on the
+    skinny kernel, larger M on mxfp4_gemm_wide (K % 128 == 0)."""
     if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
         raise ValueError("x must be a contiguous 2-D bfloat16 tensor")
     if weight.dtype != torch.uint8 or not weight.is_contiguous():
@@ -84,10 +85,57 @@ def mxfp4_gemm(x, weight, packed_scales, out=None):
     N = weight.shape[0]
     if weight.shape[1] * 2 != K:
         raise ValueError(f"shape mismatch x={tuple(x.shape)} w={tuple(weight.shape)}")
+    if M > MAX_M:
+        return mxfp4_gemm_wide(x, weight, packed_scales, out)
     if out is None:
         out = torch.empty((M, N), device=x.device, dtype=torch.bfloat16)
     check(lib.b200kv_mxfp4_gemm(weight.data_ptr(), packed_scales.data_ptr(), x.data_ptr(),
                                 out.data_ptr(), N, K, M,
                                 torch.cuda.current_stream(x.device).cuda_stream),
           "b200kv_mxfp4_gemm")
+    return out
+
+
+# (device index, stream handle) -> workspace of the wide GEMM's activation terms;
+# calls on one stream run in order, so they can share it
+_workspaces = {}
+
+
+def wide_workspace(M, K, device, stream):
+    """The cached workspace for an (M, K) call on `stream` (grown on demand)."""
+    need = lib.b200kv_mxfp4_gemm_wide_workspace_bytes(M, K)
+    if need == 0:
+        raise ValueError(f"wide GEMM needs K % 128 == 0 (K={K})")
+    key = (device.index, stream.cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def mxfp4_gemm_wide(x, weight, packed_scales, out=None, workspace=None):
+    """out[M, N] = x[M, K] @ dequant(weight, scales)^T for wide batches on
+    block-scaled tcgen05 MMAs (kind::mxf8f6f4: e2m1 weights, x as two exact
+    e4m3 terms).  x bf16 2-D with unit inner stride (row stride a multiple of
+    8), K % 128 == 0, scales packed by pack_scales().  The activation terms go
+    to `workspace` (uint8, b200kv_mxfp4_gemm_wide_workspace_bytes) or to a
+    buffer cached per device and stream."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be a 2-D bfloat16 tensor with unit inner stride")
+    if weight.dtype != torch.uint8 or not weight.is_contiguous():
+        raise TypeError("weight must be a contiguous uint8 tensor")
+    M, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] * 2 != K:
+        raise ValueError(f"shape mismatch x={tuple(x.shape)} w={tuple(weight.shape)}")
+    stream = torch.cuda.current_stream(x.device)
+    if workspace is None:
+        workspace = wide_workspace(M, K, x.device, stream)
+    if out is None:
+        out = torch.empty((M, N), device=x.device, dtype=torch.bfloat16)
+    check(lib.b200kv_mxfp4_gemm_wide(weight.data_ptr(), packed_scales.data_ptr(), x.data_ptr(),
+                                     x.stride(0), workspace.data_ptr(), workspace.numel(),
+                                     out.data_ptr(), N, K, M, stream.cuda_stream),
+          "b200kv_mxfp4_gemm_wide")
     return out

@@ -164,6 +164,24 @@ int b200kv_mxfp4_pack_scales(const void* scales, int layout, void* packed, int N
 int b200kv_mxfp4_gemm(const void* W, const void* packed_scales, const void* X, void* out, int N,
                       int K, int M, void* stream);
 
+/* Wide batches (prefill chunks, batched decode; any M >= 1, meant for M > 8):
+ * the same product on tcgen05 kind::mxf8f6f4.block_scale MMAs, weights as e2m1
+ * with the packed scale atoms above, x as two e4m3 terms with per-32 block
+ * scales written by a pre-pass into the caller's workspace (exact for every
+ * element within 2^-13 of its block maximum, within 2^-21 of it otherwise);
+ * fp32 accumulation.  The reference's counterpart is its dequant + matmul
+ * path for M > 8 (h4mv/fp8kv_hipw4.py:62-94).
+ *   b200kv_mxfp4_gemm_wide_workspace_bytes  workspace size for (M, K): 128 B
+ *       rows of 2 K bytes per 64 tokens plus scale atoms (0 if K % 128).
+ *   b200kv_mxfp4_gemm_wide  out[M, N] bf16; x rows x_stride elements apart
+ *       (a multiple of 8, >= K), K % 128 == 0, W / packed / x 16-byte aligned,
+ *       workspace 128-byte aligned.  Two launches on `stream` (pre-pass, GEMM);
+ *       calls that share a workspace must be ordered on one stream. */
+size_t b200kv_mxfp4_gemm_wide_workspace_bytes(int M, int K);
+int b200kv_mxfp4_gemm_wide(const void* W, const void* packed_scales, const void* X, int64_t x_stride,
+                           void* workspace, size_t workspace_bytes, void* out, int N, int K, int M,
+                           void* stream);
+
 /* ---- fp8 paged-KV causal prefill attention -----------------------------------
  *
  * For every sequence s with query rows cu_seqlens_q[s] .. cu_seqlens_q[s+1]-1

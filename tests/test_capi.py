@@ -54,6 +54,22 @@ def test_gemv_argument_validation(b200):
     assert lib.b200kv_last_error() == 2
 
 
+def test_wide_gemm_argument_validation(b200):
+    lib = b200.lib
+    A = 0x10000  # never dereferenced: every call below fails validation first
+    need = lib.b200kv_mxfp4_gemm_wide_workspace_bytes(100, 1024)
+    assert need == 2 * 128 * 1024 + 2 * 8 * 512
+    assert lib.b200kv_mxfp4_gemm_wide_workspace_bytes(100, 1000) == 0
+    assert lib.b200kv_mxfp4_gemm_wide(None, A, A, 1024, A, need, A, 8, 1024, 100, None) == 1
+    assert lib.b200kv_mxfp4_gemm_wide(A, A, A, 1000, A, need, A, 8, 1024, 100, None) == 1  # stride < K
+    assert lib.b200kv_mxfp4_gemm_wide(A, A, A, 1000, A, need, A, 8, 1000, 100, None) == 2  # K % 128
+    assert lib.b200kv_mxfp4_gemm_wide(A, A, A + 8, 1024, A, need, A, 8, 1024, 100, None) == 3
+    assert lib.b200kv_mxfp4_gemm_wide(A, A, A, 1028, A, need, A, 8, 1024, 100, None) == 3  # stride % 8
+    assert lib.b200kv_mxfp4_gemm_wide(A, A, A, 1024, A + 64, need, A, 8, 1024, 100, None) == 3
+    assert lib.b200kv_mxfp4_gemm_wide(A, A, A, 1024, A, need - 1, A, 8, 1024, 100, None) == 4
+    assert lib.b200kv_mxfp4_gemm_wide(A, A, A, 1024, None, need, A, 8, 1024, 100, None) == 4
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason="fake pointers are only safe without a GPU")
 def test_gemv_no_device(b200):
     A = 0x10000
