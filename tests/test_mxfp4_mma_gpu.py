@@ -174,10 +174,21 @@ def test_matches_cuda_core_kernel(cuda):
 def test_rejects_bad_arguments(cuda):
     import h4mv
     from _b200kv import B200KVError
+    from _b200kv import lib
     W, S, St, X = MO.make_case(256, 256, 1, seed=0)
     packed, _ = h4mv.pack_scales(St.to(cuda), 256, 256)
-    with pytest.raises(B200KVError):
-        h4mv.mxfp4_gemm(torch.zeros(9, 256, dtype=torch.bfloat16, device=cuda), W.to(cuda), packed)
+    x9 = torch.zeros(9, 256, dtype=torch.bfloat16, device=cuda)
+    out = torch.empty(9, 256, dtype=torch.bfloat16, device=cuda)
+    Wd = W.to(cuda)
+    # the skinny kernel takes M <= 8 (h4mv.mxfp4_gemm sends larger M to the wide one)
+    assert lib.b200kv_mxfp4_gemm(Wd.data_ptr(), packed.data_ptr(), x9.data_ptr(), out.data_ptr(), 256, 256, 9,
+                                 torch.cuda.current_stream().cuda_stream) == 2
+    with pytest.raises(B200KVError):  # the skinny kernel needs K % 256 == 0
+        h4mv.mxfp4_gemm(torch.zeros(2, 384, dtype=torch.bfloat16, device=cuda),
+                        torch.zeros(256, 192, dtype=torch.uint8, device=cuda), packed)
+    with pytest.raises(ValueError):  # the wide one K % 128 == 0
+        h4mv.mxfp4_gemm(torch.zeros(9, 192, dtype=torch.bfloat16, device=cuda),
+                        torch.zeros(256, 96, dtype=torch.uint8, device=cuda), packed)
     with pytest.raises(ValueError):
         h4mv.pack_scales(torch.zeros(256, 3, dtype=torch.uint8, device=cuda), 256, 96)
 
