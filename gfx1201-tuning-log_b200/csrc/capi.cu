@@ -95,6 +95,8 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
 size_t mxfp4_gemm_wide_workspace_bytes(int M, int K);
 int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* ws,
                            size_t ws_bytes, void* Out, int N, int K, int M, void* stream);
+int mxfp4_gemm_wide_noalloc_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* Out, int N,
+                                   int K, int M, void* stream);
 
 int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                         const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
@@ -219,6 +221,11 @@ int b200kv_mxfp4_gemm_wide(const void* W, const void* packed_scales, const void*
                            void* stream) {
   return b200kv::mxfp4_gemm_wide_launch(W, packed_scales, X, x_stride, workspace, workspace_bytes, out, N,
                                         K, M, stream);
+}
+
+int b200kv_mxfp4_gemm_wide_noalloc(const void* W, const void* packed_scales, const void* X, int64_t x_stride,
+                                   void* out, int N, int K, int M, void* stream) {
+  return b200kv::mxfp4_gemm_wide_noalloc_launch(W, packed_scales, X, x_stride, out, N, K, M, stream);
 }
 
 int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_head,

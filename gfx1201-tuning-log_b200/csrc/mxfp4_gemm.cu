@@ -624,4 +624,49 @@ int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;
 }
 
+// ---- allocation-free variant ------------------------------------------------------
+// Callers that cannot allocate device memory (an engine that has already handed
+// all free HBM to its KV-cache pool, or a host that binds this C ABI with no
+// device allocator of its own) get the same GEMM with its activation-term
+// scratch in a fixed array of this library: up to kNoAllocMaxM activation rows
+// of K <= kNoAllocMaxK (4.3 MB, held on every GPU that loads the library).
+constexpr int kNoAllocMaxM = 2 * kTok;
+constexpr int kNoAllocMaxK = 16384;
+constexpr size_t kNoAllocBytes =
+    (size_t)(kNoAllocMaxM / kTok) * kBRows * kNoAllocMaxK + (size_t)(kNoAllocMaxM / kTok) * (kNoAllocMaxK / kKStep) * kAtom;
+static __device__ __align__(256) uint8_t g_wide_scratch[kNoAllocBytes];
+
+namespace {
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxScratchDevices];  // device address of g_wide_scratch per device ordinal
+}  // namespace
+
+int mxfp4_gemm_wide_noalloc_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* Out, int N,
+                                   int K, int M, void* stream) {
+  if (M > kNoAllocMaxM || K > kNoAllocMaxK) return B200KV_ERR_WORKSPACE;
+  if (mxfp4_gemm_wide_workspace_bytes(M, K) > kNoAllocBytes) return B200KV_ERR_WORKSPACE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxScratchDevices) {
+    cudaGetLastError();
+    return B200KV_ERR_NO_DEVICE;
+  }
+  void* ptr = nullptr;
+  {
+    // set-up, once per device, with that device current: the array's device address
+    std::lock_guard<std::mutex> g(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_wide_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return B200KV_ERR_NO_DEVICE;
+      }
+      g_scratch_ptr[dev] = p;
+    }
+    ptr = g_scratch_ptr[dev];
+  }
+  // the pre-pass rewrites every byte the GEMM reads: nothing needs clearing
+  return mxfp4_gemm_wide_launch(W, Sp, X, x_ld, ptr, kNoAllocBytes, Out, N, K, M, stream);
+}
+
 }  // namespace b200kv

@@ -182,6 +182,20 @@ int b200kv_mxfp4_gemm_wide(const void* W, const void* packed_scales, const void*
                            void* workspace, size_t workspace_bytes, void* out, int N, int K, int M,
                            void* stream);
 
+/* b200kv_mxfp4_gemm_wide without a caller workspace, for callers that cannot
+ * allocate device memory: a serving engine that has already given all free HBM
+ * to its KV-cache pool, or a host that binds this C ABI and has no device
+ * allocator.  No counterpart in the reference.  The activation terms go to a
+ * scratch array inside this library (4.3 MB, held on every GPU that loads the
+ * library until exit), so M <= 128 and K <= 16384; larger sizes return
+ * B200KV_ERR_WORKSPACE.  Allocates nothing.  Its first call on a device looks
+ * up the array's device address (make that call before any stream capture).
+ * All calls on a device share the array: calls that overlap on the GPU (on
+ * different streams) race, calls ordered on one stream do not.  Each call
+ * rewrites all of the scratch it reads, so nothing has to start at zero. */
+int b200kv_mxfp4_gemm_wide_noalloc(const void* W, const void* packed_scales, const void* X,
+                                   int64_t x_stride, void* out, int N, int K, int M, void* stream);
+
 /* ---- fp8 paged-KV causal prefill attention -----------------------------------
  *
  * For every sequence s with query rows cu_seqlens_q[s] .. cu_seqlens_q[s+1]-1
