@@ -57,7 +57,7 @@ namespace {
 constexpr int kRows = 128;            // weight rows per MMA tile (MMA M)
 constexpr int kTok = 64;              // activation rows per token tile
 constexpr int kBRows = 2 * kTok;      // B rows of a token tile: term t of token j is row 64 t + j (MMA N)
-constexpr int kKStep = 128;           // K per stage: one A box, one B box and one scale atom each
+constexpr int kKStep = 128;           // K per step: one A box, one B box and one scale atom each
 constexpr int kABox = kRows * 128;    // A box in shared memory (e2m1 codes, 16 per 16-byte chunk)
 constexpr int kABoxTx = kRows * 64;   // bytes the TMA signals for it (the packed size)
 constexpr int kBBox = kBRows * 128;   // B box: e4m3 codes, 128 B rows, 128-byte swizzle
@@ -189,7 +189,8 @@ struct GemmArgs {
   __nv_bfloat16* Out;  // [M, N]
   int N, K, M;
   int nsteps;          // K / 128
-  int sps;             // stages (K steps) per K-slice
+  int sps;             // steps per K-slice
+  int kb;              // steps per stage (1 or 2)
   int nstages;         // ring depth
   int wtiles;          // ceil(N / 128)
   int ttiles;          // ceil(M / 64)
@@ -198,15 +199,28 @@ struct GemmArgs {
 // Dynamic shared memory: the stage ring, then (ks > 1) the receive area of the
 // K-slice reduction, recv[src rank][band row][tokens] in fp32, whose 16-byte
 // chunks are rotated by (band row & 7) so the finishing reads of 32
-// consecutive rows hit distinct banks.
+// consecutive rows hit distinct banks.  A stage holds kb steps: the A boxes
+// (step q, weight tile mt), the B boxes (q, token tile nt), then the scale
+// atoms, each operand's kb atoms contiguous (one bulk copy each, as they lie
+// in memory).  Every mbarrier round trip of the ring costs a few hundred ns
+// on the single-thread producer and issuer, so a stage must carry enough
+// weight bytes to cover it.
 template <int MT, int NT>
 struct GemmLayout {
-  static constexpr int kStage =
-      (MT * kABox + NT * kBBox + (MT + NT) * kAtom + 1023) / 1024 * 1024;
-  static constexpr int kSfa = MT * kABox + NT * kBBox;  // scale atoms within a stage
-  int nstages, ks;
+  int nstages, ks, kb;
+  __host__ __device__ int stage() const {
+    return (kb * (MT * kABox + NT * kBBox + (MT + NT) * kAtom) + 1023) / 1024 * 1024;
+  }
+  __host__ __device__ int a_off(int mt, int q) const { return (q * MT + mt) * kABox; }
+  __host__ __device__ int b_off(int nt, int q) const { return kb * MT * kABox + (q * NT + nt) * kBBox; }
+  __host__ __device__ int sfa_off(int mt, int q) const {
+    return kb * (MT * kABox + NT * kBBox) + (mt * kb + q) * kAtom;
+  }
+  __host__ __device__ int sfb_off(int nt, int q) const {
+    return kb * (MT * kABox + NT * kBBox) + ((MT + nt) * kb + q) * kAtom;
+  }
   __host__ __device__ int band() const { return (MT * kRows + ks - 1) / ks; }
-  __host__ __device__ size_t recv() const { return (size_t)nstages * kStage; }
+  __host__ __device__ size_t recv() const { return (size_t)nstages * stage(); }
   __host__ __device__ size_t bytes() const {
     return recv() + (ks > 1 ? (size_t)ks * band() * NT * kTok * 4 : 0) + 1024;
   }
@@ -228,10 +242,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int rank = blockIdx.x, ksz = gridDim.x;  // K-slice = rank in the cluster (ks, 1, 1)
   const int wt0 = blockIdx.y * MT, tt0 = blockIdx.z * NT;
   const int s_begin = rank * a.sps;
-  const int ns = max(0, min(a.nsteps, s_begin + a.sps) - s_begin);
+  const int ns = max(0, min(a.nsteps, s_begin + a.sps) - s_begin);  // 128-k steps of this slice
+  const int kb = a.kb;
+  const int nstg = (ns + kb - 1) / kb;  // stages of this slice
   const int mt_n = min(MT, a.wtiles - wt0), nt_n = min(NT, a.ttiles - tt0);
   const int nst = a.nstages;
-  const L lay{nst, ksz};
+  const L lay{nst, ksz, kb};
+  const int stage_bytes = lay.stage();
   const int band = lay.band();
   const int my_rows = max(0, min(band, MT * kRows - rank * band));
   float* recv = reinterpret_cast<float*>(dsm + lay.recv());
@@ -260,40 +277,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && ns > 0) {
       tma_prefetch_desc(&wmap);
       tma_prefetch_desc(&xmap);
-      const uint32_t tx = (uint32_t)(mt_n * (kABoxTx + kAtom) + nt_n * (kBBox + kAtom));
+      auto steps_of = [&](int s) { return min(kb, ns - s * kb); };
+      auto tx_of = [&](int s) {
+        return (uint32_t)(steps_of(s) * (mt_n * (kABoxTx + kAtom) + nt_n * (kBBox + kAtom)));
+      };
       auto issue_w = [&](int s) {
-        uint8_t* st = dsm + (size_t)(s % nst) * L::kStage;
+        uint8_t* st = dsm + (size_t)(s % nst) * stage_bytes;
         uint64_t* bar = &full_bar[s % nst];
-        const int k = s_begin + s;
+        const int k = s_begin + s * kb, nq = steps_of(s);
         for (int mt = 0; mt < mt_n; ++mt) {
-          tma_load_2d(st + mt * kABox, &wmap, k * kKStep, (wt0 + mt) * kRows, bar);
-          bulk_g2s(st + L::kSfa + mt * kAtom, a.Sp + ((size_t)(wt0 + mt) * a.nsteps + k) * kAtom, kAtom, bar);
+          for (int q = 0; q < nq; ++q)
+            tma_load_2d(st + lay.a_off(mt, q), &wmap, (k + q) * kKStep, (wt0 + mt) * kRows, bar);
+          bulk_g2s(st + lay.sfa_off(mt, 0), a.Sp + ((size_t)(wt0 + mt) * a.nsteps + k) * kAtom,
+                   (uint32_t)(nq * kAtom), bar);
         }
       };
       auto issue_x = [&](int s) {
-        uint8_t* st = dsm + (size_t)(s % nst) * L::kStage;
+        uint8_t* st = dsm + (size_t)(s % nst) * stage_bytes;
         uint64_t* bar = &full_bar[s % nst];
-        const int k = s_begin + s;
+        const int k = s_begin + s * kb, nq = steps_of(s);
         for (int nt = 0; nt < nt_n; ++nt) {
-          tma_load_2d(st + MT * kABox + nt * kBBox, &xmap, k * kKStep, (tt0 + nt) * kBRows, bar);
-          bulk_g2s(st + L::kSfa + (MT + nt) * kAtom, a.Xs + ((size_t)(tt0 + nt) * a.nsteps + k) * kAtom,
-                   kAtom, bar);
+          for (int q = 0; q < nq; ++q)
+            tma_load_2d(st + lay.b_off(nt, q), &xmap, (k + q) * kKStep, (tt0 + nt) * kBRows, bar);
+          bulk_g2s(st + lay.sfb_off(nt, 0), a.Xs + ((size_t)(tt0 + nt) * a.nsteps + k) * kAtom,
+                   (uint32_t)(nq * kAtom), bar);
         }
       };
       // weights and their scales are load-time data: the first ring's worth
       // streams before this grid waits on the pre-pass that writes the terms
-      const int pre = min(ns, nst);
+      const int pre = min(nstg, nst);
       for (int s = 0; s < pre; ++s) {
-        mbar_arrive_expect_tx(&full_bar[s], tx);
+        mbar_arrive_expect_tx(&full_bar[s], tx_of(s));
         issue_w(s);
       }
       griddep_wait();
       for (int s = 0; s < pre; ++s) issue_x(s);
       int issued = pre;
-      for (int s = pre; s < ns; ++s) {
+      for (int s = pre; s < nstg; ++s) {
         const int slot = s % nst;
         if (!mbar_wait_bounded(&empty_bar[slot], ((s / nst) - 1) & 1)) break;  // stop issuing
-        mbar_arrive_expect_tx(&full_bar[slot], tx);
+        mbar_arrive_expect_tx(&full_bar[slot], tx_of(s));
         issue_w(s);
         issue_x(s);
         issued = s + 1;
@@ -306,28 +329,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && ns > 0) {
       const uint32_t ring = smem_u32(dsm);
       bool failed = false;
-      for (int s = 0; s < ns; ++s) {
+      for (int s = 0; s < nstg; ++s) {
         const int slot = s % nst;
         if (!mbar_wait_bounded(&full_bar[slot], (s / nst) & 1)) {
           failed = true;  // issue nothing more
           break;
         }
         tc::fence_after_sync();
-        const uint32_t st = ring + (uint32_t)slot * L::kStage;
-        const uint32_t tsf = tbase + kSfCol + 4 * (MT + NT) * slot;
-        for (int mt = 0; mt < mt_n; ++mt) tmem_cp_atom(tsf + 4 * mt, sdesc_atom(st + L::kSfa + mt * kAtom));
-        for (int nt = 0; nt < nt_n; ++nt)
-          tmem_cp_atom(tsf + 4 * (MT + nt), sdesc_atom(st + L::kSfa + (MT + nt) * kAtom));
-#pragma unroll
-        for (int kq = 0; kq < 4; ++kq) {  // K = 32 each, scale byte kq of the atoms
-          const uint32_t sf = (uint32_t)kq;
+        const int nq = min(kb, ns - s * kb);
+        const uint32_t st = ring + (uint32_t)slot * (uint32_t)stage_bytes;
+        // scale atoms of this slot: A (mt, q) at column 4 (mt kb + q), B (nt, q) at 4 ((MT + nt) kb + q)
+        const uint32_t tsf = tbase + kSfCol + 4 * (MT + NT) * kb * slot;
+        for (int q = 0; q < nq; ++q) {
           for (int mt = 0; mt < mt_n; ++mt)
-            for (int nt = 0; nt < nt_n; ++nt)
-              mma_mxf8f6f4(tbase + (uint32_t)(mt * NT + nt) * kBRows,
-                           tc::sdesc_sw128(st + mt * kABox + 32 * kq, 16, 1024),
-                           tc::sdesc_sw128(st + MT * kABox + nt * kBBox + 32 * kq, 16, 1024),
-                           idesc_mxf8f6f4(kRows, kBRows, sf), (s > 0 || kq > 0) ? 1u : 0u,
-                           (tsf + 4 * mt) | (sf << 30), (tsf + 4 * (MT + nt)) | (sf << 30));
+            tmem_cp_atom(tsf + 4 * (mt * kb + q), sdesc_atom(st + lay.sfa_off(mt, q)));
+          for (int nt = 0; nt < nt_n; ++nt)
+            tmem_cp_atom(tsf + 4 * ((MT + nt) * kb + q), sdesc_atom(st + lay.sfb_off(nt, q)));
+        }
+        for (int q = 0; q < nq; ++q) {
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {  // K = 32 each, scale byte kq of the atoms
+            const uint32_t sf = (uint32_t)kq;
+            for (int mt = 0; mt < mt_n; ++mt)
+              for (int nt = 0; nt < nt_n; ++nt)
+                mma_mxf8f6f4(tbase + (uint32_t)(mt * NT + nt) * kBRows,
+                             tc::sdesc_sw128(st + lay.a_off(mt, q) + 32 * kq, 16, 1024),
+                             tc::sdesc_sw128(st + lay.b_off(nt, q) + 32 * kq, 16, 1024),
+                             idesc_mxf8f6f4(kRows, kBRows, sf), (s > 0 || q > 0 || kq > 0) ? 1u : 0u,
+                             (tsf + 4 * (mt * kb + q)) | (sf << 30), (tsf + 4 * ((MT + nt) * kb + q)) | (sf << 30));
+          }
         }
         tc::commit(&empty_bar[slot]);
       }
@@ -474,23 +504,27 @@ int max_active_clusters(int ks, size_t smem) {
 }
 
 struct Plan {
-  int mt = 0, nt = 0, ks = 0, nst = 0;
+  int mt = 0, nt = 0, ks = 0, nst = 0, kb = 1;
   size_t smem = 0;
 };
 
 template <int MT, int NT>
-void consider(Plan& best, double& best_cost, const GemmArgs& a, int sms, int force_ks, int force_st) {
+void consider(Plan& best, double& best_cost, const GemmArgs& a, int sms, int force_ks, int force_st,
+              int force_kb) {
   const int tiles = cdiv(a.wtiles, MT) * cdiv(a.ttiles, NT);
-  for (int ks = 1; ks <= 8 && ks <= a.nsteps; ++ks) {
+  for (int ks = 1; ks <= 8 && ks <= a.nsteps; ++ks)
+  for (int kb = 1; kb <= 2; ++kb) {
     if (force_ks && ks != force_ks) continue;
+    if (force_kb && kb != force_kb) continue;
     const int sps = cdiv(a.nsteps, ks);
-    const GemmLayout<MT, NT> l0{0, ks};
+    const int stages = cdiv(sps, kb);
+    const GemmLayout<MT, NT> l0{0, ks, kb};
     const size_t fixed = l0.bytes();
-    const int fit = (int)((kSmemMax - (long)fixed) / GemmLayout<MT, NT>::kStage);
-    int nst = min(kMaxStages, min(sps, fit));
+    const int fit = (int)((kSmemMax - (long)fixed) / l0.stage());
+    int nst = min(kMaxStages, min(stages, fit));
     if (force_st) nst = min(nst, force_st);
-    if (nst < min(2, sps)) continue;
-    const size_t smem = GemmLayout<MT, NT>{nst, ks}.bytes();
+    if (nst < 1) continue;
+    const size_t smem = GemmLayout<MT, NT>{nst, ks, kb}.bytes();
     const int resident = max_active_clusters<MT, NT>(ks, smem);
     if (resident <= 0) continue;
     const int waves = cdiv(tiles, resident);
@@ -498,15 +532,18 @@ void consider(Plan& best, double& best_cost, const GemmArgs& a, int sms, int for
     // per stage: weight bytes at this CTA's share of the HBM bandwidth
     // (about 360 cycles per 8 KB when every SM streams), or the MMAs
     // (4 x 64 cycles per 128 x 128 x 128 block), whichever is longer
+    // and at least the ring's round trip (about 700 cycles per stage)
     const double fill = min(1.0, (double)active / sms);
-    const double step = fmax(MT * 360.0 * fill, MT * NT * 256.0);
-    const double cost = waves * (sps * step + 800.0) + (ks > 1 ? 150.0 * ks * MT * NT : 0.0);
+    double stage_cost = fmax(fmax(kb * MT * 360.0 * fill, kb * MT * NT * 256.0), 700.0);
+    if (nst < 2 && stages > 1) stage_cost *= 2.0;  // a one-stage ring does not overlap loads and MMAs
+    const double cost = waves * (stages * stage_cost + 800.0) + (ks > 1 ? 150.0 * ks * MT * NT : 0.0);
     if (cost < best_cost - 1e-9) {
       best_cost = cost;
       best.mt = MT;
       best.nt = NT;
       best.ks = ks;
       best.nst = nst;
+      best.kb = kb;
       best.smem = smem;
     }
   }
@@ -592,20 +629,22 @@ int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t
   // plan: tile shape (MT weight tiles x NT token tiles), K-split, ring depth
   const int force_mt = env_int("B200KV_GEMM_MT", 0), force_nt = env_int("B200KV_GEMM_NT", 0);
   const int force_ks = env_int("B200KV_GEMM_KSPLIT", 0), force_st = env_int("B200KV_GEMM_STAGES", 0);
+  const int force_kb = env_int("B200KV_GEMM_KB", 0);
   Plan p;
   double cost = 1e30;
   auto want = [&](int mt, int nt) {
     return (!force_mt || force_mt == mt) && (!force_nt || force_nt == nt);
   };
-  if (want(1, 1)) consider<1, 1>(p, cost, a, sms, force_ks, force_st);
-  if (a.wtiles > 1 && want(2, 1)) consider<2, 1>(p, cost, a, sms, force_ks, force_st);
-  if (a.ttiles > 1 && want(1, 2)) consider<1, 2>(p, cost, a, sms, force_ks, force_st);
+  if (want(1, 1)) consider<1, 1>(p, cost, a, sms, force_ks, force_st, force_kb);
+  if ((a.wtiles > 1 || force_mt == 2) && want(2, 1)) consider<2, 1>(p, cost, a, sms, force_ks, force_st, force_kb);
+  if ((a.ttiles > 1 || force_nt == 2) && want(1, 2)) consider<1, 2>(p, cost, a, sms, force_ks, force_st, force_kb);
   if (p.ks == 0) return B200KV_ERR_UNSUPPORTED;
   a.sps = cdiv(a.nsteps, p.ks);
   a.nstages = p.nst;
+  a.kb = p.kb;
   if (env_int("B200KV_GEMM_PLAN", 0))
-    fprintf(stderr, "[b200kv] mxfp4_gemm_wide N=%d K=%d M=%d: MT=%d NT=%d ks=%d stages=%d smem=%zu\n", N, K,
-            M, p.mt, p.nt, p.ks, p.nst, p.smem);
+    fprintf(stderr, "[b200kv] mxfp4_gemm_wide N=%d K=%d M=%d: MT=%d NT=%d ks=%d kb=%d stages=%d smem=%zu\n", N,
+            K, M, p.mt, p.nt, p.ks, p.kb, p.nst, p.smem);
 
   CUtensorMap wm, xm;
   if (!encode_e2m1_unpacked_2d(&wm, W, (uint64_t)K, (uint64_t)N, (uint64_t)(K / 2), kRows) ||

@@ -10,8 +10,9 @@ With FP8KV_HIPW4=1 the CUDA implementation of the op radiance::mxfp4_linear
   * the checkpoint's scale layout [K/32, N] is repacked once and cached by
     (data_ptr, shape), never while a CUDA graph is being captured
     (fp8kv_hipw4.py:32-43): into tensor-core scale atoms for the block-scaled
-    tcgen05 kernel (h4mv.mxfp4_gemm) when K % 256 == 0 and no scale byte is
-    0 or 255, else into [N, K/32] for the CUDA-core kernel (h4mv.mxfp4_gemv);
+    tcgen05 kernels (h4mv.mxfp4_gemm) when K % 128 == 0 (K % 256 for the
+    M <= 8 kernel) and no scale byte is 0 or 255, else into [N, K/32] for the
+    CUDA-core kernel (h4mv.mxfp4_gemv);
   * out = torch.empty(M, N, bf16) and one launch on the current stream;
   * everything else goes to the op's original CUDA body.
 
@@ -22,8 +23,10 @@ The reference stole the body of the radiance fork's op once that module
 appeared (a 1500 x 0.2 s poll, fp8kv_hipw4.py:45-59).  The fork is not part
 of this environment, so when `radiance_mxfp4` cannot be imported this module
 defines the op schema itself; the original body is then `mxfp4_linear_chunked`,
-which runs the same B200 kernel over 8-row slices of x, so no shape falls back
-to a CPU or Python implementation.
+which runs the wide-batch tensor-core GEMM (h4mv.mxfp4_gemm_wide, the
+reference's dequant + matmul path for M > 8) or, for weights off the
+tensor-core path, the B200 matvec over 8-row slices of x, so no shape falls
+back to a CPU or Python implementation.
 """
 import os
 import sys
@@ -66,7 +69,7 @@ def scale_t_for(s):
 def packed_scales_for(s, N, K):
     """weight_scale [K/32, N] -> the tensor-core scale atoms (h4mv.pack_scales),
     cached like scale_t_for; False when the weight cannot take the
-    tensor-core path (K % 256, or scale bytes 0 / 255), None during capture."""
+    tensor-core path (K % 128, or scale bytes 0 / 255), None during capture."""
     import h4mv
     key = ("p", s.data_ptr(), tuple(s.shape), s.device)
     ent = _repack_cache.get(key)
@@ -75,7 +78,7 @@ def packed_scales_for(s, N, K):
     if _capturing(s):
         return None
     packed = False
-    if K % 256 == 0:
+    if K % 128 == 0:
         p, edge = h4mv.pack_scales(s.contiguous(), N, K, h4mv.SCALES_CHECKPOINT)
         packed = False if edge else p
     if len(_repack_cache) > 512:
@@ -97,13 +100,18 @@ def eligible(x, weight, weight_scale, m_limit):
 
 
 def mxfp4_linear_chunked(x, weight, weight_scale, wref=None):
-    """x [M, K] @ dequant(weight, weight_scale)^T for any M, through the B200
-    matvec on 8-row slices of x (weight_scale in the checkpoint layout)."""
+    """x [M, K] @ dequant(weight, weight_scale)^T for any M (weight_scale in
+    the checkpoint layout): M > 8 on the wide-batch tensor-core GEMM when the
+    weight's scales pack, else the B200 matvec on 8-row slices of x."""
     import torch
 
     import h4mv
     M = x.shape[0]
-    N = weight.shape[0]
+    N, K = weight.shape[0], weight.shape[1] * 2
+    if M > h4mv.MAX_M and weight.data_ptr() % 16 == 0:
+        packed = packed_scales_for(weight_scale, N, K)
+        if packed is not None and packed is not False:
+            return h4mv.mxfp4_gemm_wide(x.contiguous().to(torch.bfloat16), weight, packed)
     st = scale_t_for(weight_scale)
     if st is None:
         raise RuntimeError("mxfp4_linear: scale repack needed during CUDA graph capture; "
@@ -153,8 +161,10 @@ def make_patched(body, m_limit):
             if eligible(x, weight, weight_scale, m_limit):
                 N, K = weight.shape[0], weight.shape[1] * 2
                 packed = packed_scales_for(weight_scale, N, K) if weight.data_ptr() % 16 == 0 else False
-                if packed is not None and packed is not False:
+                if packed is not None and packed is not False and (K % 256 == 0 or x.shape[0] > h4mv.MAX_M):
                     out = h4mv.mxfp4_gemm(x, weight, packed)
+                elif packed is not None and packed is not False:
+                    out = h4mv.mxfp4_gemv(x, weight, scale_t_for(weight_scale))
                 else:
                     st = scale_t_for(weight_scale) if packed is False else None
                     out = h4mv.mxfp4_gemv(x, weight, st) if st is not None else None

@@ -122,13 +122,19 @@ def test_ragged(cuda, N, K, M):
     assert ok, worst
 
 
+@pytest.mark.parametrize("kb", [1, 2])
+@pytest.mark.parametrize("M", [130, 100, 40])
 @pytest.mark.parametrize("mt,nt,ks", [(1, 1, 1), (1, 1, 3), (2, 1, 5), (1, 2, 2), (2, 1, 8), (1, 1, 7),
                                       (1, 2, 1)])
-def test_tile_shapes_and_k_splits_bit_exact(cuda, monkeypatch, mt, nt, ks):
+def test_tile_shapes_and_k_splits_bit_exact(cuda, monkeypatch, mt, nt, ks, M, kb):
+    """Three token-tile counts (3, 2, 1) with ragged last tiles; one or two
+    128-k steps per ring stage (16 steps over ks slices leave partial last
+    stages)."""
     monkeypatch.setenv("B200KV_GEMM_MT", str(mt))
     monkeypatch.setenv("B200KV_GEMM_NT", str(nt))
     monkeypatch.setenv("B200KV_GEMM_KSPLIT", str(ks))
-    W, St, X, ref = _integer_case(1000, 2048, 130, seed=mt * 100 + nt * 10 + ks)
+    monkeypatch.setenv("B200KV_GEMM_KB", str(kb))
+    W, St, X, ref = _integer_case(1000, 2048, M, seed=mt * 100 + nt * 10 + ks + M)
     Y = _run(W, St, X, cuda)
     assert torch.equal(Y, ref)
 

@@ -281,6 +281,22 @@ def test_hipw4_chunked_body_covers_any_m(libpath, monkeypatch):
     assert rows == [(8, 8, True, True), (8, 8, True, True), (3, 3, True, True)]
 
 
+def test_hipw4_chunked_body_takes_wide_gemm(libpath, monkeypatch):
+    """M > 8 with scales that pack goes to the wide-batch tensor-core GEMM."""
+    import fp8kv_hipw4 as hw
+    import h4mv
+    packed = torch.zeros(4, dtype=torch.uint8)
+    seen = []
+    monkeypatch.setattr(hw, "packed_scales_for", lambda s, N, K: packed)
+    monkeypatch.setattr(h4mv, "mxfp4_gemm_wide", lambda x, w, p: seen.append((tuple(x.shape), p is packed)) or "wide")
+    monkeypatch.setattr(h4mv, "mxfp4_gemv", lambda *a, **k: "slices")
+    N, K = 16, 256
+    w = torch.zeros((N, K // 2), dtype=torch.uint8)
+    s = torch.zeros((K // 32, N), dtype=torch.uint8)
+    assert hw.mxfp4_linear_chunked(torch.zeros((19, K), dtype=torch.bfloat16), w, s) == "wide"
+    assert seen == [((19, K), True)]
+
+
 def test_hipw4_defines_op_when_fork_absent():
     env = dict(os.environ, FP8KV_HIPW4="1", FP8KV_OVERRIDE="0", PYTHONPATH=PKG)
     code = ("import torch, fp8kv_hipw4 as hw; "
