@@ -295,6 +295,38 @@ def prefill_part(dev, steps, warmup, barrier=None):
     return ms * 1e3, prefill_flops(lens)
 
 
+WIDE_M = 64
+
+
+def wide_gemm_part(dev, steps, warmup, barrier=None, tp=1, layers=3):
+    """Config 2 at M = WIDE_M: this rank's four 7B MXFP4 projections (config-2
+    weights: codes uniform, scales 2^-8..2^-2, packed once) on the wide-batch
+    tensor-core GEMM, `layers` distinct weight sets cycled so the weights stream
+    from HBM (3 layers = 327 MB at tp 1 against the 126 MB L2).  Returns (us per
+    layer of four GEMMs, algorithmic bytes per layer, FLOPs per layer)."""
+    import h4mv
+    shapes = rank_shapes(tp)
+    g = torch.Generator(device=dev).manual_seed(5)
+    sets = []
+    for _ in range(layers):
+        for _, N, K in shapes:
+            W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
+            S = torch.randint(119, 126, (K // 32, N), dtype=torch.uint8, device=dev, generator=g)
+            P, _ = h4mv.pack_scales(S, N, K, h4mv.SCALES_CHECKPOINT)
+            x = torch.randn(WIDE_M, K, device=dev, generator=g).to(torch.bfloat16)
+            sets.append((x, W, P, torch.empty(WIDE_M, N, dtype=torch.bfloat16, device=dev)))
+
+    def call():
+        for x, W, P, out in sets:
+            h4mv.mxfp4_gemm_wide(x, W, P, out=out)
+    graph = capture(call)
+    ms = time_graph(graph, max(steps // 2, 3), warmup, barrier) / layers
+    del graph
+    nbytes = sum(gemv_bytes(N, K, WIDE_M) for _, N, K in shapes)
+    flops = sum(2 * WIDE_M * N * K for _, N, K in shapes)
+    return ms * 1e3, nbytes, flops
+
+
 DECODE_PROMPT, DECODE_TOKENS = 4096, 256
 
 
@@ -453,6 +485,8 @@ def run_b200(args):
                if g_comm is not None else None)
     us_pre, flops_pre = prefill_part(dev, args.steps, 2, barrier)
     us_pre = max_over_ranks(us_pre, dist_on, dev)
+    us_wide, bytes_wide, flops_wide = wide_gemm_part(dev, args.steps, 2, barrier, args.tp)
+    us_wide = max_over_ranks(us_wide, dist_on, dev)
     ms_tok, _ = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None)
     ms_tok = max_over_ranks(ms_tok, dist_on, dev)
     # one rank's bytes (the per-GPU roofline)
@@ -542,6 +576,18 @@ def run_b200(args):
                                  / peaks.get("bf16_tflops", 1590.0),
                                  "note": "timed outside the decode step (not part of value); "
                                          "each rank runs the full call"},
+                "mxfp4_gemm_m64": {"workload": f"config 2 at M = {WIDE_M}: qkv, o, gate_up, down "
+                                               "(this rank's shards) on the wide-batch GEMM "
+                                               "(tcgen05 kind::mxf8f6f4, x as two exact e4m3 terms)",
+                                   "us_per_layer": us_wide,
+                                   "gbs": bytes_wide / (us_wide * 1e-6) / 1e9,
+                                   "hbm_frac": bytes_wide / (us_wide * 1e-6) / 1e9 / hbm_peak,
+                                   "tflops": flops_wide / (us_wide * 1e-6) / 1e12,
+                                   "tensor_frac": flops_wide / (us_wide * 1e-6) / 1e12
+                                   / peaks.get("bf16_tflops", 1590.0),
+                                   "note": "timed outside the decode step (not part of value); "
+                                           "tflops counts 2 M N K (the tensor core runs two e4m3 "
+                                           "terms at twice the bf16 rate, so bf16 peak is the bound)"},
                 "decode_7b": {"workload": f"config 4: full 7B MXFP4 decoder (RMSNorm, qkv, RoPE + fp8 "
                                           f"KV write, decode attention, o, SwiGLU MLP, bf16 lm_head "
                                           f"128256, greedy argmax), batch {args.batch}, "
