@@ -327,6 +327,133 @@ def wide_gemm_part(dev, steps, warmup, barrier=None, tp=1, layers=3):
     return ms * 1e3, nbytes, flops
 
 
+SERVE_DECODES, SERVE_PREFILLS, SERVE_PREFILL_LEN, SERVE_CTX = 60, 4, 2048, (2048, 32768)
+
+
+def serving_part(args, dev, barrier, layers=32, steps=2):
+    """Config 5, the serving shape on the 7B model: 64 sequences per step, 60
+    decoding (contexts ~U[2k, 32k], seeded) and 4 new 2048-token prefills, over
+    one fp8 paged pool per layer with a fragmented random block table (every
+    sequence's pages drawn from one random permutation).  A step is `layers` x
+    [qkv GEMM (M = 8252 tokens) -> KV write of the 8252 new tokens ->
+    attention -> o GEMM -> gate_up GEMM -> down GEMM] on this rank's shards
+    (tensor parallel: kv-head attention, NCCL allreduce of the o and down
+    outputs); the pages already in the pool are synthetic fp8, the prompt KV a
+    real engine would have written.  Attention runs two ways: "mixed", one
+    varlen call for the whole batch (decode tokens as one-token prefills, what
+    the vLLM forward patch does), and "split", the decode kernel for the 60
+    decode rows plus the varlen kernel for the 4 prefills.  Eager launches,
+    CUDA events, max over ranks.  Returns a dict for the bench line."""
+    import _decode
+    import fp8kv_prefill
+    import h4mv
+    import kv_cache
+    tp = args.tp
+    hq, hkv, inter = HQ // tp, HKV // tp, 14336 // tp
+    gc = torch.Generator().manual_seed(21)
+    ctx = torch.randint(SERVE_CTX[0], SERVE_CTX[1] + 1, (SERVE_DECODES,), generator=gc).tolist()
+    seq = [c + 1 for c in ctx] + [SERVE_PREFILL_LEN] * SERVE_PREFILLS
+    qlens = [1] * SERVE_DECODES + [SERVE_PREFILL_LEN] * SERVE_PREFILLS
+    T, NS = sum(qlens), len(seq)
+    nblk = [-(-L // PBLK) for L in seq]
+    NB = sum(nblk)
+    perm = torch.randperm(NB, generator=gc).to(torch.int32)
+    bt = torch.zeros(NS, max(nblk), dtype=torch.int32)
+    slots, pos = [], 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[pos:pos + n]
+        pos += n
+        first = seq[i] - qlens[i]  # position of the step's first new token
+        t = torch.arange(first, seq[i])
+        slots.append(bt[i, t // PBLK].long() * PBLK + t % PBLK)
+    slots = torch.cat(slots).to(dev)
+    bt = bt.to(dev)
+    seq_lens = torch.tensor(seq, dtype=torch.int32, device=dev)
+    cu = torch.tensor([0] + torch.tensor(qlens).cumsum(0).tolist(), dtype=torch.int32, device=dev)
+    qsl_dec = torch.arange(SERVE_DECODES + 1, dtype=torch.int32, device=dev)
+    cu_pre = (cu[SERVE_DECODES:] - SERVE_DECODES).contiguous()
+    ks = torch.full((1,), 1 / 16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(22)
+    lays = []
+    for _ in range(layers):
+        lay = {}
+        for name, N, K in rank_shapes(tp):
+            W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
+            S = torch.randint(119, 126, (K // 32, N), dtype=torch.uint8, device=dev, generator=g)
+            lay[name] = (W, h4mv.pack_scales(S, N, K, h4mv.SCALES_CHECKPOINT)[0])
+        for name in ("k", "v"):  # synthetic prompt KV (codes 0..125: finite, up to 416/16)
+            pool = torch.empty(NB, PBLK, hkv, D, dtype=torch.uint8, device=dev)
+            lay[name] = pool.random_(0, 126, generator=g).view(torch.float8_e4m3fn)
+        lays.append(lay)
+    x = torch.randn(T, 4096, device=dev, generator=g).to(torch.bfloat16)
+    qkv = torch.empty(T, (hq + 2 * hkv) * D, dtype=torch.bfloat16, device=dev)
+    attn = torch.empty(T, hq, D, dtype=torch.bfloat16, device=dev)
+    o = torch.empty(T, 4096, dtype=torch.bfloat16, device=dev)
+    gu = torch.empty(T, 2 * inter, dtype=torch.bfloat16, device=dev)
+    dn = torch.empty(T, 4096, dtype=torch.bfloat16, device=dev)
+    q = qkv[:, :hq * D].view(T, hq, D)
+    kn = qkv[:, hq * D:(hq + hkv) * D].view(T, hkv, D)
+    vn = qkv[:, (hq + hkv) * D:].view(T, hkv, D)
+    sm = D ** -0.5
+    allreduce = None
+    if tp > 1:
+        import torch.distributed as dist
+        allreduce = dist.all_reduce
+
+    def attention(L, mode):
+        if mode == "mixed":
+            fp8kv_prefill.prefill_attention(q, L["k"], L["v"], attn, cu, seq_lens, bt, ks, ks, sm,
+                                            max_qlen=SERVE_PREFILL_LEN)
+        else:
+            _decode.decode_attention(q, L["k"], L["v"], attn, qsl_dec, seq_lens[:SERVE_DECODES],
+                                     bt[:SERVE_DECODES], ks, ks, sm, out_by_qsl=True,
+                                     max_seq_len_hint=SERVE_CTX[1] + 1)
+            fp8kv_prefill.prefill_attention(q[SERVE_DECODES:], L["k"], L["v"], attn[SERVE_DECODES:], cu_pre,
+                                            seq_lens[SERVE_DECODES:], bt[SERVE_DECODES:], ks, ks, sm,
+                                            max_qlen=SERVE_PREFILL_LEN)
+
+    def step(mode, part="all"):
+        for L in lays:
+            if part in ("all", "gemm"):
+                h4mv.mxfp4_gemm_wide(x, *L["qkv"], out=qkv)
+            if part in ("all", "attn"):
+                kv_cache.reshape_and_cache_flash(kn, vn, L["k"], L["v"], slots, "fp8", ks, ks)
+                attention(L, mode)
+            if part in ("all", "gemm"):
+                h4mv.mxfp4_gemm_wide(attn.view(T, hq * D), *L["o"], out=o)
+                if allreduce:
+                    allreduce(o)
+                h4mv.mxfp4_gemm_wide(o, *L["gate_up"], out=gu)
+                h4mv.mxfp4_gemm_wide(gu[:, :inter], *L["down"], out=dn)  # stand-in for SwiGLU(gu)
+                if allreduce:
+                    allreduce(dn)
+
+    def timed(mode, part):
+        step(mode, part)
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step(mode, part)
+        e1.record()
+        torch.cuda.synchronize()
+        if barrier:
+            barrier()
+        return e0.elapsed_time(e1) / steps
+
+    res = {"mixed": timed("mixed", "all"), "split": timed("split", "all"),
+           "attn_mixed": timed("mixed", "attn"), "attn_split": timed("split", "attn"),
+           "gemm": timed("split", "gemm")}
+    kv_bytes = layers * sum(c + 1 for c in ctx) * hkv * D * 2
+    pre_flops = layers * 4 * D * hq * SERVE_PREFILLS * SERVE_PREFILL_LEN * (SERVE_PREFILL_LEN + 1) // 2
+    gemm_flops = layers * sum(2 * T * N * K for _, N, K in rank_shapes(tp))
+    del lays
+    torch.cuda.empty_cache()
+    return res, T, kv_bytes, pre_flops, gemm_flops
+
+
 DECODE_PROMPT, DECODE_TOKENS = 4096, 256
 
 
@@ -489,6 +616,10 @@ def run_b200(args):
     us_wide = max_over_ranks(us_wide, dist_on, dev)
     ms_tok, _ = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None)
     ms_tok = max_over_ranks(ms_tok, dist_on, dev)
+    serve = None
+    if args.serving == "on":
+        res, serve_tokens, serve_kv, serve_pre, serve_gemm = serving_part(args, dev, barrier)
+        serve = {k: max_over_ranks(v, dist_on, dev) for k, v in res.items()}
     # one rank's bytes (the per-GPU roofline)
     gemv_bytes_step = args.layers * sum(gemv_bytes(N, K, args.batch) for _, N, K in rank_shapes(args.tp))
     attn_bytes_step = args.layers * decode_bytes(args.batch, args.ctx, args.tp)
@@ -614,6 +745,25 @@ def run_b200(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
+        if serve is not None:
+            result["parts"]["serving_5"] = {
+                "workload": f"config 5: 7B, {SERVE_DECODES} decodes (ctx ~U[{SERVE_CTX[0]}, {SERVE_CTX[1]}], seeded) "
+                            f"+ {SERVE_PREFILLS} new {SERVE_PREFILL_LEN}-token prefills per step = {serve_tokens} "
+                            "tokens; fragmented random block table over one fp8 pool per layer (synthetic "
+                            "prompt pages); 32 layers x [qkv, KV write, attention, o, gate_up, down] on the "
+                            "wide MXFP4 GEMM; NCCL allreduce under tensor parallelism",
+                "tokens_per_step": serve_tokens,
+                "ms_per_step_mixed": serve["mixed"], "ms_per_step_split": serve["split"],
+                "tok_s_mixed": copies * serve_tokens / (serve["mixed"] * 1e-3),
+                "tok_s_split": copies * serve_tokens / (serve["split"] * 1e-3),
+                "attention_ms_mixed": serve["attn_mixed"], "attention_ms_split": serve["attn_split"],
+                "gemm_ms": serve["gemm"],
+                "gemm_tflops": serve_gemm / (serve["gemm"] * 1e-3) / 1e12,
+                "decode_kv_gb_per_step": serve_kv / 1e9, "prefill_gflop_per_step": serve_pre / 1e9,
+                "note": "mixed = one varlen attention call for the whole batch (the vLLM forward patch); "
+                        "split = decode kernel for the decode rows + varlen kernel for the prefills; "
+                        "attention_ms includes the KV write; the down GEMM reads half of gate_up's output "
+                        "in place of SwiGLU (same bytes and FLOPs); per rank under tensor parallelism"}
         if ms_comm is not None:
             result["parts"]["allreduce"] = {
                 "us_per_step": ms_comm * 1e3, "calls_per_step": 2 * args.layers,
@@ -650,6 +800,8 @@ def main():
                     help="N > 1: tensor parallelism over the N GPUs (default) or N full replicas")
     ap.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
                     help="tensor-parallel allreduce: b200kv's peer-memory kernel or NCCL")
+    ap.add_argument("--serving", choices=("on", "off"), default="on",
+                    help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1)")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
                     help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
     args = ap.parse_args()

@@ -1,0 +1,79 @@
+"""Config 5 (the serving shape) on sampled sequences against the CPU oracle
+(oracle/fp8kv_oracle.py: the reference's prefill / decode attention): a mixed
+batch of decode rows at long contexts (up to 32k, as config 5 draws them) and
+new prefills over one fragmented fp8 pool, run the two ways the serving step
+runs it -- one varlen call for the whole batch (what the vLLM forward patch
+does) and the decode kernel for the decode rows plus the varlen kernel for the
+prefills.  Tolerance as the other attention tests: max abs error < 0.05 and
+< 2e-2 of the largest output."""
+import math
+
+import pytest
+import torch
+
+import fp8kv_oracle as FO
+
+pytestmark = pytest.mark.gpu
+
+HQ, HKV, D, PBLK = 32, 8, 128, 16
+ATOL, RTOL = 0.05, 2e-2
+
+
+def _check(got, ref):
+    got = got.float().cpu()
+    err = (got - ref).abs().max().item()
+    rel = err / max(ref.abs().max().item(), 1e-30)
+    assert err < ATOL and rel < RTOL, (err, rel)
+
+
+def _serving_case(ctx, prefills, seed):
+    """Decode rows at contexts `ctx` (one new token each) and new prefills of
+    lengths `prefills`, pages of every sequence drawn from one permutation."""
+    g = torch.Generator().manual_seed(seed)
+    seq = [c + 1 for c in ctx] + list(prefills)
+    qlens = [1] * len(ctx) + list(prefills)
+    nblk = [math.ceil(L / PBLK) for L in seq]
+    nb = sum(nblk) + 5
+    k = (torch.randn(nb, PBLK, HKV, D, generator=g) * 2).to(torch.float8_e4m3fn)
+    v = (torch.randn(nb, PBLK, HKV, D, generator=g) * 2).to(torch.float8_e4m3fn)
+    perm = torch.randperm(nb, generator=g).to(torch.int32)
+    bt = torch.zeros(len(seq), max(nblk), dtype=torch.int32)
+    pos = 0
+    for s, n in enumerate(nblk):
+        bt[s, :n] = perm[pos:pos + n]
+        pos += n
+    T = sum(qlens)
+    q = torch.randn(T, HQ, D, generator=g).to(torch.bfloat16)
+    cu = torch.tensor([0] + torch.tensor(qlens).cumsum(0).tolist(), dtype=torch.int32)
+    return q, k, v, bt, cu, torch.tensor(seq, dtype=torch.int32)
+
+
+CTX = [30001, 2048, 17000, 32768, 5000]
+PRE = [384, 129]
+
+
+def test_mixed_batch_one_varlen_call(cuda):
+    import fp8kv_prefill
+    q, k, v, bt, cu, lens = _serving_case(CTX, PRE, seed=1)
+    out = torch.zeros_like(q, device=cuda)
+    fp8kv_prefill.prefill_attention(q.to(cuda), k.to(cuda), v.to(cuda), out, cu.to(cuda), lens.to(cuda),
+                                    bt.to(cuda), 0.9, 1.2, D ** -0.5, max_qlen=max(PRE))
+    _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 0.9, 1.2, D ** -0.5))
+
+
+def test_split_decode_rows_and_prefills(cuda):
+    """Decode kernel on the decode rows, varlen kernel on the prefills (views
+    into the same q / out / block table, as the serving step slices them)."""
+    import _decode
+    import fp8kv_prefill
+    q, k, v, bt, cu, lens = _serving_case(CTX, PRE, seed=2)
+    nd = len(CTX)
+    qd, kd, vd, btd, lensd = q.to(cuda), k.to(cuda), v.to(cuda), bt.to(cuda), lens.to(cuda)
+    out = torch.zeros_like(qd)
+    qsl = torch.arange(nd + 1, dtype=torch.int32, device=cuda)
+    _decode.decode_attention(qd, kd, vd, out, qsl, lensd[:nd], btd[:nd], 0.9, 1.2, D ** -0.5,
+                             out_by_qsl=True, max_seq_len_hint=max(CTX) + 1)
+    cu_pre = (cu[nd:] - nd).to(cuda)
+    fp8kv_prefill.prefill_attention(qd[nd:], kd, vd, out[nd:], cu_pre, lensd[nd:], btd[nd:], 0.9, 1.2,
+                                    D ** -0.5, max_qlen=max(PRE))
+    _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 0.9, 1.2, D ** -0.5))
