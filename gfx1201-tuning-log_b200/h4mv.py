@@ -97,8 +97,11 @@ def mxfp4_gemm(x, weight, packed_scales, out=None):
 
 
 # (device index, stream handle) -> workspace of the wide GEMM's activation terms;
-# calls on one stream run in order, so they can share it
+# calls on one stream run in order, so they can share it.  A workspace that is
+# outgrown is kept alive, never freed: a CUDA graph captured with it (vLLM
+# captures one per batch size, in one memory pool) still writes to it.
 _workspaces = {}
+_outgrown = []
 
 
 def wide_workspace(M, K, device, stream):
@@ -109,6 +112,8 @@ def wide_workspace(M, K, device, stream):
     key = (device.index, stream.cuda_stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < need:
+        if ws is not None:
+            _outgrown.append(ws)
         ws = torch.empty(need, dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws

@@ -337,3 +337,24 @@ def test_sitecustomize_chain_patches_once():
     assert "WRAPPED True False vllm.v1.attention.backends.triton_attn" in r.stdout
     assert "[fp8kv-override] installed" in r.stderr
     assert "[fp8kv-prefill] installed" in r.stderr
+
+
+def test_wide_workspace_is_never_freed_when_outgrown(libpath, monkeypatch):
+    """A graph captured with a smaller workspace keeps writing to it, so growing
+    the per-stream workspace must keep the old one alive."""
+    import h4mv
+
+    class _Stream:
+        cuda_stream = 12345
+
+    class _Dev:
+        index = 99
+    orig = torch.empty
+    monkeypatch.setattr(h4mv.torch, "empty", lambda n, dtype=None, device=None: orig(n, dtype=dtype))
+    monkeypatch.setattr(h4mv, "_workspaces", {})
+    monkeypatch.setattr(h4mv, "_outgrown", [])
+    a = h4mv.wide_workspace(64, 256, _Dev(), _Stream())
+    b = h4mv.wide_workspace(200, 256, _Dev(), _Stream())
+    c = h4mv.wide_workspace(100, 256, _Dev(), _Stream())
+    assert b.numel() > a.numel() and c is b
+    assert any(t is a for t in h4mv._outgrown)
