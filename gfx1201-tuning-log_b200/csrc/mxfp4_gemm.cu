@@ -194,6 +194,7 @@ struct GemmArgs {
   int nstages;         // ring depth
   int wtiles;          // ceil(N / 128)
   int ttiles;          // ceil(M / 64)
+  int vec_out;         // Out 16-byte aligned and N % 8 == 0: 16-byte output stores
 };
 
 // Dynamic shared memory: the stage ring, then (ks > 1) the receive area of the
@@ -394,7 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < 32; ++j) v[j] = 0.f;
           }
           const int tok0 = nt * kTok + 32 * h;  // first token (within the CTA tile) of v
-          if (ksz == 1) {
+          if (ksz == 1 && a.vec_out) {
+            // into the (drained) ring as a [token][row] bf16 tile, stored below in 16-byte chunks
+            __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(dsm);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) tile[(size_t)(tok0 + j) * (MT * kRows) + r] = __float2bfloat16_rn(v[j]);
+          } else if (ksz == 1) {
             const int m0 = tt0 * kTok + tok0;
             if (n < a.N)
 #pragma unroll
@@ -420,6 +426,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     tc::fence_before_sync();
+    if (ksz == 1 && a.vec_out) {
+      // the tile's token rows are contiguous runs of output: coalesced 16-byte stores
+      named_bar_sync(1, 128);
+      const uint4* tile = reinterpret_cast<const uint4*>(dsm);
+      constexpr int kCh = MT * kRows / 8;  // 16-byte chunks per token row of the tile
+      for (int idx = et; idx < kT * kCh; idx += 128) {
+        const int tok = idx / kCh, c = idx % kCh;
+        const int m = tt0 * kTok + tok, n0 = wt0 * kRows + 8 * c;
+        if (m < a.M && n0 < a.N)  // N % 8 == 0: a chunk lies wholly inside or outside
+          *reinterpret_cast<uint4*>(a.Out + (size_t)m * a.N + n0) = tile[idx];
+      }
+    }
     if (ksz > 1) {
       // finish this rank's band: fixed-order sum over the ranks' partials
       named_bar_sync(1, 128);  // the local partial is in place
@@ -625,6 +643,7 @@ int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t
   a.Sp = static_cast<const uint8_t*>(Sp);
   a.Xs = Xs;
   a.Out = static_cast<__nv_bfloat16*>(Out);
+  a.vec_out = (reinterpret_cast<uintptr_t>(Out) & 15) == 0 && N % 8 == 0;
 
   // plan: tile shape (MT weight tiles x NT token tiles), K-split, ring depth
   const int force_mt = env_int("B200KV_GEMM_MT", 0), force_nt = env_int("B200KV_GEMM_NT", 0);

@@ -183,3 +183,18 @@ def test_rejects_bad_arguments(cuda):
         h4mv.mxfp4_gemm_wide(X.to(cuda), W.to(cuda), p, workspace=small)
     with pytest.raises(ValueError):
         h4mv.wide_workspace(16, 96, cuda, torch.cuda.current_stream())
+
+
+@pytest.mark.parametrize("N,offset", [(1000, 0), (1001, 0), (1000, 3)])
+def test_unsplit_output_stores(cuda, monkeypatch, N, offset):
+    """Without a K-split the tile leaves through 16-byte stores when N % 8 == 0
+    and the output is 16-byte aligned, else element by element; an output
+    view at an odd element offset takes the second path."""
+    import h4mv
+    monkeypatch.setenv("B200KV_GEMM_KSPLIT", "1")
+    W, St, X, ref = _integer_case(N, 1024, 70, seed=N + offset)
+    buf = torch.full((70 * N + offset,), float("nan"), dtype=torch.bfloat16, device=cuda)
+    out = buf[offset:].view(70, N)
+    h4mv.mxfp4_gemm_wide(X.to(cuda), W.to(cuda), _packed(St, N, 1024, cuda), out=out)
+    assert torch.equal(out.float().cpu(), ref)
+    assert bool(buf[:offset].isnan().all())
