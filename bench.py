@@ -401,7 +401,10 @@ def serving_part(args, dev, barrier, layers=32, steps=2):
         allreduce = dist.all_reduce
 
     def attention(L, mode):
-        if mode == "mixed":
+        if mode == "mixed":  # the forward patch's path: split on the device by query count
+            fp8kv_prefill.mixed_attention(q, L["k"], L["v"], attn, cu, seq_lens, bt, ks, ks, sm,
+                                          max_qlen=SERVE_PREFILL_LEN, max_seq_len=SERVE_CTX[1] + 1)
+        elif mode == "one_call":
             fp8kv_prefill.prefill_attention(q, L["k"], L["v"], attn, cu, seq_lens, bt, ks, ks, sm,
                                             max_qlen=SERVE_PREFILL_LEN)
         else:
@@ -445,6 +448,7 @@ def serving_part(args, dev, barrier, layers=32, steps=2):
 
     res = {"mixed": timed("mixed", "all"), "split": timed("split", "all"),
            "attn_mixed": timed("mixed", "attn"), "attn_split": timed("split", "attn"),
+           "attn_one_call": timed("one_call", "attn"),
            "gemm": timed("split", "gemm")}
     kv_bytes = layers * sum(c + 1 for c in ctx) * hkv * D * 2
     pre_flops = layers * 4 * D * hq * SERVE_PREFILLS * SERVE_PREFILL_LEN * (SERVE_PREFILL_LEN + 1) // 2
@@ -757,11 +761,14 @@ def run_b200(args):
                 "tok_s_mixed": copies * serve_tokens / (serve["mixed"] * 1e-3),
                 "tok_s_split": copies * serve_tokens / (serve["split"] * 1e-3),
                 "attention_ms_mixed": serve["attn_mixed"], "attention_ms_split": serve["attn_split"],
+                "attention_ms_one_call": serve["attn_one_call"],
                 "gemm_ms": serve["gemm"],
                 "gemm_tflops": serve_gemm / (serve["gemm"] * 1e-3) / 1e12,
                 "decode_kv_gb_per_step": serve_kv / 1e9, "prefill_gflop_per_step": serve_pre / 1e9,
-                "note": "mixed = one varlen attention call for the whole batch (the vLLM forward patch); "
-                        "split = decode kernel for the decode rows + varlen kernel for the prefills; "
+                "note": "mixed = b200kv_attn_varlen_mixed, what the vLLM forward patch calls (decode "
+                        "rows to the decode kernel, prefills to the varlen kernel, split on the device); "
+                        "split = the same two kernels as two calls on host-known row ranges; one_call = "
+                        "the varlen kernel for the whole batch; "
                         "attention_ms includes the KV write; the down GEMM reads half of gate_up's output "
                         "in place of SwiGLU (same bytes and FLOPs); per rank under tensor parallelism"}
         if ms_comm is not None:

@@ -92,6 +92,17 @@ lib.b200kv_prefill_attn.argtypes = (
      _i32, _i32, _i32, _i32,          # hq, hkv, head_dim, block_size
      _i32, _i32,                      # num_blocks, kv_dtype
      _vp])
+lib.b200kv_attn_varlen_mixed.restype = _i32
+lib.b200kv_attn_varlen_mixed.argtypes = (
+    [_vp, _i64, _i64,                 # q, strides
+     _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64,  # caches, strides
+     _vp, _i64, _i64,                 # out, strides
+     _vp, _vp, _vp, _i64,             # cu_seqlens_q, seq_lens, block_table, bt stride
+     _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
+     _i32, _i32, _i32,                # num_seqs, max_qlen, max_seq_len
+     _i32, _i32, _i32, _i32,          # hq, hkv, head_dim, block_size
+     _i32, _i32, _i32,                # num_blocks, max_blocks_per_seq, kv_dtype
+     _vp])
 
 lib.b200kv_mxfp4_packed_scales_bytes.restype = ctypes.c_size_t
 lib.b200kv_mxfp4_packed_scales_bytes.argtypes = [_i32, _i32]

@@ -105,7 +105,7 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int hq, int hkv, int head_dim,
-                        int block_size, int num_blocks, int kv_dtype, void* stream);
+                        int block_size, int num_blocks, int kv_dtype, int only_multi, void* stream);
 
 void set_last_error(int e) { t_last_error = e; }
 
@@ -178,7 +178,7 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
       q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
       out_stride_tok, out_stride_head, qsl, seq_lens, block_table, bt_stride, k_scale, v_scale,
       sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
-      max_blocks_per_seq, max_seq_len_hint, kv_dtype, out_by_qsl, num_splits, stream);
+      max_blocks_per_seq, max_seq_len_hint, kv_dtype, out_by_qsl ? 1 : 0, num_splits, stream);
 }
 
 int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
@@ -195,7 +195,33 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
       q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
       out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
       v_scale, sm_scale, num_seqs, max_qlen, q0_single, qlen_single, num_q_heads, num_kv_heads,
-      head_dim, block_size, num_blocks, kv_dtype, stream);
+      head_dim, block_size, num_blocks, kv_dtype, 0, stream);
+}
+
+int b200kv_attn_varlen_mixed(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                             const void* k_cache, const void* v_cache, int64_t sk0, int64_t sk1,
+                             int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2, void* out,
+                             int64_t out_stride_tok, int64_t out_stride_head,
+                             const int32_t* cu_seqlens_q, const int32_t* seq_lens,
+                             const int32_t* block_table, int64_t bt_stride, const float* k_scale,
+                             const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
+                             int max_seq_len, int num_q_heads, int num_kv_heads, int head_dim,
+                             int block_size, int num_blocks, int max_blocks_per_seq, int kv_dtype,
+                             void* stream) {
+  if (!cu_seqlens_q || !seq_lens || max_qlen < 1) return B200KV_ERR_INVALID_ARG;
+  // one-token sequences on the split-K decode kernel (output row = the token's row)
+  int r = b200kv::decode_attn_launch(
+      q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
+      out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
+      v_scale, sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
+      max_blocks_per_seq, max_seq_len, kv_dtype, 1 | 2, 0, stream);
+  if (r != B200KV_OK || max_qlen == 1) return r;
+  // the rest on the varlen kernel
+  return b200kv::prefill_attn_launch(
+      q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
+      out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
+      v_scale, sm_scale, num_seqs, max_qlen, 0, 0, num_q_heads, num_kv_heads, head_dim, block_size,
+      num_blocks, kv_dtype, 1, stream);
 }
 
 size_t b200kv_mxfp4_packed_scales_bytes(int N, int K) {

@@ -71,7 +71,8 @@ struct DecodeParams {
   const float* k_scale;
   const float* v_scale;
   float sm_scale;
-  int block_size, bs_shift, out_by_qsl;  // bs_shift = log2(block_size) or -1
+  int block_size, bs_shift;  // bs_shift = log2(block_size) or -1
+  int out_by_qsl;  // bit 0: output row qsl[s] (else s); bit 1: one-token sequences only
 };
 
 namespace {
@@ -122,6 +123,13 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeParam
   const int g = lane >> 2;   // fragment row group: head (S^T) / token (K^T)
   const int c = lane & 3;
 
+  // mixed batches: sequences with more than one query token belong to the
+  // varlen prefill kernel (cluster-uniform: the cluster serves one sequence)
+  if ((p.out_by_qsl & 2) && p.qsl[seq + 1] - p.qsl[seq] != 1) {
+    griddep_wait();
+    return;
+  }
+
   // The next kernel may launch now.  Sequence metadata and block-table rows
   // are read before this grid waits on the previous one (no kernel that
   // triggers early writes them); q, K and V are read, and the output written,
@@ -129,7 +137,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const DecodeParam
   if (tid == 0) griddep_launch_dependents();
   const int seqlen = max(p.seq_lens[seq], 0);
   const int q_tok = p.qsl[seq];
-  const int out_row = p.out_by_qsl ? q_tok : seq;
+  const int out_row = (p.out_by_qsl & 1) ? q_tok : seq;
   const int per = ((seqlen + csize - 1) / csize + 15) & ~15;
   const int lo = min(seqlen, rank * per);
   const int hi = min(seqlen, lo + per);

@@ -69,7 +69,7 @@ struct TmaDecodeParams {
   const float* v_scale;
   float sm_scale;
   int bs_shift;  // log2(block_size), block_size in {16, 32, 64, 128}
-  int out_by_qsl;
+  int out_by_qsl;  // bit 0: output row qsl[s] (else s); bit 1: one-token sequences only
 };
 
 template <int GQA>
@@ -107,6 +107,14 @@ __global__ void __launch_bounds__(kThreadsT)
   const int g = lane >> 2;
   const int c = lane & 3;
 
+  // Mixed batches: a sequence with more than one query token is the varlen
+  // prefill kernel's (every CTA of the cluster serves this sequence, so the
+  // whole cluster leaves, before any barrier or cluster arrival).
+  if ((p.out_by_qsl & 2) && p.qsl[seq + 1] - p.qsl[seq] != 1) {
+    griddep_wait();
+    return;
+  }
+
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&S.full_bar[s], 1);
@@ -124,7 +132,7 @@ __global__ void __launch_bounds__(kThreadsT)
   }
   const int seqlen = max(p.seq_lens[seq], 0);
   const int q_tok = p.qsl[seq];
-  const int out_row = p.out_by_qsl ? q_tok : seq;
+  const int out_row = (p.out_by_qsl & 1) ? q_tok : seq;
   const int bs = 1 << p.bs_shift;
   const int unit = max(bs, 16);  // shares start on a page boundary
   const int per = ((seqlen + csize - 1) / csize + unit - 1) / unit * unit;

@@ -63,6 +63,7 @@ struct PrefillParams {
   float sm_scale;
   int block_size, bs_shift;
   int q0_single, qlen_single;
+  int only_multi;  // skip one-token sequences (the decode kernel's, in a mixed batch)
 };
 
 // Byte offset of the 16-byte chunk `c16` (0..15) of row `r` of a 128 x 128 f16
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const Prefill
   const int kvlen = p.seq_lens ? p.seq_lens[seq] : p.q0_single + p.qlen_single;
   const int q0 = kvlen - qlen;
   const int t0 = qt * TPT;
-  if (t0 >= qlen || qlen <= 0) return;  // CTA-uniform
+  if (t0 >= qlen || qlen <= 0 || (p.only_multi && qlen == 1)) return;  // CTA-uniform
   const int last_tok = min(qlen, t0 + TPT) - 1;
   const int kv_hi = q0 + last_tok + 1;  // keys [0, kv_hi) are visible to this tile
   const int ntiles = (kv_hi + kBN - 1) / kBN;
@@ -374,7 +375,7 @@ int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                        const float* v_scale, float sm_scale, int num_seqs, int qmax,
                        int q0_single, int qlen_single, int gqa, int hkv, int block_size,
-                       int num_blocks, void* stream);
+                       int num_blocks, int only_multi, void* stream);
 
 int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                         const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
@@ -383,7 +384,7 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int hq, int hkv, int head_dim,
-                        int block_size, int num_blocks, int kv_dtype, void* stream) {
+                        int block_size, int num_blocks, int kv_dtype, int only_multi, void* stream) {
   if (!q || !k_cache || !v_cache || !out || !block_table) return B200KV_ERR_INVALID_ARG;
   if (num_seqs <= 0 || hq <= 0 || hkv <= 0 || block_size <= 0 || num_blocks < 0 || hq % hkv)
     return B200KV_ERR_INVALID_ARG;
@@ -411,7 +412,7 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                                      out, o_st, o_sh, cu_seqlens_q, seq_lens, block_table,
                                      bt_stride, k_scale, v_scale, sm_scale, num_seqs, qmax,
                                      q0_single, qlen_single, gqa, hkv, block_size, num_blocks,
-                                     stream);
+                                     only_multi, stream);
     if (r >= 0) return r;
   }
   PrefillParams p;
@@ -436,6 +437,7 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
   p.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz((unsigned)block_size) : -1;
   p.q0_single = q0_single;
   p.qlen_single = qlen_single;
+  p.only_multi = only_multi;
   const int qtiles = cdiv(qmax, kRows / gqa);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;

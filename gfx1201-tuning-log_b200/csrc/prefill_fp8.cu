@@ -96,6 +96,7 @@ struct Fp8PrefillParams {
   int pblk_shift;  // log2(block_size), block_size in {16, 32, 64, 128}
   int q0_single, qlen_single;
   int qpairs;      // gridDim.x: pairs of 128-row query tiles
+  int only_multi;  // skip one-token sequences (the decode kernel's, in a mixed batch)
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -200,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kvlen = p.seq_lens ? p.seq_lens[seq] : p.q0_single + p.qlen_single;
   const int q0 = kvlen - qlen;
   const int t0 = pair * 2 * TPT;  // first token of tile A
-  if (t0 >= qlen || qlen <= 0) return;  // CTA-uniform
+  if (t0 >= qlen || qlen <= 0 || (p.only_multi && qlen == 1)) return;  // CTA-uniform
   const bool hasB = t0 + TPT < qlen;
   const int kvhiA = q0 + min(qlen, t0 + TPT);  // keys [0, kvhi) are visible to a tile
   const int kvhiB = hasB ? q0 + min(qlen, t0 + 2 * TPT) : kvhiA;
@@ -552,7 +553,7 @@ int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                        const float* v_scale, float sm_scale, int num_seqs, int qmax,
                        int q0_single, int qlen_single, int gqa, int hkv, int block_size,
-                       int num_blocks, void* stream) {
+                       int num_blocks, int only_multi, void* stream) {
   if (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128) return -1;
   if (num_blocks <= 0) return -1;
   CUtensorMap km, vm;
@@ -579,6 +580,7 @@ int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
   p.q0_single = q0_single;
   p.qlen_single = qlen_single;
   p.qpairs = cdiv(qmax, 2 * (kRows / gqa));
+  p.only_multi = only_multi;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (gqa) {

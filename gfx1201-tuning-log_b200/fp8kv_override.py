@@ -12,8 +12,9 @@ reference does (fp8kv_override.py:48-109):
     (fp8kv_v3.run), the reference's fast path;
   * with FP8KV_PREFILL=1 (the reference's switch, fp8kv_prefill.py:148),
     batches that carry prefill tokens run the varlen causal prefill kernel for
-    every sequence -- several sequences and mixed prefill + decode batches
-    included (a decode token is a one-token prefill at position seq_len - 1),
+    their prefills and the split-K decode kernel for their one-token
+    sequences, split on the device (a decode token is a one-token prefill at
+    position seq_len - 1, so the result is the varlen kernel's for the batch),
     where the reference's gate took exactly one sequence
     (fp8kv_prefill.py:159-172);
   * anything else, or any exception, falls back to the wrapped forward;
@@ -171,10 +172,12 @@ def _install_impl():
                              max_seq_len=attn_metadata.max_seq_len)
                 counts["decode"] += 1
             else:
-                fp8kv_prefill.prefill_attention(
+                # decode tokens of a mixed batch go to the split-K decode kernel,
+                # the prefills to the varlen kernel (split on the device)
+                fp8kv_prefill.mixed_attention(
                     q, kc, vc, out, attn_metadata.query_start_loc, attn_metadata.seq_lens,
                     attn_metadata.block_table, layer._k_scale, layer._v_scale, self.scale,
-                    max_qlen=attn_metadata.max_query_len)
+                    max_qlen=attn_metadata.max_query_len, max_seq_len=attn_metadata.max_seq_len)
                 counts["prefill"] += 1
             if engaged[0] <= 0:
                 engaged[0] = 1

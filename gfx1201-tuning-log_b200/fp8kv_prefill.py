@@ -79,6 +79,37 @@ def prefill_attention(q, k_cache, v_cache, out, cu_seqlens_q, seq_lens, block_ta
                    v_scale, sm_scale, num_seqs, int(max_qlen), 0, 0)
 
 
+def mixed_attention(q, k_cache, v_cache, out, cu_seqlens_q, seq_lens, block_table,
+                    k_scale, v_scale, sm_scale, max_qlen, max_seq_len):
+    """prefill_attention's result for a batch that mixes decode tokens and
+    prefills, split on the device by query count: one-token sequences on the
+    split-K decode kernel, the rest on the varlen kernel (no host sync)."""
+    if q.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise TypeError("q and out must be bfloat16")
+    if cu_seqlens_q.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise TypeError("cu_seqlens_q and seq_lens must be int32")
+    if block_table.dtype != torch.int32 or block_table.stride(-1) != 1:
+        raise TypeError("block_table must be int32 with contiguous rows")
+    num_seqs = cu_seqlens_q.shape[0] - 1
+    if seq_lens.shape[0] < num_seqs or block_table.shape[0] < num_seqs:
+        raise ValueError("seq_lens and block_table need a row per sequence of cu_seqlens_q")
+    dev = q.device
+    ks, vs = _scale(k_scale, dev), _scale(v_scale, dev)
+    check(lib.b200kv_attn_varlen_mixed(
+        q.data_ptr(), q.stride(0), q.stride(1),
+        k_cache.data_ptr(), v_cache.data_ptr(),
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+        v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
+        out.data_ptr(), out.stride(0), out.stride(1),
+        cu_seqlens_q.data_ptr(), seq_lens.data_ptr(), block_table.data_ptr(), block_table.stride(0),
+        ks.data_ptr(), vs.data_ptr(), float(sm_scale),
+        num_seqs, int(max_qlen), int(max_seq_len), q.shape[1], k_cache.shape[2], q.shape[2],
+        k_cache.shape[1], min(k_cache.shape[0], v_cache.shape[0]), block_table.shape[1],
+        _kv_dtype(k_cache), torch.cuda.current_stream(dev).cuda_stream),
+        "b200kv_attn_varlen_mixed")
+    return out
+
+
 def _install():
     """FP8KV_PREFILL=1: prefill batches (max_query_len > 1) go to this kernel
     through the fp8kv_override patch of TritonAttentionImpl.forward; the gate

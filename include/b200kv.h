@@ -233,6 +233,30 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         int num_q_heads, int num_kv_heads, int head_dim, int block_size,
                         int num_blocks, int kv_dtype, void* stream);
 
+/* Mixed batches (decode tokens and prefills in one varlen batch, as vLLM's
+ * TritonAttentionImpl.forward receives them, vllm-fp8kv/fp8kv_prefill.py:156-198
+ * takes the whole batch through its prefill kernel): the same result as
+ * b200kv_prefill_attn over the batch, with the work split on the device by
+ * each sequence's query count, without a host sync.  Sequences with one query
+ * token run on the split-K decode kernel (that token attends its whole
+ * context, as a one-token prefill does), the others on the varlen prefill
+ * kernel; each kernel leaves the other's sequences untouched (two launches on
+ * `stream`).  No counterpart call in the reference.
+ *   max_seq_len  upper bound of seq_lens (sizes the decode kernel's split);
+ *   max_blocks_per_seq  block_table row capacity;  other arguments as
+ *   b200kv_prefill_attn's varlen form (cu_seqlens_q and seq_lens required). */
+int b200kv_attn_varlen_mixed(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                             const void* k_cache, const void* v_cache,
+                             int64_t sk0, int64_t sk1, int64_t sk2,
+                             int64_t sv0, int64_t sv1, int64_t sv2,
+                             void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                             const int32_t* cu_seqlens_q, const int32_t* seq_lens,
+                             const int32_t* block_table, int64_t bt_stride,
+                             const float* k_scale, const float* v_scale, float sm_scale,
+                             int num_seqs, int max_qlen, int max_seq_len,
+                             int num_q_heads, int num_kv_heads, int head_dim, int block_size,
+                             int num_blocks, int max_blocks_per_seq, int kv_dtype, void* stream);
+
 /* ---- paged KV-cache write ------------------------------------------------------
  *
  * For every token t < num_tokens with slot = slot_mapping[t] >= 0:

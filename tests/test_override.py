@@ -59,7 +59,7 @@ def override(libpath, monkeypatch):
     import fp8kv_v3
     import kv_cache
     monkeypatch.setattr(fp8kv_v3, "run", lambda *a, **k: calls["decode"].append((a, k)))
-    monkeypatch.setattr(fp8kv_prefill, "prefill_attention", lambda *a, **k: calls["prefill"].append((a, k)))
+    monkeypatch.setattr(fp8kv_prefill, "mixed_attention", lambda *a, **k: calls["prefill"].append((a, k)))
     monkeypatch.setattr(kv_cache, "reshape_and_cache_flash", lambda *a, **k: calls["kvw"].append(a))
     monkeypatch.setenv("FP8KV_KVWRITE", "1")
     assert fp8kv_override._install()
@@ -161,7 +161,7 @@ def test_prefill_falls_back_unless_enabled(override):
     cls.forward(_impl(), layer, q, None, None, kv, md, out)
     assert calls["orig"] == 1 and len(calls["prefill"]) == 1
     a, k = calls["prefill"][0]
-    assert a[4] is md.query_start_loc and k["max_qlen"] == 4
+    assert a[4] is md.query_start_loc and k["max_qlen"] == 4 and k["max_seq_len"] == md.max_seq_len
 
 
 def test_ineligible_and_failing_calls_fall_back(override, monkeypatch):

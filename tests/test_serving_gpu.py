@@ -77,3 +77,38 @@ def test_split_decode_rows_and_prefills(cuda):
     fp8kv_prefill.prefill_attention(qd[nd:], kd, vd, out[nd:], cu_pre, lensd[nd:], btd[nd:], 0.9, 1.2,
                                     D ** -0.5, max_qlen=max(PRE))
     _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 0.9, 1.2, D ** -0.5))
+
+
+def test_device_split_entry(cuda):
+    """b200kv_attn_varlen_mixed (the forward patch's path for mixed batches):
+    one-token sequences on the decode kernel, the rest on the varlen kernel,
+    chosen on the device; within tolerance of the oracle and bit for bit equal
+    to the two separate calls of the split arrangement."""
+    import _decode
+    import fp8kv_prefill
+    q, k, v, bt, cu, lens = _serving_case(CTX, PRE, seed=3)
+    qd, kd, vd, btd, lensd, cud = q.to(cuda), k.to(cuda), v.to(cuda), bt.to(cuda), lens.to(cuda), cu.to(cuda)
+    out = torch.full_like(qd, float("nan"))
+    fp8kv_prefill.mixed_attention(qd, kd, vd, out, cud, lensd, btd, 0.9, 1.2, D ** -0.5,
+                                  max_qlen=max(PRE), max_seq_len=max(CTX) + 1)
+    _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 0.9, 1.2, D ** -0.5))
+    nd = len(CTX)
+    ref = torch.zeros_like(qd)
+    qsl = torch.arange(nd + 1, dtype=torch.int32, device=cuda)
+    _decode.decode_attention(qd, kd, vd, ref, qsl, lensd[:nd], btd[:nd], 0.9, 1.2, D ** -0.5,
+                             out_by_qsl=True, max_seq_len_hint=max(CTX) + 1)
+    fp8kv_prefill.prefill_attention(qd[nd:], kd, vd, ref[nd:], (cud[nd:] - nd).contiguous(), lensd[nd:],
+                                    btd[nd:], 0.9, 1.2, D ** -0.5, max_qlen=max(PRE))
+    assert torch.equal(out, ref)
+
+
+def test_device_split_all_decode_and_all_prefill(cuda):
+    """Batches with only one-token sequences, or none, through the same entry."""
+    import fp8kv_prefill
+    for ctx, pre in (([3000, 100, 7000], []), ([], [200, 33, 512])):
+        q, k, v, bt, cu, lens = _serving_case(ctx, pre, seed=4 + len(ctx))
+        out = torch.full_like(q, float("nan"), device=cuda)
+        fp8kv_prefill.mixed_attention(q.to(cuda), k.to(cuda), v.to(cuda), out, cu.to(cuda), lens.to(cuda),
+                                      bt.to(cuda), 1.0, 1.0, D ** -0.5, max_qlen=max(pre, default=1),
+                                      max_seq_len=int(lens.max()))
+        _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 1.0, 1.0, D ** -0.5))
