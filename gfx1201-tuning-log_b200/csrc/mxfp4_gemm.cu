@@ -195,6 +195,7 @@ struct GemmArgs {
   int wtiles;          // ceil(N / 128)
   int ttiles;          // ceil(M / 64)
   int vec_out;         // Out 16-byte aligned and N % 8 == 0: 16-byte output stores
+  int n256;            // NT = 2: both token tiles in one N = 256 MMA (B200KV_GEMM_N256=0: two of 128)
 };
 
 // Dynamic shared memory: the stage ring, then (ks > 1) the receive area of the
@@ -339,25 +340,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::fence_after_sync();
         const int nq = min(kb, ns - s * kb);
         const uint32_t st = ring + (uint32_t)slot * (uint32_t)stage_bytes;
-        // scale atoms of this slot: A (mt, q) at column 4 (mt kb + q), B (nt, q) at 4 ((MT + nt) kb + q)
+        // scale atoms of this slot: A (mt, q) at column 4 (mt kb + q), B (nt, q) at
+        // 4 (MT kb + q NT + nt): the atoms of a step's token tiles side by side,
+        // rows 128 nt + r of an N = 256 B operand at column r / 32 + 4 nt
         const uint32_t tsf = tbase + kSfCol + 4 * (MT + NT) * kb * slot;
+        auto sfa_col = [&](int mt, int q) { return tsf + 4 * (mt * kb + q); };
+        auto sfb_col = [&](int nt, int q) { return tsf + 4 * (MT * kb + q * NT + nt); };
         for (int q = 0; q < nq; ++q) {
-          for (int mt = 0; mt < mt_n; ++mt)
-            tmem_cp_atom(tsf + 4 * (mt * kb + q), sdesc_atom(st + lay.sfa_off(mt, q)));
-          for (int nt = 0; nt < nt_n; ++nt)
-            tmem_cp_atom(tsf + 4 * ((MT + nt) * kb + q), sdesc_atom(st + lay.sfb_off(nt, q)));
+          for (int mt = 0; mt < mt_n; ++mt) tmem_cp_atom(sfa_col(mt, q), sdesc_atom(st + lay.sfa_off(mt, q)));
+          for (int nt = 0; nt < nt_n; ++nt) tmem_cp_atom(sfb_col(nt, q), sdesc_atom(st + lay.sfb_off(nt, q)));
         }
+        // two token tiles: their B boxes are adjacent (256 K-major rows), so one
+        // N = 256 MMA takes both -- half the MMAs to issue from this thread
+        const bool n256 = NT == 2 && nt_n == 2 && a.n256;
         for (int q = 0; q < nq; ++q) {
 #pragma unroll
           for (int kq = 0; kq < 4; ++kq) {  // K = 32 each, scale byte kq of the atoms
             const uint32_t sf = (uint32_t)kq;
-            for (int mt = 0; mt < mt_n; ++mt)
-              for (int nt = 0; nt < nt_n; ++nt)
-                mma_mxf8f6f4(tbase + (uint32_t)(mt * NT + nt) * kBRows,
-                             tc::sdesc_sw128(st + lay.a_off(mt, q) + 32 * kq, 16, 1024),
-                             tc::sdesc_sw128(st + lay.b_off(nt, q) + 32 * kq, 16, 1024),
-                             idesc_mxf8f6f4(kRows, kBRows, sf), (s > 0 || q > 0 || kq > 0) ? 1u : 0u,
-                             (tsf + 4 * (mt * kb + q)) | (sf << 30), (tsf + 4 * ((MT + nt) * kb + q)) | (sf << 30));
+            const uint32_t acc = (s > 0 || q > 0 || kq > 0) ? 1u : 0u;
+            for (int mt = 0; mt < mt_n; ++mt) {
+              const uint64_t adesc = tc::sdesc_sw128(st + lay.a_off(mt, q) + 32 * kq, 16, 1024);
+              if (n256) {
+                mma_mxf8f6f4(tbase + (uint32_t)(mt * NT) * kBRows, adesc,
+                             tc::sdesc_sw128(st + lay.b_off(0, q) + 32 * kq, 16, 1024),
+                             idesc_mxf8f6f4(kRows, 2 * kBRows, sf), acc, sfa_col(mt, q) | (sf << 30),
+                             sfb_col(0, q) | (sf << 30));
+              } else {
+                for (int nt = 0; nt < nt_n; ++nt)
+                  mma_mxf8f6f4(tbase + (uint32_t)(mt * NT + nt) * kBRows, adesc,
+                               tc::sdesc_sw128(st + lay.b_off(nt, q) + 32 * kq, 16, 1024),
+                               idesc_mxf8f6f4(kRows, kBRows, sf), acc, sfa_col(mt, q) | (sf << 30),
+                               sfb_col(nt, q) | (sf << 30));
+              }
+            }
           }
         }
         tc::commit(&empty_bar[slot]);
@@ -550,9 +565,13 @@ void consider(Plan& best, double& best_cost, const GemmArgs& a, int sms, int for
     // per stage: weight bytes at this CTA's share of the HBM bandwidth
     // (about 360 cycles per 8 KB when every SM streams), or the MMAs
     // (4 x 64 cycles per 128 x 128 x 128 block), whichever is longer
-    // and at least the ring's round trip (about 700 cycles per stage)
+    // or the single issuing thread: about 70 cycles per MMA, 53 per scale-atom
+    // copy and 250 per mbarrier wait (two token tiles go in one N = 256 MMA).
+    // With one token tile (M <= 64) a flat 700 cycles fits the measurements better.
     const double fill = min(1.0, (double)active / sms);
-    double stage_cost = fmax(fmax(kb * MT * 360.0 * fill, kb * MT * NT * 256.0), 700.0);
+    const int mmas = kb * 4 * MT * ((NT == 2 && a.n256) ? 1 : NT);
+    const double issue = a.ttiles > 1 ? mmas * 70.0 + kb * (MT + NT) * 53.0 + 250.0 : 700.0;
+    double stage_cost = fmax(fmax(kb * MT * 360.0 * fill, kb * MT * NT * 256.0), issue);
     if (nst < 2 && stages > 1) stage_cost *= 2.0;  // a one-stage ring does not overlap loads and MMAs
     const double cost = waves * (stages * stage_cost + 800.0) + (ks > 1 ? 150.0 * ks * MT * NT : 0.0);
     if (cost < best_cost - 1e-9) {
@@ -643,6 +662,7 @@ int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t
   a.Sp = static_cast<const uint8_t*>(Sp);
   a.Xs = Xs;
   a.Out = static_cast<__nv_bfloat16*>(Out);
+  a.n256 = env_int("B200KV_GEMM_N256", 1) != 0;
   a.vec_out = (reinterpret_cast<uintptr_t>(Out) & 15) == 0 && N % 8 == 0;
 
   // plan: tile shape (MT weight tiles x NT token tiles), K-split, ring depth

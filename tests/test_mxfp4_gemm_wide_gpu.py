@@ -198,3 +198,15 @@ def test_unsplit_output_stores(cuda, monkeypatch, N, offset):
     h4mv.mxfp4_gemm_wide(X.to(cuda), W.to(cuda), _packed(St, N, 1024, cuda), out=out)
     assert torch.equal(out.float().cpu(), ref)
     assert bool(buf[:offset].isnan().all())
+
+
+@pytest.mark.parametrize("n256", ["0", "1"])
+@pytest.mark.parametrize("M", [100, 128, 300])
+def test_two_token_tiles_one_or_two_mmas(cuda, monkeypatch, n256, M):
+    """With two token tiles per CTA the kernel issues one N = 256 MMA (scale
+    atoms of the two tiles side by side in tensor memory) or two of N = 128;
+    both bit-exact on integer inputs, ragged last token tile included."""
+    monkeypatch.setenv("B200KV_GEMM_NT", "2")
+    monkeypatch.setenv("B200KV_GEMM_N256", n256)
+    W, St, X, ref = _integer_case(640, 2048, M, seed=M + int(n256))
+    assert torch.equal(_run(W, St, X, cuda), ref)
