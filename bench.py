@@ -621,7 +621,7 @@ def run_b200(args):
     ms_tok, _ = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None)
     ms_tok = max_over_ranks(ms_tok, dist_on, dev)
     serve = None
-    if args.serving == "on" or (args.serving == "auto" and args.tp == 1):
+    if args.serving == "on":
         res, serve_tokens, serve_kv, serve_pre, serve_gemm = serving_part(args, dev, barrier)
         serve = {k: max_over_ranks(v, dist_on, dev) for k, v in res.items()}
     # one rank's bytes (the per-GPU roofline)
@@ -807,9 +807,8 @@ def main():
                     help="N > 1: tensor parallelism over the N GPUs (default) or N full replicas")
     ap.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
                     help="tensor-parallel allreduce: b200kv's peer-memory kernel or NCCL")
-    ap.add_argument("--serving", choices=("auto", "on", "off"), default="auto",
-                    help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1); "
-                         "auto = on one GPU only, on = also under tensor parallelism")
+    ap.add_argument("--serving", choices=("on", "off"), default="on",
+                    help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1)")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
                     help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
     args = ap.parse_args()
