@@ -105,6 +105,26 @@ def test_decode_argument_validation(b200):
     assert _decode_call(lib, k=0x10008) == 3
 
 
+def _mixed_call(lib, cu=0x10000, lens=0x10000, maxq=4, q=0x10000, hq=32, d=128, maxblk=8):
+    A = 0x10000  # never dereferenced: every call below fails validation first
+    return lib.b200kv_attn_varlen_mixed(q, 32 * 128, 128, A, A, 16 * 8 * 128, 8 * 128, 128,
+                                        16 * 8 * 128, 8 * 128, 128, A, 32 * 128, 128, cu, lens, A, 8,
+                                        A, A, 0.088, 2, maxq, 100, hq, 8, d, 16, 64, maxblk, 0, None)
+
+
+def test_mixed_attention_argument_validation(b200):
+    """b200kv_attn_varlen_mixed needs the varlen form (cu_seqlens_q, seq_lens)
+    and a positive max_qlen, then validates as the decode and prefill calls."""
+    lib = b200.lib
+    assert _mixed_call(lib, cu=None) == 1
+    assert _mixed_call(lib, lens=None) == 1
+    assert _mixed_call(lib, maxq=0) == 1
+    assert _mixed_call(lib, q=None) == 1
+    assert _mixed_call(lib, hq=24) == 2           # GQA 3
+    assert _mixed_call(lib, d=64) == 2
+    assert _mixed_call(lib, maxblk=0) == 1
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason="fake pointers are only safe without a GPU")
 def test_decode_no_device(b200):
     assert _decode_call(b200.lib) == 6
