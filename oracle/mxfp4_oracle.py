@@ -12,10 +12,17 @@ Follows:
   * h4mv/h4mv.cu:33-41       e2m1 bit decode (zero iff (v & 7) == 0, subnormal 0.5)
   * h4mv/h4mv.cu:72          kernel's scale: fp32 bit pattern (b << 23), so that
                              b == 0 gives 0.0 and b == 255 gives +inf
+  * h4mv/h4mv.cu:43-104      h4mv_kernel_order_reference(): the reference
+                             kernel's own order of operations (per-lane group
+                             partials, scale multiply, wave32 xor reduction,
+                             round-half-up to bf16), bit for bit
 Pinned by the reference's own known-answer tests (one-hot probes,
 h4mv/h4mv_test.py:38-52 and w4-hip-demo/probe_w4hip.py:13-47), restated in
-tests/test_oracle_pins.py, and by exhaustive codec tables (tests/test_codecs.py)
-checked against the reference's E2M1 table and torch's float8_e8m0fnu dtype.
+tests/test_oracle_pins.py, by exhaustive codec tables (tests/test_codecs.py)
+checked against the reference's E2M1 table and torch's float8_e8m0fnu dtype,
+and by outputs of the reference kernel itself compiled for the CPU
+(oracle/Makefile -> oracle/_ref/libh4mv_ref.so; committed as
+tests/golden/h4mv_ref_cases.npz by tests/golden/gen_h4mv_golden.py).
 """
 import numpy as np
 import torch
@@ -105,3 +112,56 @@ def make_case(N, K, M, seed, s_lo=119, s_hi=126):
     S = torch.randint(s_lo, s_hi, (K // 32, N), dtype=torch.uint8, generator=g)
     X = torch.randn(M, K, generator=g).to(torch.bfloat16)
     return W, S, S.t().contiguous(), X
+
+
+def h4mv_kernel_order_reference(W, St, X):
+    """bf16 output of the reference kernel h4mv_t<MT> (h4mv/h4mv.cu:43-104) in
+    its own order of operations, as uint16 bits [M, N]:
+      * lane l (of a 32-wide wave per output row) takes groups g = l, l+32, ...
+        (h4mv.cu:68); per group, part = sum over the 16 weight bytes in order of
+        dot2(w pair, x pair, part) -- two exact products and the fp32 running
+        value summed and rounded once (the fused dot2 model of
+        oracle/h4mv_host/hip/hip_runtime.h) -- then acc += part * 2^(b-127)
+        with the scale as fp32 bits b << 23 (h4mv.cu:72,90);
+      * the 32 lane sums are reduced by xor shuffles 16, 8, 4, 2, 1 (h4mv.cu:96-97);
+      * lane 0 rounds fp32 -> bf16 as (f >> 16) + ((f >> 15) & 1), i.e. ties
+        away from zero (h4mv.cu:101).
+    W uint8 [N, K/2], St uint8 [N, K/32] (transposed scales), X bf16 [M, K]."""
+    W = np.asarray(torch.as_tensor(W).cpu().numpy(), dtype=np.uint8)
+    St = np.asarray(torch.as_tensor(St).cpu().numpy(), dtype=np.uint8)
+    xf = torch.as_tensor(X).cpu().float().numpy().astype(np.float64)  # bf16 values, exact
+    N, KW = W.shape
+    K = 2 * KW
+    M = xf.shape[0]
+    ngrp = K // 32
+    lut = np.array(E2M1_LUT, dtype=np.float64)
+    w = np.empty((N, K), dtype=np.float64)
+    w[:, 0::2] = lut[W & 0xF]
+    w[:, 1::2] = lut[W >> 4]
+    sc = e8m0_bits(St)                                    # [N, ngrp] fp32
+    lanes = np.arange(32)
+    acc = np.zeros((N, 32, M), dtype=np.float32)
+    for gi in range(-(-ngrp // 32)):
+        g = gi * 32 + lanes                               # group of each lane
+        valid = g < ngrp
+        gc = np.where(valid, g, 0)
+        part = np.zeros((N, 32, M), dtype=np.float32)
+        for i in range(16):                               # the 16 weight bytes of a group
+            k0 = 32 * gc + 2 * i
+            p0 = w[:, k0][:, :, None] * xf[:, k0].T[None, :, :]
+            p1 = w[:, k0 + 1][:, :, None] * xf[:, k0 + 1].T[None, :, :]
+            part = ((p0 + p1) + part.astype(np.float64)).astype(np.float32)
+        with np.errstate(over="ignore", invalid="ignore"):
+            term = (part * sc[:, gc][:, :, None]).astype(np.float32)
+            acc = np.where(valid[None, :, None], (acc + term).astype(np.float32), acc)
+    v = acc
+    with np.errstate(over="ignore", invalid="ignore"):
+        for off in (16, 8, 4, 2, 1):
+            v = (v + v[:, lanes ^ off, :]).astype(np.float32)
+    f = v[:, 0, :].T.copy().view(np.uint32)              # [M, N]
+    return ((f >> np.uint32(16)) + ((f >> np.uint32(15)) & np.uint32(1))).astype(np.uint16)
+
+
+def bf16_bits_to_float(bits):
+    """uint16 bf16 bit patterns -> float32 values."""
+    return (np.asarray(bits, dtype=np.uint32) << np.uint32(16)).view(np.float32)

@@ -127,3 +127,82 @@ def test_gemv_oracle_scale_modes():
     c = MO.mxfp4_linear_reference(W, S0, X, scale_mode="bits")
     d = MO.mxfp4_linear_reference(W[0:1, :16], S0[:1, :1], X[:, :32], scale_mode="bits")
     assert torch.all(d == 0) and torch.isfinite(c).all()
+
+
+# ---- MXFP4: outputs of the reference kernel itself ----------------------------------
+# tests/golden/h4mv_ref_cases.npz holds outputs of h4mv_t<MT> (h4mv/h4mv.cu:43-104)
+# compiled for the CPU (oracle/Makefile, tests/golden/gen_h4mv_golden.py).
+H4MV_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "h4mv_ref_cases.npz")
+H4MV_REF_LIB = os.path.join(os.path.dirname(os.path.dirname(__file__)), "oracle", "_ref", "libh4mv_ref.so")
+
+
+def _h4mv_cases():
+    z = np.load(H4MV_GOLDEN)
+    names = sorted({k.split("/")[0] for k in z.files})
+    return {n: (z[n + "/W"], z[n + "/St"], _bf16(z[n + "/X"]), z[n + "/out"]) for n in names}
+
+
+H4MV = _h4mv_cases()
+
+
+@pytest.mark.parametrize("name", sorted(H4MV))
+def test_kernel_order_oracle_matches_reference_kernel_outputs(name):
+    """The restatement of the reference kernel's order of operations gives its
+    outputs bit for bit (every case, edge scale bytes 0 and 255 included)."""
+    W, St, X, out = H4MV[name]
+    assert np.array_equal(MO.h4mv_kernel_order_reference(W, St, X), out)
+
+
+@pytest.mark.parametrize("name", sorted(n for n in H4MV if not n.startswith("edge")))
+def test_checker_oracle_within_one_rounding_of_reference_kernel(name):
+    """The fp32 oracle every GPU test checks against (h4mv_test.py:19-32) is within
+    one bf16 rounding of the reference kernel's outputs: they differ only in fp32
+    summation order and in the final rounding (the kernel rounds ties away from
+    zero, torch to even)."""
+    W, St, X, out = H4MV[name]
+    S = torch.from_numpy(St).t().contiguous()
+    ref = MO.mxfp4_linear_reference(torch.from_numpy(W), S, X, scale_mode="bits").numpy()
+    got = MO.bf16_bits_to_float(out)
+    tol = np.abs(ref) * 2.0 ** -8 + 1e-6 * np.abs(ref).max()
+    assert bool((np.abs(got - ref) <= tol).all())
+
+
+def test_reference_kernel_one_hot_and_structured_row():
+    """The known-answer probes, answered by the reference kernel itself: every
+    one-hot position gives exactly 1.0 for all M = 8 rows (h4mv_test.py:38-52),
+    and the structured row equals the exact integer dot product
+    (probe_w4hip.py:33-47: small integers, every sum exact in fp32)."""
+    for k in range(32):
+        W, St, X, out = H4MV[f"onehot_k{k:02d}"]
+        assert bool((MO.bf16_bits_to_float(out) == 1.0).all()), k
+    W, St, X, out = H4MV["structured_row"]
+    exact = MO.mxfp4_linear_reference(torch.from_numpy(W), torch.from_numpy(St).t().contiguous(), X)
+    assert np.array_equal(MO.bf16_bits_to_float(out), exact.to(torch.bfloat16).float().numpy())
+
+
+def _load_h4mv_ref():
+    import ctypes
+    import subprocess
+    if not os.path.exists(H4MV_REF_LIB):
+        ref = os.environ.get("B200KV_REFERENCE", "/root/reference")
+        if not os.path.exists(os.path.join(ref, "h4mv", "h4mv.cu")):
+            pytest.skip("reference checkout absent and oracle/_ref not built")
+        subprocess.run(["make", "-C", os.path.dirname(os.path.dirname(H4MV_REF_LIB)), f"REF={ref}"],
+                       check=True, stdout=subprocess.DEVNULL)
+    lib = ctypes.CDLL(H4MV_REF_LIB)
+    lib.h4mv_host_launch.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 3
+    lib.h4mv_host_launch.restype = ctypes.c_int
+    return lib
+
+
+@pytest.mark.parametrize("N,K,M,seed", [(12, 4096, 1, 1), (9, 14336, 8, 2), (33, 2048, 3, 3), (7, 1056, 6, 4)])
+def test_reference_kernel_host_build_matches_kernel_order_oracle(N, K, M, seed):
+    """Fresh inputs through the reference kernel's host build (oracle/_ref) and
+    the kernel-order restatement: identical bits."""
+    lib = _load_h4mv_ref()
+    W, S, St, X = MO.make_case(N, K, M, seed=seed)
+    out = np.zeros((M, N), dtype=np.uint16)
+    Xn = np.ascontiguousarray(X.view(torch.int16).numpy())
+    Wn, Sn = np.ascontiguousarray(W.numpy()), np.ascontiguousarray(St.numpy())
+    assert lib.h4mv_host_launch(Wn.ctypes.data, Sn.ctypes.data, Xn.ctypes.data, out.ctypes.data, N, K, M) == 0
+    assert np.array_equal(MO.h4mv_kernel_order_reference(W, St, X), out)
