@@ -35,6 +35,7 @@
 // the pre-pass (programmatic dependent launch).
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -48,6 +49,7 @@
 
 #include "b200kv.h"
 #include "b200kv_common.cuh"
+#include "mxfp4_tc.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
 
@@ -61,63 +63,20 @@ constexpr int kKStep = 128;           // K per step: one A box, one B box and on
 constexpr int kABox = kRows * 128;    // A box in shared memory (e2m1 codes, 16 per 16-byte chunk)
 constexpr int kABoxTx = kRows * 64;   // bytes the TMA signals for it (the packed size)
 constexpr int kBBox = kBRows * 128;   // B box: e4m3 codes, 128 B rows, 128-byte swizzle
-constexpr int kAtom = 512;            // scale atom: 128 rows x 4 groups
+constexpr int kAtom = mx::kAtom;      // scale atom: 128 rows x 4 groups
 constexpr int kThreads = 192;
 constexpr int kMaxStages = 8;
 constexpr int kTmemCols = 512;
 constexpr int kSfCol = 256;           // first tensor-memory column of the scale-atom ring
 constexpr int kSmemMax = 227 * 1024;
 
-// instruction descriptor, kind::mxf8f6f4 block-scaled: A e2m1 (format 5 of this
-// kind), B e4m3 (format 0), both K-major, e8m0 scales, scale-factor byte ids
-// (0..3: one byte per MMA, K = 32)
-__host__ __device__ constexpr uint32_t idesc_mxf8f6f4(int M, int N, uint32_t sf_id) {
-  return (sf_id << 4) | (5u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | (1u << 23) |
-         ((uint32_t)(M >> 4) << 24) | (sf_id << 29);
-}
-
-// shared-memory descriptor of a 512-byte scale atom (32 rows x 16 B, no swizzle)
-__device__ __forceinline__ uint64_t sdesc_atom(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)(16 >> 4) << 16;
-  d |= (uint64_t)(128 >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  return d;
-}
-
-__device__ __forceinline__ void tmem_cp_atom(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
-__device__ __forceinline__ void mma_mxf8f6f4(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                             uint32_t acc, uint32_t sfa, uint32_t sfb) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n}" ::"r"(d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
-      : "memory");
-}
-
-// (lo, hi) -> two e4m3 codes, lo in the low byte (round to nearest even, saturating)
-__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
-  return (uint32_t)r;
-}
-// two e4m3 codes (low byte first) -> their values
-__device__ __forceinline__ float2 e4m3x2_val(uint32_t codes) {
-  uint32_t h;
-  asm("{\n .reg .b16 t;\n cvt.u16.u32 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}" : "=r"(h) : "r"(codes));
-  return __half22float2(*reinterpret_cast<const __half2*>(&h));
-}
-
-// e8m0 byte of the scale that maps a block maximum mx into [128, 256)
-// (127 = 2^0 for an all-zero block)
-__device__ __forceinline__ int term_scale(float mx) {
-  if (mx == 0.f) return 127;
-  const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF);
-  return max(E - 7, 0);
-}
+using mx::e4m3x2;
+using mx::e4m3x2_val;
+using mx::idesc_mxf8f6f4;
+using mx::mma_mxf8f6f4;
+using mx::sdesc_atom;
+using mx::term_scale;
+using mx::tmem_cp_atom;
 
 // x [M, K] (row stride x_ld) -> the B operand of every 64-token tile tt,
 // Xq[tt][128][K] (row 64 t + j = term t of token 64 tt + j, e4m3), and its
@@ -717,11 +676,36 @@ static __device__ __align__(256) uint8_t g_wide_scratch[kNoAllocBytes];
 namespace {
 constexpr int kMaxScratchDevices = 64;
 std::mutex g_scratch_mu;
-void* g_scratch_ptr[kMaxScratchDevices];  // device address of g_wide_scratch per device ordinal
+// device address of g_wide_scratch per device ordinal, and the context it was
+// looked up in: a device reset (or a primary context torn down and made again)
+// reloads the module, so the address is looked up again when the context changes
+void* g_scratch_ptr[kMaxScratchDevices];
+CUcontext g_scratch_ctx[kMaxScratchDevices];
+
+CUcontext current_context() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    else
+      cudaGetLastError();
+  });
+  CUcontext c = nullptr;
+  if (fn && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
 }  // namespace
 
 int mxfp4_gemm_wide_noalloc_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* Out, int N,
                                    int K, int M, void* stream) {
+  // argument errors first, in the workspace entry point's order, then the scratch limit
+  if (!W || !Sp || !X || !Out) return B200KV_ERR_INVALID_ARG;
+  if (N <= 0 || K <= 0 || M <= 0 || x_ld < K) return B200KV_ERR_INVALID_ARG;
+  if (K % kKStep) return B200KV_ERR_UNSUPPORTED;
   if (M > kNoAllocMaxM || K > kNoAllocMaxK) return B200KV_ERR_WORKSPACE;
   if (mxfp4_gemm_wide_workspace_bytes(M, K) > kNoAllocBytes) return B200KV_ERR_WORKSPACE;
   int dev = 0;
@@ -731,15 +715,18 @@ int mxfp4_gemm_wide_noalloc_launch(const void* W, const void* Sp, const void* X,
   }
   void* ptr = nullptr;
   {
-    // set-up, once per device, with that device current: the array's device address
+    // set-up, once per device (and context), with that device current: the
+    // array's device address
     std::lock_guard<std::mutex> g(g_scratch_mu);
-    if (!g_scratch_ptr[dev]) {
+    const CUcontext ctx = current_context();
+    if (!g_scratch_ptr[dev] || g_scratch_ctx[dev] != ctx) {
       void* p = nullptr;
       if (cudaGetSymbolAddress(&p, g_wide_scratch) != cudaSuccess || !p) {
         cudaGetLastError();
         return B200KV_ERR_NO_DEVICE;
       }
       g_scratch_ptr[dev] = p;
+      g_scratch_ctx[dev] = ctx;
     }
     ptr = g_scratch_ptr[dev];
   }

@@ -13,6 +13,9 @@ import pytest
 import torch
 
 import mxfp4_oracle as MO
+from mxfp4_terms import e4m3_terms_reference as _e4m3_terms_reference
+from mxfp4_terms import integer_case as _integer_case
+from mxfp4_terms import within_one_rounding as _within_one_rounding
 
 pytestmark = pytest.mark.gpu
 
@@ -30,39 +33,6 @@ def _run(W, St, X, dev, **kw):
     import h4mv
     N, K = W.shape[0], W.shape[1] * 2
     return h4mv.mxfp4_gemm_wide(X.to(dev), W.to(dev), _packed(St, N, K, dev), **kw).float().cpu()
-
-
-def _within_one_rounding(Y, ref):
-    tol = ref.abs() * 2.0 ** -8 + 1e-6 * ref.abs().max()
-    return bool(((Y - ref).abs() <= tol).all()), float(((Y - ref).abs() - tol).max())
-
-
-def _e4m3_terms_reference(x):
-    """CPU restatement of the activation split: per 32-element block two e4m3
-    terms, each with scale 2^(floor(log2 m) - 7) for the block maximum m of
-    what is left (2^0 for an all-zero block), codes rounded to nearest even."""
-    r = x.double().view(x.shape[0], -1, 32).clone()
-    total = torch.zeros_like(r)
-    for _ in range(2):
-        mx = r.abs().amax(-1, keepdim=True)
-        s = torch.where(mx > 0, torch.exp2(torch.floor(torch.log2(mx.clamp(min=1e-300))) - 7),
-                        torch.ones_like(mx))
-        q = (r / s).float().to(torch.float8_e4m3fn).double() * s
-        total += q
-        r = r - q
-    return total.view_as(x).float()
-
-
-def _integer_case(N, K, M, seed):
-    """Weights uniform over the 16 codes with scale 2^0 and x integers in
-    [-8, 8]: every product is a multiple of 1/2 and every partial sum is exact
-    in fp32, so the bf16 result is unique."""
-    g = torch.Generator().manual_seed(seed)
-    W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, generator=g)
-    St = torch.full((N, K // 32), 127, dtype=torch.uint8)
-    X = torch.randint(-8, 9, (M, K), generator=g).to(torch.bfloat16)
-    ref = (X.double() @ MO.dequant_weight(W, St.t().contiguous()).double().t()).to(torch.bfloat16)
-    return W, St, X, ref.float()
 
 
 def test_one_hot_reproduces_x_exactly(cuda):
@@ -161,9 +131,9 @@ def test_dispatch_from_mxfp4_gemm(cuda):
 
 
 def test_matches_skinny_kernel_where_both_apply(cuda):
-    """At M = 8 both tensor-core kernels agree to two bf16 roundings of the
-    largest output (the skinny kernel's six-term split is within 5e-4 of each
-    block maximum)."""
+    """At M = 8 both tensor-core kernels (the same two-term activation split,
+    different summation orders) agree to two bf16 roundings of the largest
+    output."""
     import h4mv
     N, K, M = 4096, 4096, 8
     W, S, St, X = MO.make_case(N, K, M, seed=12)

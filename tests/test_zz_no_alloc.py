@@ -18,7 +18,7 @@ def test_two_calls_match_workspace_entry_point(cuda):
     import h4mv
     from _b200kv import lib
     stream = torch.cuda.current_stream().cuda_stream
-    for (N, K, M, seed) in [(4096, 4096, 64, 1), (1000, 14336, 100, 2)]:
+    for (N, K, M, seed) in [(4096, 4096, 64, 1), (1000, 14336, 100, 2), (256, 16384, 128, 3)]:
         W, S, St, X = MO.make_case(N, K, M, seed=seed)
         Wd, Xd = W.to(cuda), X.to(cuda)
         packed, _ = h4mv.pack_scales(St.to(cuda), N, K)
@@ -43,3 +43,11 @@ def test_refuses_sizes_past_the_scratch(cuda):
                                               out.data_ptr(), 128, 128, 129, stream) == 4
     assert lib.b200kv_mxfp4_gemm_wide_noalloc(W.data_ptr(), W.data_ptr(), big.data_ptr(), 16512,
                                               out.data_ptr(), 128, 16512, 1, stream) == 4
+    # M = 128 fills the array to its last byte at K = 16384; one more k-step is refused
+    assert lib.b200kv_mxfp4_gemm_wide_noalloc(W.data_ptr(), W.data_ptr(), big.data_ptr(), 16512,
+                                              out.data_ptr(), 128, 16512, 128, stream) == 4
+    # argument errors come first, as in the workspace entry point
+    assert lib.b200kv_mxfp4_gemm_wide_noalloc(None, W.data_ptr(), big.data_ptr(), 128,
+                                              out.data_ptr(), 128, 128, 129, stream) == 1
+    assert lib.b200kv_mxfp4_gemm_wide_noalloc(W.data_ptr(), W.data_ptr(), big.data_ptr(), 64,
+                                              out.data_ptr(), 128, 128, 129, stream) == 1
