@@ -117,6 +117,22 @@ lib.b200kv_mxfp4_gemm_wide.argtypes = [_vp, _vp, _vp, _i64, _vp, ctypes.c_size_t
 lib.b200kv_mxfp4_gemm_wide_noalloc.restype = _i32
 lib.b200kv_mxfp4_gemm_wide_noalloc.argtypes = [_vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _vp]
 
+
+
+class ChainOp(ctypes.Structure):
+    """b200kv_chain_op (include/b200kv.h)."""
+    _fields_ = [("weight", _vp), ("packed_scales", _vp), ("x", _vp), ("x_stride", _i64),
+                ("out", _vp), ("out_stride", _i64), ("N", ctypes.c_int32), ("K", ctypes.c_int32),
+                ("x_from", ctypes.c_int32), ("epilogue", ctypes.c_int32)]
+
+
+lib.b200kv_mxfp4_chain_workspace_bytes.restype = ctypes.c_size_t
+lib.b200kv_mxfp4_chain_workspace_bytes.argtypes = [ctypes.POINTER(ChainOp), _i32, _i32]
+lib.b200kv_mxfp4_chain.restype = _i32
+lib.b200kv_mxfp4_chain.argtypes = [ctypes.POINTER(ChainOp), _i32, _i32, _vp, ctypes.c_size_t, _vp]
+CHAIN_STORE = 0
+CHAIN_SWIGLU = 1
+
 lib.b200kv_kv_write.restype = _i32
 lib.b200kv_kv_write.argtypes = ([_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp] + [_i64] * 6 +
                                 [_vp, _vp, _vp] + [_i32] * 5 + [_vp])

@@ -14,6 +14,7 @@ enum DeviceStatus : int {
   kDevMbarrierTimeout = 0x101,   // a bulk copy never completed on its mbarrier
   kDevSplitOverflow = 0x102,     // seq_len larger than the context bound given
   kDevPeerTimeout = 0x103,       // a peer GPU's flag did not arrive in time
+  kDevChainTimeout = 0x104,      // a chained GEMV's input tile was not ready in time
 };
 extern __device__ int g_device_status;
 
@@ -53,6 +54,18 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over its `count` threads: every
+// thread gets the same answer, so all of them can leave a loop together.
+__device__ __forceinline__ bool named_bar_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
 // Bounded wait on an mbarrier phase.  Returns false (and records the device
 // status) when the phase did not complete within `max_tries` polls.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
@@ -71,6 +84,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
   atomicExch(&g_device_status, kDevMbarrierTimeout);
   return false;
+}
+
+// Global nanosecond timer (bounded spins on flags in global memory).
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
 }
 
 // One non-blocking test of an mbarrier phase.

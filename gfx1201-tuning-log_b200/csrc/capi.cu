@@ -93,6 +93,8 @@ int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, 
 int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
                      void* stream);
 size_t mxfp4_gemm_wide_workspace_bytes(int M, int K);
+size_t mxfp4_chain_workspace_bytes(const b200kv_chain_op* ops, int nops, int M);
+int mxfp4_chain_launch(const b200kv_chain_op* ops, int nops, int M, void* ws, size_t ws_bytes, void* stream);
 int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* ws,
                            size_t ws_bytes, void* Out, int N, int K, int M, void* stream);
 int mxfp4_gemm_wide_noalloc_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* Out, int N,
@@ -252,6 +254,15 @@ int b200kv_mxfp4_gemm_wide(const void* W, const void* packed_scales, const void*
 int b200kv_mxfp4_gemm_wide_noalloc(const void* W, const void* packed_scales, const void* X, int64_t x_stride,
                                    void* out, int N, int K, int M, void* stream) {
   return b200kv::mxfp4_gemm_wide_noalloc_launch(W, packed_scales, X, x_stride, out, N, K, M, stream);
+}
+
+size_t b200kv_mxfp4_chain_workspace_bytes(const b200kv_chain_op* ops, int nops, int M) {
+  return b200kv::mxfp4_chain_workspace_bytes(ops, nops, M);
+}
+
+int b200kv_mxfp4_chain(const b200kv_chain_op* ops, int nops, int M, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  return b200kv::mxfp4_chain_launch(ops, nops, M, workspace, workspace_bytes, stream);
 }
 
 int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_head,

@@ -7,7 +7,9 @@ argument order, raw ctypes call of h4mv_launch on the current stream);
 """
 import torch
 
-from _b200kv import check, lib
+import ctypes
+
+from _b200kv import CHAIN_STORE, CHAIN_SWIGLU, ChainOp, check, lib
 
 MAX_M = 8
 
@@ -144,3 +146,67 @@ def mxfp4_gemm_wide(x, weight, packed_scales, out=None, workspace=None):
                                      out.data_ptr(), N, K, M, stream.cuda_stream),
           "b200kv_mxfp4_gemm_wide")
     return out
+
+
+# ---- chains of dependent matvecs in one persistent launch ----------------------------
+def gate_up_row_order(inter, device=None):
+    """Row order of a fused [gate; up] weight ([2 inter, K], gate rows first) for
+    the chain's SwiGLU epilogue: blocks of 64 gate rows followed by the matching
+    64 up rows.  Apply once at load time to the weight's rows (and to its scales
+    before packing); inter % 64 == 0."""
+    if inter % 64:
+        raise ValueError(f"SwiGLU interleave needs inter % 64 == 0 (inter={inter})")
+    t = torch.arange(inter // 64, device=device)
+    r = torch.arange(64, device=device)
+    gate = (t[:, None] * 64 + r[None, :])
+    return torch.stack([gate, gate + inter], dim=1).reshape(-1)
+
+
+class MXFP4Chain:
+    """A fixed list of dependent MXFP4 matvecs (1 <= M <= 8) run by one
+    persistent launch (b200kv_mxfp4_chain).  Each op is a dict with
+    `weight` (uint8 [N, K/2]), `scales` (packed by pack_scales), `out` (bf16
+    [M, N], or [M, N/2] for epilogue CHAIN_SWIGLU) and either `x` (bf16 [M, K]
+    with unit inner stride) or `x_from` (index of an earlier op whose output is
+    x); optional `epilogue`.  The workspace, with its per-tile counters and
+    ready flags, belongs to this object: it is zeroed once here and must not be
+    shared with another chain.  Call run() on the stream the inputs were
+    written on (CUDA-graph capturable)."""
+
+    def __init__(self, ops, M, device):
+        self.M = M
+        self.device = torch.device(device)
+        self._keep = []
+        arr = (ChainOp * len(ops))()
+        for j, o in enumerate(ops):
+            w, p, out = o["weight"], o["scales"], o["out"]
+            N, K = w.shape[0], w.shape[1] * 2
+            x_from = o.get("x_from", -1)
+            epi = o.get("epilogue", CHAIN_STORE)
+            if w.dtype != torch.uint8 or not w.is_contiguous():
+                raise TypeError("weight must be a contiguous uint8 tensor")
+            if out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+                raise ValueError("out must be bf16 with unit inner stride")
+            x = o.get("x")
+            if x_from < 0:
+                if x is None or x.dtype != torch.bfloat16 or x.stride(-1) != 1 or x.shape[-1] != K:
+                    raise ValueError(f"op {j}: x must be bf16 [M, {K}] with unit inner stride")
+            arr[j].weight = w.data_ptr()
+            arr[j].packed_scales = p.data_ptr()
+            arr[j].x = x.data_ptr() if x_from < 0 else 0
+            arr[j].x_stride = x.stride(0) if x_from < 0 else 0
+            arr[j].out = out.data_ptr()
+            arr[j].out_stride = out.stride(0)
+            arr[j].N, arr[j].K, arr[j].x_from, arr[j].epilogue = N, K, x_from, epi
+            self._keep += [w, p, out] + ([x] if x_from < 0 else [])
+        self._ops = arr
+        self._n = len(ops)
+        nbytes = lib.b200kv_mxfp4_chain_workspace_bytes(arr, self._n, M)
+        if nbytes == 0:
+            raise ValueError("invalid chain (shapes, x_from, epilogue or M)")
+        self.workspace = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+
+    def run(self):
+        check(lib.b200kv_mxfp4_chain(self._ops, self._n, self.M, self.workspace.data_ptr(),
+                                     self.workspace.numel(), torch.cuda.current_stream(self.device).cuda_stream),
+              "b200kv_mxfp4_chain")

@@ -56,11 +56,13 @@ int b200kv_last_error(void);
  * Device-side status word written by kernels that hit a bounded wait limit.
  * 0 = clean; B200KV_DEV_MBARRIER_TIMEOUT: an mbarrier (a copy or a peer warp)
  * never completed; B200KV_DEV_PEER_TIMEOUT: a peer GPU's allreduce flag did not
- * arrive.  Reading it synchronises the given stream.
+ * arrive; B200KV_DEV_CHAIN_TIMEOUT: an input tile of a chained GEMV
+ * (b200kv_mxfp4_chain) was not ready in time.  Reading it synchronises the given stream.
  * b200kv_reset_device_status() clears it (async on stream).
  */
 #define B200KV_DEV_MBARRIER_TIMEOUT 0x101
 #define B200KV_DEV_PEER_TIMEOUT     0x103
+#define B200KV_DEV_CHAIN_TIMEOUT    0x104
 int b200kv_get_device_status(void* stream, int* status_out);
 int b200kv_reset_device_status(void* stream);
 
@@ -195,6 +197,46 @@ int b200kv_mxfp4_gemm_wide(const void* W, const void* packed_scales, const void*
  * rewrites all of the scratch it reads, so nothing has to start at zero. */
 int b200kv_mxfp4_gemm_wide_noalloc(const void* W, const void* packed_scales, const void* X,
                                    int64_t x_stride, void* out, int N, int K, int M, void* stream);
+
+/* A chain of dependent MXFP4 matvecs (1 <= M <= 8) in one persistent launch:
+ * op j computes the product of b200kv_mxfp4_gemm on (weight_j, packed scales,
+ * x_j), where x_j is an input of the call or op x_from's output, so a decode
+ * step's o -> gate_up -> down -> next qkv runs without a launch boundary
+ * between the products.  Every SM streams its share of every op's weights
+ * without waiting (load-time data) and waits, per 128-k box, only for the
+ * tiles of the producing op that hold that slice of x; a tile whose K range is
+ * split over several SMs is reduced in a fixed order through the workspace.
+ * Arithmetic per op as b200kv_mxfp4_gemm (x as two exact e4m3 terms, fp32
+ * accumulation, bf16 output).  No counterpart call in the reference, whose
+ * engine launches one h4mv per linear (h4mv/fp8kv_hipw4.py:62-94).
+ *   epilogue B200KV_CHAIN_STORE: out[m, n] (bf16, rows out_stride apart).
+ *   epilogue B200KV_CHAIN_SWIGLU: the op's weight rows are interleaved in
+ *     blocks of 64 (rows 128 t .. 128 t + 63 = gate rows 64 t .., the next 64 =
+ *     the matching up rows), N % 128 == 0, and out[m, i] = bf16(bf16(silu(g)) * u)
+ *     for i < N / 2 (the rounding of b200kv_swiglu).
+ *   x_from = -1: x (bf16, rows x_stride apart, 16-byte aligned, x_stride % 8 == 0)
+ *     is read from `x`; x_from = i < j: x is op i's output (x, x_stride ignored).
+ *   K % 128 == 0, at most 8 ops.  The workspace (b200kv_mxfp4_chain_workspace_bytes,
+ *   256-byte aligned) holds per-tile counters and ready flags that persist
+ *   across calls: zero it once before the first call and keep one workspace
+ *   per chain that is replayed (a call that reported B200KV_DEV_CHAIN_TIMEOUT
+ *   leaves it inconsistent: zero it again).  One CTA per SM, cooperative. */
+#define B200KV_CHAIN_STORE  0
+#define B200KV_CHAIN_SWIGLU 1
+typedef struct b200kv_chain_op {
+  const void* weight;          /* uint8 [N, K/2], e2m1 pairs, 16-byte aligned */
+  const void* packed_scales;   /* b200kv_mxfp4_pack_scales output for (N, K) */
+  const void* x;               /* bf16 [M, K] when x_from == -1 */
+  int64_t x_stride;            /* elements between x rows */
+  void* out;                   /* bf16 [M, N] (N / 2 for SWIGLU) */
+  int64_t out_stride;          /* elements between output rows */
+  int32_t N, K;
+  int32_t x_from;              /* -1, or the index of an earlier op whose output is x */
+  int32_t epilogue;            /* B200KV_CHAIN_STORE or B200KV_CHAIN_SWIGLU */
+} b200kv_chain_op;
+size_t b200kv_mxfp4_chain_workspace_bytes(const b200kv_chain_op* ops, int nops, int M);
+int b200kv_mxfp4_chain(const b200kv_chain_op* ops, int nops, int M, void* workspace, size_t workspace_bytes,
+                       void* stream);
 
 /* ---- fp8 paged-KV causal prefill attention -----------------------------------
  *
