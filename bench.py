@@ -1,20 +1,26 @@
 #!/usr/bin/env python
 """Hot-path benchmark on B200: one 7B-class decode step's attention + MXFP4
-linears (BASELINE metric "decode-attn & MXFP4 GEMV HBM GB/s").
+linears (BASELINE metric "decode-attn & MXFP4 GEMV HBM GB/s; 7B decode tok/s
+at bs 1/4/8, 1-8 GPU").
 
 A step = 32 layers x [ qkv GEMV (M=B) -> paged fp8 decode attention over
 B sequences of 4096 tokens (q read straight out of the qkv output) -> o_proj
 GEMV -> gate_up GEMV ; down GEMV (M=B, K=14336) ], every layer with its own
 weights and KV pool (3.9 GB at B=1, far above the 126 MB L2, so no flush is
 needed between steps).  value = algorithmic HBM bytes of the step / device time.
+The same line carries the step's parts at B = 1, 4 and 8, the 7B decoder's
+tok/s at B = 1, 4 and 8 (config 4), config 2 at M = 64, config 3 (prefill)
+and config 5 (serving), each with its CPU baseline where the metric has one.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl b200|reference]
 
-N > 1 runs under torchrun as independent replicas (one model per GPU, weak
-scaling, no collective on the data path); the reported time is the max over
-ranks.  `--impl reference` times the reference's own CPU path for this work
-(the PyTorch dequant + attention / dequant + matmul checker restated in
-oracle/) on the host's cores, on a bounded sample (one layer per step).
+N > 1 runs under torchrun with tensor parallelism over the N GPUs (attention
+by kv head, qkv/gate_up column-parallel, o/down row-parallel + allreduce;
+--parallel replicas runs N independent copies instead); the reported time is
+the max over ranks.  `--impl reference` times the reference's own CPU path
+for this work (the PyTorch dequant + attention / dequant + matmul checker
+restated in oracle/) on the host's cores, on a bounded sample (one layer per
+step).
 """
 import argparse
 import json
@@ -65,8 +71,8 @@ def workload_config(args):
                         f"qkv/o/gate_up/down at M={args.batch} + fp8 paged decode attention "
                         f"{args.batch} seq x {args.ctx} ctx, GQA 32/8, D 128, block 16]",
             "batch": args.batch, "ctx": args.ctx, "layers": args.layers,
-            "mxfp4_kernel": ("block-scaled tcgen05 (kind::mxf4), scales packed at load"
-                             if args.gemv == "tc" else "CUDA-core mma.sync"),
+            "mxfp4_kernel": ("block-scaled tcgen05 (kind::mxf8f6f4: e2m1 weights, x as two exact e4m3 "
+                             "terms), scales packed at load" if args.gemv == "tc" else "CUDA-core mma.sync"),
             "l2": "inputs larger than L2 (distinct weights/KV per layer), no flush",
             "parallelism": (f"tp{args.tp}: attention by kv head, qkv/gate_up column-parallel, "
                             f"o/down row-parallel + {args.allreduce} allreduce (in the CUDA graph)"
@@ -135,14 +141,13 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-def build_model(args, dev):
-    """Random-init weights and KV pools for `layers` layers on `dev`."""
-    B, ctx, L, tp = args.batch, args.ctx, args.layers, args.tp
-    hkv = HKV // tp  # this rank's kv heads
+def build_weights(args, dev):
+    """Random-init MXFP4 weights of `layers` layers (this rank's shards), scales
+    packed at load; shared by every batch size."""
+    tp = args.tp
     g = torch.Generator(device=dev).manual_seed(1234 + args.rank)
-    layers = []
-    nblk = ctx // PBLK
-    for _ in range(L):
+    weights = []
+    for _ in range(args.layers):
         lay = {}
         for name, N, K in rank_shapes(tp):
             W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
@@ -154,6 +159,22 @@ def build_model(args, dev):
                 lay[name] = (W, packed)
             else:
                 lay[name] = (W, St)
+        weights.append(lay)
+    return weights
+
+
+def build_model(args, dev, weights, B):
+    """Per-layer fp8 KV pools for B sequences of args.ctx tokens (random
+    permuted block tables, per-tensor amax/448 scales), the layers' inputs, and
+    the step's output buffers.  Returns (layers, bufs); layers[i] holds the
+    weights of layer i too."""
+    ctx, tp = args.ctx, args.tp
+    hkv = HKV // tp  # this rank's kv heads
+    g = torch.Generator(device=dev).manual_seed(4321 + 17 * B + args.rank)
+    layers = []
+    nblk = ctx // PBLK
+    for w in weights:
+        lay = dict(w)
         nb = B * nblk
         kf = torch.randn(nb, PBLK, hkv, D, device=dev, generator=g)
         ks = kf.abs().max() / 448.0
@@ -170,6 +191,7 @@ def build_model(args, dev):
         lay["act"] = torch.randn(B, 14336 // tp, device=dev, generator=g).to(torch.bfloat16)
         layers.append(lay)
     bufs = {
+        "B": B,
         "qkv": torch.empty(B, 6144 // tp, dtype=torch.bfloat16, device=dev),
         "attn": torch.empty(B, HQ // tp, D, dtype=torch.bfloat16, device=dev),
         "o": torch.empty(B, 4096, dtype=torch.bfloat16, device=dev),
@@ -188,7 +210,7 @@ def run_step(layers, bufs, args, which=("gemv", "attn", "comm")):
     import fp8kv_v3
     import h4mv
     import tp
-    B = args.batch
+    B = bufs["B"]
     hq = HQ // args.tp
     sm = D ** -0.5
     gemv = h4mv.mxfp4_gemm if args.gemv == "tc" else h4mv.mxfp4_gemv
@@ -461,16 +483,15 @@ def serving_part(args, dev, barrier, layers=32, steps=2):
 DECODE_PROMPT, DECODE_TOKENS = 4096, 256
 
 
-def decode_7b_part(args, dev, barrier, allreduce):
+def decode_7b_part(args, dev, barrier, allreduce, B):
     """Config 4: the full 7B MXFP4 decoder (decoder.py) decoding DECODE_TOKENS
     greedy tokens per sequence after a DECODE_PROMPT-token prompt, batch
-    args.batch, one CUDA-graph replay per token.  The prompt's KV pages are
+    B, one CUDA-graph replay per token.  The prompt's KV pages are
     synthetic (random fp8 of the cache's scale), not computed: the decode cost
     depends only on their length; the prefill kernel is timed as config 3.
     Returns (ms per token step, tokens/s over the whole batch)."""
     import decoder
     cfg = decoder.SEVEN_B
-    B = args.batch
     gather = None
     if args.tp > 1:
         import torch.distributed as dist
@@ -492,8 +513,38 @@ def decode_7b_part(args, dev, barrier, allreduce):
     graph = capture(dec.step)
     steps = min(DECODE_TOKENS - 3, args.steps)
     ms = time_graph(graph, steps, 1, barrier)
-    del graph
+    del graph, dec
+    torch.cuda.empty_cache()
     return ms, B / (ms * 1e-3)
+
+
+BATCH_SWEEP = (1, 4, 8)
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "mxfp4_mma_7b_m1.md")
+
+
+def profile_traffic():
+    """Average DRAM bytes per launch of the four 7B shapes at M = 1 from the
+    `dram_bytes_per_launch:` line of the committed ncu summary (None when the
+    summary has no such line)."""
+    try:
+        with open(TRAFFIC_PROFILE) as f:
+            for line in f:
+                if line.startswith("dram_bytes_per_launch:"):
+                    vals = [float(t.split("=")[1]) for t in line.split(":", 1)[1].split()]
+                    return sum(vals) / len(vals), f"{os.path.relpath(TRAFFIC_PROFILE, ROOT)} (ncu, four shapes)"
+    except (OSError, ValueError, IndexError):
+        pass
+    return None, None
 
 
 def max_over_ranks(x, dist_on, dev):
@@ -522,6 +573,136 @@ def cpu_layer_sample(args, seed=0):
     FO.decode_reference(dc["q"], dc["k_cache"], dc["v_cache"], dc["qsl"], dc["seq_lens"],
                         dc["block_table"], dc["k_scale"], dc["v_scale"], dc["sm_scale"])
     return time.perf_counter() - t0, layer_bytes(B, args.ctx)
+
+
+def cpu_prefill_baseline():
+    """Config 3 on the host: the oracle's causal prefill (prefill_test.py:23-38,
+    per sequence) on the 512- and 1024-token sequences of config 3 (a bounded
+    sample), scaled to the whole call by FLOPs.  Returns the cpu_baseline dict."""
+    sys.path.insert(0, ORACLE)
+    import fp8kv_oracle as FO
+    torch.set_num_threads(os.cpu_count())
+    lens = PREFILL_LENS[:2]
+    g = torch.Generator().manual_seed(3)
+    T = sum(lens)
+    nblk = [L // PBLK for L in lens]
+    nb = sum(nblk)
+    q = torch.randn(T, HQ, D, generator=g).to(torch.bfloat16)
+    kc = (torch.randn(nb, PBLK, HKV, D, generator=g) * 8).to(torch.float8_e4m3fn)
+    vc = (torch.randn(nb, PBLK, HKV, D, generator=g) * 8).to(torch.float8_e4m3fn)
+    perm = torch.randperm(nb, generator=g).to(torch.int32)
+    bt = torch.zeros(len(lens), max(nblk), dtype=torch.int32)
+    pos = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = perm[pos:pos + n]
+        pos += n
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    t0 = time.perf_counter()
+    FO.prefill_reference(q, kc, vc, cu, sl, bt, 1 / 16, 1 / 16, D ** -0.5)
+    t = time.perf_counter() - t0
+    tflops = prefill_flops(lens) / t / 1e12
+    return {"value": tflops, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+            "us_per_call_extrapolated": prefill_flops(PREFILL_LENS) / (tflops * 1e12) * 1e6,
+            "sample": f"oracle causal prefill of the {list(lens)}-token sequences of config 3 "
+                      f"({prefill_flops(lens) / 1e9:.1f} GFLOP, {t:.2f} s), scaled to the call by FLOPs"}
+
+
+_CPU_CACHE = {}
+
+
+def cpu_decoder_baseline(B):
+    """Config 4 on the host: one oracle decoder step (oracle/decoder_oracle.py,
+    HF Llama semantics) of a 2-layer model of the 7B widths at batch B over
+    4096-token fp8 caches, and its final norm + 128256-row lm_head alone; a
+    32-layer step is extrapolated from the per-layer time.  Returns the
+    cpu_baseline dict (tok/s)."""
+    sys.path.insert(0, ORACLE)
+    import dataclasses
+
+    import decoder
+    import decoder_oracle as DO
+    torch.set_num_threads(os.cpu_count())
+    cfg = decoder.SEVEN_B
+    ctx = DECODE_PROMPT
+    table = DO.rope_table(ctx + 8, cfg.head_dim, cfg.rope_theta)
+    if "head" not in _CPU_CACHE:  # 2 x 0.5 G bf16 values, drawn once
+        _CPU_CACHE["head"] = decoder.random_head(cfg, 7)
+    head = _CPU_CACHE["head"]
+    if "layers" not in _CPU_CACHE:
+        _CPU_CACHE["layers"] = []
+        for li in range(2):
+            lay = decoder.random_layer(cfg, li, 7)
+            _CPU_CACHE["layers"].append({k: ((v[0], v[1].t().contiguous()) if isinstance(v, tuple) else v)
+                                         for k, v in lay.items()})
+    nblk = -(-(ctx + 1) // cfg.block_size)
+    g = torch.Generator().manual_seed(5)
+    caches = []
+    for _ in range(2):
+        k = (torch.randn(B * nblk, cfg.block_size, cfg.kv_heads, cfg.head_dim, generator=g) * 4)
+        v = (torch.randn(B * nblk, cfg.block_size, cfg.kv_heads, cfg.head_dim, generator=g) * 4)
+        caches.append({"k": k.to(torch.float8_e4m3fn), "v": v.to(torch.float8_e4m3fn), "ks": 0.05, "vs": 0.05})
+    bt = torch.arange(B * nblk, dtype=torch.int32).view(B, nblk)
+    tokens = torch.randint(0, cfg.vocab, (B,), generator=g)
+    positions = torch.full((B,), ctx, dtype=torch.int32)
+    w = {"embed": head["embed"], "lm_head": head["lm_head"], "final_norm": head["final_norm"],
+         "layers": _CPU_CACHE["layers"]}
+    t2 = t_head = 1e30
+    for _ in range(2):  # the first call pays first-touch costs
+        t0 = time.perf_counter()
+        DO.decode_step(dataclasses.replace(cfg, layers=2), w, caches, tokens, positions, bt, table)
+        t2 = min(t2, time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        x = DO.rmsnorm(head["embed"][tokens.long()], head["final_norm"], cfg.eps)
+        x.float() @ head["lm_head"].float().t()
+        t_head = min(t_head, time.perf_counter() - t0)
+    per_layer = max((t2 - t_head) / 2, 1e-9)
+    step = cfg.layers * per_layer + t_head
+    return {"value": B / step, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle decoder step at batch {B} of a 2-layer model of the 7B widths ({t2:.2f} s) "
+                      f"and its final norm + lm_head alone ({t_head:.2f} s), extrapolated to {cfg.layers} "
+                      f"layers: {step:.1f} s per token step"}
+
+
+def cpu_serving_baseline():
+    """Config 5 on the host, subsampled: one layer of the oracle at 7B widths
+    for 64 of the step's 8252 tokens through the four MXFP4 projections, the
+    decode attention of 4 of its 60 sequences (contexts drawn as config 5
+    draws them) and the causal prefill of one 2048-token sequence; the 32-layer
+    step is extrapolated linearly (tokens for the projections, sequences for
+    attention).  Returns the cpu_baseline dict (tok/s)."""
+    sys.path.insert(0, ORACLE)
+    import fp8kv_oracle as FO
+    import mxfp4_oracle as MO
+    torch.set_num_threads(os.cpu_count())
+    T = SERVE_DECODES + SERVE_PREFILLS * SERVE_PREFILL_LEN
+    tok = 64
+    gc = torch.Generator().manual_seed(21)
+    ctx = torch.randint(SERVE_CTX[0], SERVE_CTX[1] + 1, (SERVE_DECODES,), generator=gc).tolist()
+    t0 = time.perf_counter()
+    for i, (_, N, K) in enumerate(SHAPES):
+        W, S, St, X = MO.make_case(N, K, tok, seed=i)
+        MO.mxfp4_linear_reference(W, S, X)
+    t_gemm = time.perf_counter() - t0
+    dc = FO.make_decode_case(4, [c + 1 for c in ctx[:4]], seed=2)
+    t0 = time.perf_counter()
+    FO.decode_reference(dc["q"], dc["k_cache"], dc["v_cache"], dc["qsl"], dc["seq_lens"], dc["block_table"],
+                        dc["k_scale"], dc["v_scale"], dc["sm_scale"])
+    t_dec = time.perf_counter() - t0
+    L = SERVE_PREFILL_LEN
+    nb = L // PBLK
+    g = torch.Generator().manual_seed(3)
+    q = torch.randn(L, HQ, D, generator=g).to(torch.bfloat16)
+    kc = (torch.randn(nb, PBLK, HKV, D, generator=g) * 8).to(torch.float8_e4m3fn)
+    t0 = time.perf_counter()
+    FO.prefill_reference(q, kc, kc, torch.tensor([0, L], dtype=torch.int32), torch.tensor([L], dtype=torch.int32),
+                         torch.arange(nb, dtype=torch.int32).view(1, nb), 1 / 16, 1 / 16, D ** -0.5)
+    t_pre = time.perf_counter() - t0
+    step = 32 * (t_gemm * T / tok + t_dec * SERVE_DECODES / 4 + t_pre * SERVE_PREFILLS)
+    return {"value": T / step, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"1 layer: projections for {tok} of {T} tokens ({t_gemm:.2f} s), decode attention of 4 "
+                      f"of {SERVE_DECODES} sequences ({t_dec:.2f} s), one {L}-token prefill ({t_pre:.2f} s); "
+                      f"extrapolated to 32 layers x the whole batch: {step:.0f} s per step"}
 
 
 def cpu_baseline(args, reps=3):
@@ -565,6 +746,28 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------------------
+def run_mxfp4_m1(args):
+    """The four 7B MXFP4 projections at M = 1 through h4mv.mxfp4_gemm, --warmup
+    then --steps rounds of four launches (each on its own weights): the case the
+    committed ncu summary of the dominant kernel captures."""
+    import h4mv
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    cases = []
+    for _, N, K in SHAPES:
+        W = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g)
+        St = torch.randint(119, 126, (N, K // 32), dtype=torch.uint8, device=dev, generator=g)
+        P, _ = h4mv.pack_scales(St, N, K)
+        x = torch.randn(1, K, device=dev, generator=g).to(torch.bfloat16)
+        cases.append((x, W, P, torch.empty(1, N, dtype=torch.bfloat16, device=dev)))
+    for _ in range(args.warmup + args.steps):
+        for x, W, P, out in cases:
+            h4mv.mxfp4_gemm(x, W, P, out=out)
+    torch.cuda.synchronize()
+    print(json.dumps({"part": "mxfp4_m1", "launches": 4 * (args.warmup + args.steps)}))
+
+
 def run_b200(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -583,7 +786,8 @@ def run_b200(args):
                                 device_id=dev)
         barrier = dist.barrier
 
-    layers, bufs = build_model(args, dev)
+    weights = build_weights(args, dev)
+    layers, bufs = build_model(args, dev, weights, args.batch)
     comm = None
     if args.tp > 1:
         import tp
@@ -609,17 +813,55 @@ def run_b200(args):
     clk = clocks.stop()
     ms = max_over_ranks(ms, dist_on, dev)
 
+    if args.part == "step":
+        if rank == 0:
+            print(json.dumps({"part": "step", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup}))
+        del g_step, g_gemv, g_attn, g_comm
+        if dist_on:
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier()
+            if comm is not None:
+                comm.close()
+            dist.destroy_process_group()
+        return None
+
     # ---- per-kernel breakdown (same graphs, kernel class alone) ------------
     ms_gemv = max_over_ranks(time_graph(g_gemv, args.steps, 2, barrier), dist_on, dev)
     ms_attn = max_over_ranks(time_graph(g_attn, args.steps, 2, barrier), dist_on, dev)
     ms_comm = (max_over_ranks(time_graph(g_comm, args.steps, 2, barrier), dist_on, dev)
                if g_comm is not None else None)
+    # ---- the step's parts at B = 1, 4, 8 (north_star's "at batch 1-8") ----
+    hbm_peak_sweep = _peaks().get("hbm_gbs", 6650.0)
+    sweep = {}
+    for Bs in BATCH_SWEEP:
+        if Bs == args.batch:
+            lay_s, buf_s, gg, ga = layers, bufs, g_gemv, g_attn
+        else:
+            lay_s, buf_s = build_model(args, dev, weights, Bs)
+            gg = capture(lambda: run_step(lay_s, buf_s, args, which=("gemv",)))
+            ga = capture(lambda: run_step(lay_s, buf_s, args, which=("attn",)))
+        ms_g = max_over_ranks(time_graph(gg, args.steps, 2, barrier), dist_on, dev)
+        ms_a = max_over_ranks(time_graph(ga, args.steps, 2, barrier), dist_on, dev)
+        gb = args.layers * sum(gemv_bytes(N, K, Bs) for _, N, K in rank_shapes(args.tp))
+        ab = args.layers * decode_bytes(Bs, args.ctx, args.tp)
+        sweep[Bs] = {
+            "mxfp4_gemv": {"us_per_step": ms_g * 1e3, "launches_per_step": 4 * args.layers,
+                           "gbs": gb / (ms_g * 1e-3) / 1e9, "hbm_frac": gb / (ms_g * 1e-3) / 1e9 / hbm_peak_sweep},
+            "decode_attn": {"us_per_step": ms_a * 1e3, "launches_per_step": args.layers,
+                            "gbs": ab / (ms_a * 1e-3) / 1e9, "hbm_frac": ab / (ms_a * 1e-3) / 1e9 / hbm_peak_sweep}}
+        if Bs != args.batch:
+            del gg, ga, lay_s, buf_s
+            torch.cuda.empty_cache()
     us_pre, flops_pre = prefill_part(dev, args.steps, 2, barrier)
     us_pre = max_over_ranks(us_pre, dist_on, dev)
     us_wide, bytes_wide, flops_wide = wide_gemm_part(dev, args.steps, 2, barrier, args.tp)
     us_wide = max_over_ranks(us_wide, dist_on, dev)
-    ms_tok, _ = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None)
-    ms_tok = max_over_ranks(ms_tok, dist_on, dev)
+    dec7 = {}
+    for Bs in BATCH_SWEEP:
+        ms_b, _ = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None, Bs)
+        dec7[Bs] = max_over_ranks(ms_b, dist_on, dev)
+    ms_tok = dec7[args.batch] if args.batch in dec7 else None
     serve = None
     if args.serving == "on":
         res, serve_tokens, serve_kv, serve_pre, serve_gemm = serving_part(args, dev, barrier)
@@ -675,18 +917,19 @@ def run_b200(args):
     gemv_gbs = gemv_bytes_step / (ms_gemv * 1e-3) / 1e9
     n_gemv = args.layers * 4
 
-    # DRAM bytes per launch of the dominant kernel from one ncu capture
-    # (dram__bytes_read.sum + dram__bytes_write.sum, cold cache) of the four
-    # 7B shapes at M = 1: 13.43, 8.97, 62.72 and 31.27 MB for qkv, o,
-    # gate_up and down.  Other configurations have no capture.
+    # DRAM bytes per launch of the dominant kernel (dram__bytes_read.sum +
+    # dram__bytes_write.sum) from the committed ncu summary of the four 7B
+    # shapes at M = 1, averaged over the four launches of a layer
     traffic, traffic_src = None, None
     if args.gemv == "tc" and args.batch == 1 and args.tp == 1:
-        traffic = (13.43 + 8.97 + 62.72 + 31.27) / 4 * 1e6
-        traffic_src = "ncu dram__bytes_read+write of the four shapes at M=1, averaged"
+        traffic, traffic_src = profile_traffic()
 
     result = None
     if rank == 0:
         cpu = cpu_baseline(args) if world == 1 else None
+        cpu_pre = cpu_prefill_baseline() if world == 1 else None
+        cpu_dec = {b: cpu_decoder_baseline(b) for b in BATCH_SWEEP} if world == 1 else {}
+        cpu_srv = cpu_serving_baseline() if world == 1 and serve is not None else None
         copies = world // args.tp  # full model copies streamed per step
         value = copies * step_bytes / (ms * 1e-3) / 1e9
         result = {
@@ -709,6 +952,7 @@ def run_b200(args):
                                  "bound": "tensor", "peak_tflops": peaks.get("bf16_tflops", 1590.0),
                                  "frac": flops_pre / (us_pre * 1e-6) / 1e12
                                  / peaks.get("bf16_tflops", 1590.0),
+                                 "cpu_baseline": cpu_pre,
                                  "note": "timed outside the decode step (not part of value); "
                                          "each rank runs the full call"},
                 "mxfp4_gemm_m64": {"workload": f"config 2 at M = {WIDE_M}: qkv, o, gate_up, down "
@@ -725,12 +969,21 @@ def run_b200(args):
                                            "terms at twice the bf16 rate, so bf16 peak is the bound)"},
                 "decode_7b": {"workload": f"config 4: full 7B MXFP4 decoder (RMSNorm, qkv, RoPE + fp8 "
                                           f"KV write, decode attention, o, SwiGLU MLP, bf16 lm_head "
-                                          f"128256, greedy argmax), batch {args.batch}, "
+                                          f"128256, greedy argmax), batch 1/4/8, "
                                           f"{DECODE_PROMPT}-token prompt (synthetic KV pages), "
                                           f"tokens {DECODE_PROMPT}+; one CUDA-graph replay per token",
+                              "by_batch": {str(b): {"ms_per_token_step": dec7[b],
+                                                    "tok_s": copies * b / (dec7[b] * 1e-3),
+                                                    "cpu_baseline": cpu_dec.get(b)}
+                                           for b in BATCH_SWEEP},
                               "ms_per_token_step": ms_tok,
-                              "tok_s": copies * args.batch / (ms_tok * 1e-3),
+                              "tok_s": copies * args.batch / (ms_tok * 1e-3) if ms_tok else None,
                               "note": "timed outside the hot-path step (not part of value)"},
+                "batch_sweep": {"workload": "the step's two kernel classes alone (same graphs as value) at "
+                                            "B = 1, 4, 8: MXFP4 GEMV at M = B (qkv, o, gate_up, down x "
+                                            f"{args.layers} layers) and decode attention over B x {args.ctx} "
+                                            "tokens", "by_batch": {str(b): v for b, v in sweep.items()},
+                                "peak_gbs": hbm_peak},
             },
             "roofline": {"bound": "hbm",
                          "kernel": "mxfp4_mma_kernel" if args.gemv == "tc" else "mxfp4_gemv_kernel",
@@ -743,9 +996,10 @@ def run_b200(args):
             "cpu_baseline": cpu,
             "e2e": {"value": copies * step_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "pinned host activations -> H2D, graph of public-API calls "
-                            f"(h4mv.{'mxfp4_gemm' if args.gemv == 'tc' else 'mxfp4_gemv'}, "
-                            "fp8kv_v3.run), D2H of outputs"},
+                    "path": "pinned host activations -> H2D, then one CUDA-graph replay of the step's "
+                            f"public-API calls (h4mv.{'mxfp4_gemm' if args.gemv == 'tc' else 'mxfp4_gemv'}, "
+                            "fp8kv_v3.run) captured once, as a graph-replayed engine runs them (their Python "
+                            "dispatch is outside the timed region), D2H of outputs"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
@@ -765,6 +1019,7 @@ def run_b200(args):
                 "gemm_ms": serve["gemm"],
                 "gemm_tflops": serve_gemm / (serve["gemm"] * 1e-3) / 1e12,
                 "decode_kv_gb_per_step": serve_kv / 1e9, "prefill_gflop_per_step": serve_pre / 1e9,
+                "cpu_baseline": cpu_srv,
                 "note": "mixed = b200kv_attn_varlen_mixed, what the vLLM forward patch calls (decode "
                         "rows to the decode kernel, prefills to the varlen kernel, split on the device); "
                         "split = the same two kernels as two calls on host-known row ranges; one_call = "
@@ -811,6 +1066,9 @@ def main():
                     help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1)")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
                     help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
+    ap.add_argument("--part", choices=("all", "step", "mxfp4_m1"), default="all",
+                    help="all: the full line; step: the headline step only (for an ncu launch list); "
+                         "mxfp4_m1: the four 7B MXFP4 launches at M = 1, --steps times (for an ncu capture)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 300 if args.impl == "b200" else 10
@@ -820,6 +1078,8 @@ def main():
     args.rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         run_reference(args)
+    elif args.part == "mxfp4_m1":
+        run_mxfp4_m1(args)
     else:
         run_b200(args)
 

@@ -27,7 +27,8 @@
 //    (bounded, %globaltimer, acquire loads) on their ready flags;
 //  * four issuing warps take every fourth box into accumulators of their own
 //    (one thread issues a block-scaled MMA about every 127 cycles);
-//  * four epilogue warps drain a segment's accumulators.  A tile split over
+//  * two groups of four epilogue warps take alternate segments (four
+//    accumulator buffers) and drain a segment's accumulators.  A tile split over
 //    several CTAs is reduced through global memory: each segment writes its
 //    fp32 partial, counts itself on the tile's counter, and the last to arrive
 //    adds the partials in segment order (so the result does not depend on
@@ -76,12 +77,14 @@ constexpr int kNS = 10;               // weight ring slots (one box each)
 constexpr int kNXS = 18;              // activation-term ring slots
 constexpr int kNI = 4;                // MMA-issuing warps
 constexpr int kXW = 4;                // activation-split warps
-constexpr int kEw0 = 1 + kNI + kXW;   // first of the four epilogue warps
-constexpr int kThreads = 32 * (kEw0 + 4);
+constexpr int kEG = 2;                // epilogue warpgroups (alternate segments)
+constexpr int kND = 4;                // accumulator buffers (segment sigma uses sigma % 4)
+constexpr int kEw0 = 1 + kNI + kXW;   // first of the 4 kEG epilogue warps
+constexpr int kThreads = 32 * (kEw0 + 4 * kEG);
 constexpr int kDStride = 16 * kNI;    // accumulator buffer: 16 columns per issuer
-constexpr int kColA = 2 * kDStride;   // weight-scale atoms of the ring slots
+constexpr int kColA = kND * kDStride;  // weight-scale atoms of the ring slots
 constexpr int kColB = kColA + 4 * kNS;  // activation-scale atoms
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;
 static_assert(kColB + 4 * kNXS <= (int)kTmemCols, "tensor-memory columns");
 constexpr int kEpiStore = B200KV_CHAIN_STORE, kEpiSwiglu = B200KV_CHAIN_SWIGLU;
 constexpr unsigned long long kSpinLimitNs = 200ull * 1000 * 1000;
@@ -92,7 +95,7 @@ constexpr size_t kOffAtoms = (size_t)kNS * kBox;
 constexpr size_t kOffXb = (kOffAtoms + (size_t)kNS * kAtom + 1023) / 1024 * 1024;
 constexpr size_t kOffXa = kOffXb + (size_t)kNXS * kBBox;
 constexpr size_t kOffEx = kOffXa + (size_t)kNXS * kAtom;
-constexpr size_t kSmem = kOffEx + (size_t)kTile * kMaxM * 4 + 1024;
+constexpr size_t kSmem = kOffEx + (size_t)kEG * kTile * kMaxM * 4 + 1024;
 static_assert(kOffXb % 1024 == 0, "activation boxes must be 1024-aligned");
 
 struct ChainOpDev {
@@ -119,18 +122,18 @@ struct ChainMaps {
   CUtensorMap m[kMaxOps];
 };
 
-__device__ __forceinline__ int64_t range_start(int c, int64_t T, int G) { return (int64_t)c * T / G; }
+__device__ __forceinline__ int range_start(int c, int T, int G) { return c * T / G; }
 // CTA whose range holds box b
-__device__ __host__ __forceinline__ int cta_of(int64_t b, int64_t T, int G) { return (int)(((b + 1) * G - 1) / T); }
+__device__ __host__ __forceinline__ int cta_of(int b, int T, int G) { return ((b + 1) * G - 1) / T; }
 
 // segments of tile `tile` (boxes [ts, te)): CTAs with a non-empty part of it;
 // returns the count and this CTA's ordinal among them
-__device__ __host__ inline int tile_segments(int64_t T, int G, int nsteps, int tile, int c, int* ord) {
-  const int64_t ts = (int64_t)tile * nsteps, te = ts + nsteps;
+__device__ __host__ inline int tile_segments(int T, int G, int nsteps, int tile, int c, int* ord) {
+  const int ts = tile * nsteps, te = ts + nsteps;
   const int f = cta_of(ts, T, G), l = cta_of(te - 1, T, G);
   int n = 0, o = -1;
   for (int cc = f; cc <= l; ++cc) {
-    const int64_t a0 = (int64_t)cc * T / G, a1 = (int64_t)(cc + 1) * T / G;
+    const int a0 = cc * T / G, a1 = (cc + 1) * T / G;
     if ((a0 > ts ? a0 : ts) < (a1 < te ? a1 : te)) {
       if (cc == c) o = n;
       ++n;
@@ -162,6 +165,16 @@ __device__ bool wait_flag(const uint32_t* flag, uint32_t want, volatile int* abo
   }
 }
 
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // Visits the CTA's segments in order: fn(j, tile, k0, n, s, sigma) with s the
@@ -171,14 +184,14 @@ __device__ __forceinline__ void for_each_segment(const ChainArgs& a, int c, F&& 
   int s = 0, sigma = 0;
   for (int j = 0; j < a.nops; ++j) {
     const ChainOpDev& op = a.op[j];
-    const int64_t T = (int64_t)op.ntiles * op.nsteps;
-    int64_t b = range_start(c, T, a.G);
-    const int64_t b1 = range_start(c + 1, T, a.G);
+    const int T = op.ntiles * op.nsteps;
+    int b = range_start(c, T, a.G);
+    const int b1 = range_start(c + 1, T, a.G);
     while (b < b1) {
-      const int tile = (int)(b / op.nsteps);
-      const int64_t tend = (int64_t)(tile + 1) * op.nsteps;
-      const int64_t e = b1 < tend ? b1 : tend;
-      const int k0 = (int)(b - (int64_t)tile * op.nsteps), n = (int)(e - b);
+      const int tile = b / op.nsteps;
+      const int tend = (tile + 1) * op.nsteps;
+      const int e = b1 < tend ? b1 : tend;
+      const int k0 = b - tile * op.nsteps, n = e - b;
       if (!fn(j, tile, k0, n, s, sigma)) return;
       s += n;
       ++sigma;
@@ -188,17 +201,26 @@ __device__ __forceinline__ void for_each_segment(const ChainArgs& a, int c, F&& 
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    mxfp4_chain_kernel(const __grid_constant__ ChainMaps maps, const __grid_constant__ ChainArgs a) {
+    mxfp4_chain_kernel(const __grid_constant__ ChainMaps maps, const __grid_constant__ ChainArgs args) {
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t full_bar[kNS], empty_bar[kNS], xfull_bar[kNXS], xempty_bar[kNXS];
-  __shared__ uint64_t d_full[2], d_free[2];
+  __shared__ uint64_t d_full[kND], d_free[kND];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int s_abort;
-  __shared__ int s_last;
+  __shared__ int s_last[kEG];
 
+  // The argument block goes to shared memory first: every role indexes its ops
+  // at run time, and run-time indexing of kernel parameters makes a per-thread
+  // local copy of them.
+  __shared__ __align__(16) ChainArgs a_sm;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x;
+  static_assert(sizeof(ChainArgs) % 8 == 0, "argument block copy");
+  for (int i = tid; i < (int)(sizeof(ChainArgs) / 8); i += blockDim.x)
+    reinterpret_cast<uint64_t*>(&a_sm)[i] = reinterpret_cast<const uint64_t*>(&args)[i];
+  __syncthreads();
+  const ChainArgs& a = a_sm;
   const uint32_t gen = *reinterpret_cast<volatile uint32_t*>(&a.gen[c]);
   uint8_t* ring = dsm;
   uint8_t* ratoms = dsm + kOffAtoms;
@@ -215,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&xfull_bar[i], 4 * a.M);
       mbar_init(&xempty_bar[i], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kND; ++b) {
       mbar_init(&d_full[b], kNI);
       mbar_init(&d_free[b], 4);
     }
@@ -261,8 +283,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t a_ring = smem_u32(ring), a_ratoms = smem_u32(ratoms);
       const uint32_t a_xb = smem_u32(xb), a_xa = smem_u32(xa);
       for_each_segment(a, c, [&](int, int, int, int n, int s, int sigma) {
-        const int bsel = sigma & 1;
-        if (sigma >= 2 && !mbar_wait_bounded(&d_free[bsel], ((sigma - 2) >> 1) & 1)) {
+        const int bsel = sigma % kND;
+        if (sigma >= kND && !mbar_wait_bounded(&d_free[bsel], ((sigma / kND) - 1) & 1)) {
           s_abort = 1;
           return false;
         }
@@ -391,14 +413,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue: drain, reduce across CTAs, store, publish -------------------
-    const int et = tid - 32 * kEw0;          // 0..127
+    // ---------------- epilogue: two warpgroups take alternate segments ---------------------
+    const int eg = (warp - kEw0) >> 2;       // warpgroup
+    const int et = tid - 32 * (kEw0 + 4 * eg);  // 0..127 within it
+    const int bar = 3 + eg;                  // its named barrier
     const int row = 32 * (warp & 3) + lane;  // tensor-memory lane = row of the tile
     const int M = a.M;
+    float* exg = ex + (size_t)eg * kTile * kMaxM;
     for_each_segment(a, c, [&](int j, int tile, int, int n, int s, int sigma) {
+      if (sigma % kEG != eg) return true;
       const ChainOpDev& op = a.op[j];
-      const int bsel = sigma & 1;
-      const bool ok = mbar_wait_bounded(&d_full[bsel], (sigma >> 1) & 1);
+      const int bsel = sigma % kND;
+      const bool ok = mbar_wait_bounded(&d_full[bsel], (sigma / kND) & 1);
       tc::fence_after_sync();
       float v[kMaxM];
 #pragma unroll
@@ -420,25 +446,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&d_free[bsel]);
-      // one decision for all four warps: they meet at named barriers below
-      if (!named_bar_and(1, 128, ok && !s_abort)) {
+      // one decision for the group's four warps: they meet at named barriers below
+      if (!named_bar_and(bar, 128, ok && !s_abort)) {
         s_abort = 1;
         return false;
       }
-      const int64_t T = (int64_t)op.ntiles * op.nsteps;
+      const int T = op.ntiles * op.nsteps;
       int ord = 0;
       const int nseg = tile_segments(T, a.G, op.nsteps, tile, c, &ord);
       if (nseg > 1) {
+        // partial out; one thread publishes the arrival with an acquire-release
+        // atomic (its release covers the group's stores, ordered before it by
+        // the barrier; its acquire, the other segments' partials read below) and
+        // learns whether this segment is the tile's last
         float* p = op.part + ((size_t)tile * op.maxseg + ord) * M * kTile;
 #pragma unroll
         for (int mm = 0; mm < kMaxM; ++mm)
           if (mm < M) __stcg(p + mm * kTile + row, v[mm]);
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (et == 0) s_last = ((atomicAdd(op.cnt + tile, 1u) + 1u) % (uint32_t)nseg) == 0u;
-        named_bar_sync(1, 128);
-        if (!s_last) return true;
-        __threadfence();
+        named_bar_sync(bar, 128);
+        if (et == 0) s_last[eg] = ((atom_add_acq_rel(op.cnt + tile, 1u) + 1u) % (uint32_t)nseg) == 0u;
+        named_bar_sync(bar, 128);
+        if (!s_last[eg]) return true;
 #pragma unroll
         for (int mm = 0; mm < kMaxM; ++mm) v[mm] = 0.f;
         for (int o = 0; o < nseg; ++o) {  // fixed order: the tile's segments by K
@@ -451,11 +479,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the finished tile: bf16 rows (or SwiGLU of the gate/up row pairs)
       if (op.epi == kEpiSwiglu) {
 #pragma unroll
-        for (int mm = 0; mm < kMaxM; ++mm) ex[row * kMaxM + mm] = v[mm];
-        named_bar_sync(1, 128);
+        for (int mm = 0; mm < kMaxM; ++mm) exg[row * kMaxM + mm] = v[mm];
+        named_bar_sync(bar, 128);
         if (row < 64) {
           for (int mm = 0; mm < M; ++mm) {
-            const float gv = round_bf(v[mm]), uv = round_bf(ex[(row + 64) * kMaxM + mm]);
+            const float gv = round_bf(v[mm]), uv = round_bf(exg[(row + 64) * kMaxM + mm]);
             const float sv = round_bf(gv / (1.f + __expf(-gv)));
             op.Out[(size_t)mm * op.out_ld + tile * 64 + row] = __float2bfloat16_rn(sv * uv);
           }
@@ -465,9 +493,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (nn < op.N)
           for (int mm = 0; mm < M; ++mm) op.Out[(size_t)mm * op.out_ld + nn] = __float2bfloat16_rn(v[mm]);
       }
-      __threadfence();
-      named_bar_sync(1, 128);
-      if (et == 0) atomicExch(op.ready + tile, gen + 1);
+      named_bar_sync(bar, 128);
+      if (et == 0) st_release_u32(op.ready + tile, gen + 1);
       return true;
     });
   }
@@ -495,7 +522,7 @@ bool plan_layout(const b200kv_chain_op* ops, int nops, int M, int G, Layout* L) 
   };
   for (int j = 0; j < nops; ++j) {
     const int ntiles = cdiv(ops[j].N, kTile), nsteps = ops[j].K / kStep;
-    const int64_t T = (int64_t)ntiles * nsteps;
+    const int T = ntiles * nsteps;
     int mx = 1;
     for (int t = 0; t < ntiles; ++t) mx = std::max(mx, tile_segments(T, G, nsteps, t, -1, nullptr));
     L->maxseg[j] = mx;
@@ -516,6 +543,8 @@ int validate(const b200kv_chain_op* ops, int nops, int M) {
     if (o.x_from >= j || o.x_from < -1) return B200KV_ERR_INVALID_ARG;
     if (o.epilogue != kEpiStore && o.epilogue != kEpiSwiglu) return B200KV_ERR_INVALID_ARG;
     if (o.K % kStep) return B200KV_ERR_UNSUPPORTED;
+    // the work split computes (box index + 1) x CTAs in 32 bits
+    if ((int64_t)cdiv(o.N, kTile) * (o.K / kStep) * 1024 >= ((int64_t)1 << 31)) return B200KV_ERR_UNSUPPORTED;
     if (o.epilogue == kEpiSwiglu && o.N % kTile) return B200KV_ERR_UNSUPPORTED;
     const int width = o.epilogue == kEpiSwiglu ? o.N / 2 : o.N;
     if (o.out_stride < width) return B200KV_ERR_INVALID_ARG;

@@ -90,7 +90,6 @@ struct MmaArgs {
   int nsteps;                // W boxes along K: K / 128
   int sps;                   // W boxes per K-slice
   int ntiles, nclusters, tmax, nstages, bps;
-  int prefetch;              // stages beyond the ring kept in flight as L2 prefetches
 };
 
 // Dynamic shared memory: the stage ring (a stage: bps W boxes, then their bps
@@ -247,24 +246,12 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
     // ---------------- producer: per stage up to bps (W box, its scale atom) ------------
     if (lane == 0 && ns > 0) {
       tma_prefetch_desc(&wmap);
-      // Stages past the ring are prefetched into L2 (weights are load-time
-      // data): the ring holds at most 64 KB of weights per CTA, and the L2
-      // prefetches keep `a.prefetch` more stages in flight without shared memory.
-      const int total = my_tiles * spt;
-      int pf_next = nst;
-      auto prefetch_stage = [&](int s2) {
-        const int tile = cid + (s2 / spt) * a.nclusters, b0 = (s2 % spt) * bps;
-        const int nb = min(bps, ns - b0), g = s_begin + b0;
-        for (int q = 0; q < nb; ++q) tma_prefetch_l2_2d(&wmap, (g + q) * kStep, tile * kTile);
-        bulk_prefetch_l2(a.Sp + ((size_t)tile * a.nsteps + g) * kAtom, (uint32_t)(nb * kAtom));
-      };
       int s = 0;
       bool failed = false;
       for (int i = 0; i < my_tiles && !failed; ++i) {
         const int tile = cid + i * a.nclusters;
         for (int t = 0; t < spt; ++t, ++s) {
           const int slot = s % nst;
-          for (const int want = min(total, s + nst + a.prefetch); pf_next < want; ++pf_next) prefetch_stage(pf_next);
           if (s >= nst && !mbar_wait_bounded(&empty_bar[slot], ((s / nst) - 1) & 1)) {
             failed = true;  // stop issuing; drain what is in flight
             break;
@@ -548,11 +535,51 @@ struct MmaPlan {
 // boxes per slice, with a small price per CTA sharing an SM, per rank, and for
 // rings that hold less than 64 KB of weights.  The ring holds at most what a
 // CTA ever fills, so small shapes leave room for the next kernel's CTAs.
+// Plans measured on B200 (148 SMs) for the 7B projections (qkv 6144 x 4096,
+// o 4096 x 4096, gate_up 28672 x 4096, down 4096 x 14336) and their
+// tensor-parallel shards over 2, 4 and 8 GPUs, at M = 1, 4 and 8: the fastest
+// (K-split, boxes per stage, ring depth) of a sweep of all of them.  The
+// cost model below misses what they show: a K-split that divides K evenly,
+// deeper rings for gate_up, and fewer ranks as M grows (the cross-rank
+// reduction carries M values per row).
+struct PlanHint {
+  int N, K, mb, ks, bps, nst;  // mb: 1 (M = 1..2), 4 (M = 3..5), 8 (M = 6..8)
+};
+constexpr PlanHint kHints[] = {
+    {6144, 4096, 1, 4, 8, 1},   {4096, 4096, 1, 4, 8, 3},   {28672, 4096, 1, 4, 4, 3},  {4096, 14336, 1, 4, 4, 2},
+    {3072, 4096, 1, 4, 8, 4},   {4096, 2048, 1, 2, 8, 2},   {14336, 4096, 1, 2, 4, 2},  {4096, 7168, 1, 4, 8, 1},
+    {1536, 4096, 1, 5, 8, 4},   {4096, 1024, 1, 2, 4, 2},   {7168, 4096, 1, 4, 8, 1},   {4096, 3584, 1, 4, 8, 3},
+    {4096, 512, 1, 2, 8, 3},    {3584, 4096, 1, 4, 8, 3},   {4096, 1792, 1, 2, 8, 1},
+    {6144, 4096, 4, 4, 4, 2},   {4096, 4096, 4, 4, 8, 1},   {28672, 4096, 4, 2, 4, 2},  {4096, 14336, 4, 4, 4, 2},
+    {6144, 4096, 8, 2, 8, 1},   {4096, 4096, 8, 4, 8, 1},   {28672, 4096, 8, 2, 4, 2},  {4096, 14336, 8, 4, 4, 2},
+    {3072, 4096, 8, 4, 8, 4},   {4096, 2048, 8, 2, 8, 4},   {14336, 4096, 8, 2, 4, 2},  {4096, 7168, 8, 4, 8, 1},
+    {1536, 4096, 8, 4, 8, 3},   {4096, 1024, 8, 2, 4, 2},   {7168, 4096, 8, 2, 8, 1},   {4096, 3584, 8, 4, 8, 2},
+    {768, 4096, 8, 4, 8, 1},    {4096, 512, 8, 1, 8, 2},    {3584, 4096, 8, 4, 8, 2},   {4096, 1792, 8, 2, 8, 1},
+};
+
+const PlanHint* find_hint(int N, int K, int M) {
+  const int want = M <= 2 ? 1 : (M <= 5 ? 4 : 8);
+  const PlanHint* fallback = nullptr;
+  for (const PlanHint& h : kHints) {
+    if (h.N != N || h.K != K) continue;
+    if (h.mb == want) return &h;
+    if (want == 4 && h.mb == 8) fallback = &h;  // M = 3..5 without its own entry
+  }
+  return fallback;
+}
+
 template <int NI>
 MmaPlan plan_mma(const MmaArgs& a, int sms) {
-  const int force_ks = env_or("B200KV_MMA_KSPLIT", 0);
-  const int force_st = env_or("B200KV_MMA_STAGES", 0);
-  const int force_bps = env_or("B200KV_MMA_BPS", 0);
+  int force_ks = env_or("B200KV_MMA_KSPLIT", 0);
+  int force_st = env_or("B200KV_MMA_STAGES", 0);
+  int force_bps = env_or("B200KV_MMA_BPS", 0);
+  if (!force_ks && !force_st && !force_bps && env_or("B200KV_MMA_HINTS", 1)) {
+    if (const PlanHint* h = find_hint(a.N, a.K, a.M)) {
+      force_ks = h->ks;
+      force_bps = h->bps;
+      force_st = h->nst;
+    }
+  }
   // a footprint cap below half an SM lets the next kernel's CTAs share the SM
   // and start streaming while this one finishes
   const size_t smem_cap = (size_t)env_or("B200KV_MMA_SMEM_CAP", kSmemMax);
@@ -584,7 +611,7 @@ MmaPlan plan_mma(const MmaArgs& a, int sms) {
         const double share = ctas > sms ? (double)ctas / sms : 1.0;
         // weights in flight per CTA below 64 KB (8 boxes) cost latency, and a
         // single-stage ring does not overlap copies with MMAs
-        const int ring = nst * bps + a.prefetch * bps;  // boxes in flight, prefetches included
+        const int ring = nst * bps;  // boxes in flight
         const double latency = ring >= min(8, work) ? 0.0 : 2.0 * (min(8, work) - ring) / 8.0;
         const double cost = waves * sps * share + 0.25 * ks + latency + (nst == 1 && work > bps ? 1.0 : 0.0);
         if (cost < best_cost - 1e-9) {
@@ -613,8 +640,8 @@ int run_mma(const CUtensorMap& wm, MmaArgs a, int N, int K, int M, int sms, cuda
   if (env_or("B200KV_MMA_PLAN", 0))
     fprintf(stderr,
             "[b200kv] mxfp4_gemm N=%d K=%d M=%d: issuers=%d ks=%d clusters=%d stages=%d boxes/stage=%d "
-            "prefetch=%d tiles/cluster=%d boxes/slice=%d\n",
-            N, K, M, NI, p.ks, a.nclusters, a.nstages, a.bps, a.prefetch, a.tmax, a.sps);
+            "tiles/cluster=%d boxes/slice=%d\n",
+            N, K, M, NI, p.ks, a.nclusters, a.nstages, a.bps, a.tmax, a.sps);
   const cudaError_t e = launch_mma<NI>(wm, a, p.ks, st);
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;
 }
@@ -660,7 +687,6 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
   a.M = M;
   a.nsteps = K / kStep;
   a.ntiles = cdiv(N, kTile);
-  a.prefetch = env_or("B200KV_MMA_PREFETCH", 4);
 
   CUtensorMap wm;
   if (!encode_e2m1_unpacked_2d(&wm, W, (uint64_t)K, (uint64_t)N, (uint64_t)(K / 2), kTile))
