@@ -16,7 +16,8 @@
 //    T_j = tiles x K/128; the part of that range inside one 128-row tile is a
 //    segment (a contiguous K range of that tile);
 //  * warp 0 streams every box of the CTA's list, op after op, through a
-//    10-slot ring (TMA, unpacked e2m1 + the box's scale atom) -- weights are
+//    ring of 5 stages of 2 boxes (TMA, unpacked e2m1 + the boxes' scale atoms;
+//    one box per stage streams at ~3.7 TB/s on this part, two at ~5.3) -- weights are
 //    load-time data, so it never waits on a dependency and runs ahead across
 //    op boundaries as far as the ring allows;
 //  * four activation warps write, for each box, x's 128-element slice as two
@@ -73,7 +74,9 @@ constexpr int kAtom = mx::kAtom;
 constexpr int kNB = 16;               // B rows: term t of activation row m is row 8 t + m
 constexpr int kBBox = kNB * 128;
 constexpr int kMaxM = 8;
-constexpr int kNS = 10;               // weight ring slots (one box each)
+constexpr int kNS = 10;               // weight ring box slots
+constexpr int kSB = 2;                // boxes per ring stage (one mbarrier): DRAM streams 128 B of a row per request pair
+constexpr int kNST = kNS / kSB;       // ring stages
 constexpr int kNXS = 18;              // activation-term ring slots
 constexpr int kNI = 4;                // MMA-issuing warps
 constexpr int kXW = 4;                // activation-split warps
@@ -204,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mxfp4_chain_kernel(const __grid_constant__ ChainMaps maps, const __grid_constant__ ChainArgs args) {
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ uint64_t full_bar[kNS], empty_bar[kNS], xfull_bar[kNXS], xempty_bar[kNXS];
+  __shared__ uint64_t full_bar[kNST], empty_bar[kNST], xfull_bar[kNXS], xempty_bar[kNXS];
   __shared__ uint64_t d_full[kND], d_free[kND];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int s_abort;
@@ -229,9 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* ex = reinterpret_cast<float*>(dsm + kOffEx);
 
   if (tid == 0) {
-    for (int i = 0; i < kNS; ++i) {
+    for (int i = 0; i < kNST; ++i) {
       mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], 1);
+      mbar_init(&empty_bar[i], kSB);  // one commit per box
     }
     for (int i = 0; i < kNXS; ++i) {
       mbar_init(&xfull_bar[i], 4 * a.M);
@@ -255,26 +258,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- producer: every weight box of the CTA's list ----------------------
     if (lane == 0) {
       for (int j = 0; j < a.nops; ++j) tma_prefetch_desc(&maps.m[j]);
-      int issued = 0;
+      int total = 0;
+      for_each_segment(a, c, [&](int, int, int, int n, int s, int) {
+        total = s + n;
+        return true;
+      });
+      int issued = 0;  // stages
       for_each_segment(a, c, [&](int j, int tile, int k0, int n, int s, int) {
         const ChainOpDev& op = a.op[j];
         for (int q = 0; q < n; ++q) {
-          const int box = s + q, slot = box % kNS;
-          if (box >= kNS && !mbar_wait_bounded(&empty_bar[slot], ((box / kNS) - 1) & 1)) {
-            s_abort = 1;
-            return false;
+          const int box = s + q, sb = box / kSB, st = sb % kNST;
+          if (box % kSB == 0) {  // a new stage: its slot free, its bytes expected
+            if (sb >= kNST && !mbar_wait_bounded(&empty_bar[st], ((sb / kNST) - 1) & 1)) {
+              s_abort = 1;
+              return false;
+            }
+            if (s_abort) return false;
+            const int nb = total - box < kSB ? total - box : kSB;
+            mbar_arrive_expect_tx(&full_bar[st], (uint32_t)(nb * (kBoxTx + kAtom)));
+            issued = sb + 1;
           }
-          if (s_abort) return false;
-          mbar_arrive_expect_tx(&full_bar[slot], (uint32_t)(kBoxTx + kAtom));
-          tma_load_2d(ring + (size_t)slot * kBox, &maps.m[j], (k0 + q) * kStep, tile * kTile, &full_bar[slot]);
+          const int slot = box % kNS;
+          tma_load_2d(ring + (size_t)slot * kBox, &maps.m[j], (k0 + q) * kStep, tile * kTile, &full_bar[st]);
           bulk_g2s(ratoms + (size_t)slot * kAtom, op.Sp + ((size_t)tile * op.nsteps + k0 + q) * kAtom, kAtom,
-                   &full_bar[slot]);
-          issued = box + 1;
+                   &full_bar[st]);
         }
         return true;
       });
       // drain: every copy issued has landed before the CTA may exit
-      for (int t = issued > kNS ? issued - kNS : 0; t < issued; ++t) mbar_wait_bounded(&full_bar[t % kNS], (t / kNS) & 1);
+      for (int t = issued > kNST ? issued - kNST : 0; t < issued; ++t)
+        mbar_wait_bounded(&full_bar[t % kNST], (t / kNST) & 1);
     }
   } else if (warp <= kNI) {
     // ---------------- MMA issuers: issuer ii takes boxes s with s % 4 == ii ----------------
@@ -292,8 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool first = true;
         const uint32_t tD = tbase + (uint32_t)(bsel * kDStride + 16 * ii);
         for (int q = (ii - s % kNI + kNI) % kNI; q < n; q += kNI) {
-          const int box = s + q, slot = box % kNS, xs = box % kNXS;
-          if (!mbar_wait_bounded(&full_bar[slot], (box / kNS) & 1) ||
+          const int box = s + q, slot = box % kNS, xs = box % kNXS, sb = box / kSB;
+          if (!mbar_wait_bounded(&full_bar[sb % kNST], (sb / kNST) & 1) ||
               !mbar_wait_bounded(&xfull_bar[xs], (box / kNXS) & 1) || s_abort) {
             s_abort = 1;
             return false;
@@ -311,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                              tb | (sf << 30));
           }
           first = false;
-          tc::commit(&empty_bar[slot]);
+          tc::commit(&empty_bar[sb % kNST]);
           tc::commit(&xempty_bar[xs]);
         }
         tc::commit(&d_full[bsel]);
