@@ -484,30 +484,38 @@ DECODE_PROMPT, DECODE_TOKENS = 4096, 256
 
 
 def decode_7b_part(args, dev, barrier, allreduce, B):
-    """Config 4: the full 7B MXFP4 decoder (decoder.py) decoding DECODE_TOKENS
-    greedy tokens per sequence after a DECODE_PROMPT-token prompt, batch
-    B, one CUDA-graph replay per token.  The prompt's KV pages are
-    synthetic (random fp8 of the cache's scale), not computed: the decode cost
-    depends only on their length; the prefill kernel is timed as config 3.
-    Returns (ms per token step, tokens/s over the whole batch)."""
+    """Config 4: the full 7B MXFP4 decoder (decoder.py): a DECODE_PROMPT-token
+    random-id prompt per sequence through MXFP4Decoder.prefill (wide MXFP4
+    GEMMs, RoPE + fp8 KV write, varlen causal prefill attention; eager, timed:
+    the time to the first token), then greedy decode steps at batch B reading
+    the cache the prefill wrote, one CUDA-graph replay per token.  Returns
+    (ms per token step, tokens/s, ms of the prefill)."""
     import decoder
     cfg = decoder.SEVEN_B
     gather = None
+    big_allreduce = None
     if args.tp > 1:
         import torch.distributed as dist
 
         def gather(out, inp):
             dist.all_gather_into_tensor(out.view(-1), inp.contiguous().view(-1))
+
+        def big_allreduce(t):  # the prompt's [B x 4096, 4096] partials: NCCL
+            dist.all_reduce(t)
     dec = decoder.MXFP4Decoder(cfg, dev, B, DECODE_PROMPT + DECODE_TOKENS + 16, seed=7, tp=args.tp,
                                rank=args.rank, allreduce=allreduce, gather=gather)
-    g = torch.Generator(device=dev).manual_seed(11 + args.rank)
-    npb = DECODE_PROMPT // cfg.block_size
-    for kv in dec.kv:  # prompt pages of every sequence
-        for name in ("k", "v"):
-            pages = kv[name].view(B, dec.maxblk, *kv[name].shape[1:])[:, :npb]
-            pages.copy_((torch.randn(pages.shape, device=dev, generator=g) * 4).to(torch.float8_e4m3fn))
-    dec.positions.fill_(DECODE_PROMPT)
-    dec.tokens.copy_(torch.randint(0, cfg.vocab, (B,), device=dev, generator=g))
+    g = torch.Generator(device=dev).manual_seed(11)  # the same prompts on every rank
+    prompts = torch.randint(0, cfg.vocab, (B, DECODE_PROMPT), device=dev, generator=g)
+    dec.prefill(prompts[:, :64].contiguous(), allreduce=big_allreduce)  # warm-up (kernels, workspaces)
+    torch.cuda.synchronize()
+    if barrier:
+        barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    dec.prefill(prompts, allreduce=big_allreduce)
+    e1.record()
+    torch.cuda.synchronize()
+    ms_prefill = e0.elapsed_time(e1)
     dec.step()
     dec.step()
     graph = capture(dec.step)
@@ -515,7 +523,7 @@ def decode_7b_part(args, dev, barrier, allreduce, B):
     ms = time_graph(graph, steps, 1, barrier)
     del graph, dec
     torch.cuda.empty_cache()
-    return ms, B / (ms * 1e-3)
+    return ms, B / (ms * 1e-3), ms_prefill
 
 
 BATCH_SWEEP = (1, 4, 8)
@@ -857,10 +865,11 @@ def run_b200(args):
     us_pre = max_over_ranks(us_pre, dist_on, dev)
     us_wide, bytes_wide, flops_wide = wide_gemm_part(dev, args.steps, 2, barrier, args.tp)
     us_wide = max_over_ranks(us_wide, dist_on, dev)
-    dec7 = {}
+    dec7, pre7 = {}, {}
     for Bs in BATCH_SWEEP:
-        ms_b, _ = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None, Bs)
+        ms_b, _, ms_p = decode_7b_part(args, dev, barrier, args.allreduce_fn if args.tp > 1 else None, Bs)
         dec7[Bs] = max_over_ranks(ms_b, dist_on, dev)
+        pre7[Bs] = max_over_ranks(ms_p, dist_on, dev)
     ms_tok = dec7[args.batch] if args.batch in dec7 else None
     serve = None
     if args.serving == "on":
@@ -969,11 +978,15 @@ def run_b200(args):
                                            "terms at twice the bf16 rate, so bf16 peak is the bound)"},
                 "decode_7b": {"workload": f"config 4: full 7B MXFP4 decoder (RMSNorm, qkv, RoPE + fp8 "
                                           f"KV write, decode attention, o, SwiGLU MLP, bf16 lm_head "
-                                          f"128256, greedy argmax), batch 1/4/8, "
-                                          f"{DECODE_PROMPT}-token prompt (synthetic KV pages), "
-                                          f"tokens {DECODE_PROMPT}+; one CUDA-graph replay per token",
+                                          f"128256, greedy argmax), batch 1/4/8, a random-id "
+                                          f"{DECODE_PROMPT}-token prompt per sequence prefilled by the model "
+                                          f"(prefill_ms: wide MXFP4 GEMMs, RoPE + fp8 KV write, varlen causal "
+                                          f"prefill attention), then decode tokens {DECODE_PROMPT}+ reading "
+                                          f"that cache, one CUDA-graph replay per token",
                               "by_batch": {str(b): {"ms_per_token_step": dec7[b],
                                                     "tok_s": copies * b / (dec7[b] * 1e-3),
+                                                    "prefill_ms": pre7[b],
+                                                    "prefill_tok_s": copies * b * DECODE_PROMPT / (pre7[b] * 1e-3),
                                                     "cpu_baseline": cpu_dec.get(b)}
                                            for b in BATCH_SWEEP},
                               "ms_per_token_step": ms_tok,

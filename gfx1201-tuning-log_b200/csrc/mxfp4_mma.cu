@@ -569,17 +569,26 @@ const PlanHint* find_hint(int N, int K, int M) {
 }
 
 template <int NI>
+MmaPlan plan_mma_forced(const MmaArgs& a, int sms, int force_ks, int force_st, int force_bps);
+
+// The measured plan of the shape when there is one and it fits (more
+// activation rows need more shared memory), else the cost model's.
+template <int NI>
 MmaPlan plan_mma(const MmaArgs& a, int sms) {
-  int force_ks = env_or("B200KV_MMA_KSPLIT", 0);
-  int force_st = env_or("B200KV_MMA_STAGES", 0);
-  int force_bps = env_or("B200KV_MMA_BPS", 0);
+  const int force_ks = env_or("B200KV_MMA_KSPLIT", 0);
+  const int force_st = env_or("B200KV_MMA_STAGES", 0);
+  const int force_bps = env_or("B200KV_MMA_BPS", 0);
   if (!force_ks && !force_st && !force_bps && env_or("B200KV_MMA_HINTS", 1)) {
     if (const PlanHint* h = find_hint(a.N, a.K, a.M)) {
-      force_ks = h->ks;
-      force_bps = h->bps;
-      force_st = h->nst;
+      const MmaPlan p = plan_mma_forced<NI>(a, sms, h->ks, h->nst, h->bps);
+      if (p.ks) return p;
     }
   }
+  return plan_mma_forced<NI>(a, sms, force_ks, force_st, force_bps);
+}
+
+template <int NI>
+MmaPlan plan_mma_forced(const MmaArgs& a, int sms, int force_ks, int force_st, int force_bps) {
   // a footprint cap below half an SM lets the next kernel's CTAs share the SM
   // and start streaming while this one finishes
   const size_t smem_cap = (size_t)env_or("B200KV_MMA_SMEM_CAP", kSmemMax);

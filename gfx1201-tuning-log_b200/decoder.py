@@ -11,12 +11,16 @@ lm_head vocab-parallel with a (max, index) gather for the argmax.
 
 A decode step reads tokens, positions and the block tables from device
 tensors and advances them on the device, so it can be captured once in a CUDA
-graph and replayed token after token.
+graph and replayed token after token.  prefill() runs a prompt through the
+same layers with the wide MXFP4 GEMM, the fused RoPE + KV write and the varlen
+causal prefill kernel, so the decode loop continues from a cache the prefill
+wrote.
 """
 from dataclasses import dataclass
 
 import torch
 
+import fp8kv_prefill
 import fp8kv_v3
 import h4mv
 from _b200kv import KV_BF16, KV_FP8_E4M3, check, lib
@@ -101,12 +105,12 @@ def shard_layer(lay, cfg, rank, tp):
 
 def _linear(W, St, device, kernel="auto"):
     """Weights on the device with their scales in the layout of the faster
-    kernel: tensor-core atoms when K % 256 == 0 and no edge byte, else (or
+    kernel: tensor-core atoms when K % 128 == 0 and no edge byte, else (or
     with kernel="mma.sync") the transposed scales of the mma.sync kernel."""
     W = W.to(device).contiguous()
     St = St.to(device).contiguous()
     N, K = W.shape[0], W.shape[1] * 2
-    if K % 256 == 0 and kernel == "auto":
+    if K % 128 == 0 and kernel == "auto":
         packed, edge = h4mv.pack_scales(St, N, K)
         if not edge:
             return ("tc", W, packed)
@@ -115,9 +119,11 @@ def _linear(W, St, device, kernel="auto"):
 
 def _gemm(x, lin, out):
     kind, W, S = lin
-    if kind == "tc":
+    if kind == "tc":  # M > 8 goes to the wide-batch GEMM
         return h4mv.mxfp4_gemm(x, W, S, out=out)
-    return h4mv.mxfp4_gemv(x, W, S, out=out)
+    for m0 in range(0, x.shape[0], h4mv.MAX_M):  # the mma.sync matvec, 8 rows at a time
+        h4mv.mxfp4_gemv(x[m0:m0 + h4mv.MAX_M], W, S, out=out[m0:m0 + h4mv.MAX_M])
+    return out
 
 
 def _stream(t):
@@ -205,6 +211,80 @@ class MXFP4Decoder:
         check(lib.b200kv_swiglu(b["gu"].data_ptr(), b["act"].data_ptr(), self.B, self.cfg.inter // self.tp,
                                 _stream(b["gu"])), "b200kv_swiglu")
 
+    # ---- prompt ----------------------------------------------------------------
+    def prefill(self, prompts, allreduce=None):
+        """Run prompts (device int64 [B, P], every sequence P tokens, P <
+        max_ctx) through the model from position 0: per layer the qkv, o,
+        gate_up and down products at M = B * P (wide MXFP4 GEMM), RoPE + fp8 KV
+        write of every prompt token, and varlen causal prefill attention.
+        Writes this rank's logits of each sequence's last prompt token, sets
+        tokens to the greedy next token and positions to P, and returns the
+        tokens.  allreduce sums the row-parallel partials of all B * P rows
+        (default: the decode allreduce)."""
+        cfg, d, bs, B = self.cfg, self.cfg.head_dim, self.cfg.block_size, self.B
+        P = prompts.shape[1]
+        if prompts.shape[0] != B or P >= self.max_ctx:
+            raise ValueError(f"prompts must be [{B}, P] with P < {self.max_ctx}")
+        T, H, dev = B * P, cfg.hidden, self.dev
+        red = allreduce if allreduce is not None else self.allreduce
+        pos = torch.arange(P, dtype=torch.int32, device=dev).repeat(B)
+        seq = torch.arange(B, device=dev).repeat_interleave(P)
+        slots = self.block_table[seq, (pos // bs).long()].long() * bs + (pos % bs).long()
+        cu = torch.arange(0, T + 1, P, dtype=torch.int32, device=dev)
+        lens = torch.full((B,), P, dtype=torch.int32, device=dev)
+        z = lambda *s: torch.empty(*s, dtype=torch.bfloat16, device=dev)  # noqa: E731
+        h = torch.index_select(self.embed, 0, prompts.reshape(-1))
+        x, o, dn = z(T, H), z(T, H), z(T, H)
+        qkv = z(T, (self.hq + 2 * self.hkv) * d)
+        attn = z(T, self.hq, d)
+        gu, act = z(T, 2 * cfg.inter // self.tp), z(T, cfg.inter // self.tp)
+        st = _stream(h)
+
+        def norm(delta, w):
+            check(lib.b200kv_rmsnorm_residual(h.data_ptr(), delta.data_ptr() if delta is not None else None,
+                                              w.data_ptr(), x.data_ptr(), T, H, float(cfg.eps), st),
+                  "b200kv_rmsnorm_residual")
+        norm(None, self.layers[0]["in_norm"] if self.layers else self.final_norm)
+        for li, lay in enumerate(self.layers):
+            kv = self.kv[li]
+            k, v = kv["k"], kv["v"]
+            _gemm(x, lay["qkv"], qkv)
+            check(lib.b200kv_rope_kv_write(
+                qkv.data_ptr(), qkv.stride(0), pos.data_ptr(), self.rope.data_ptr(), self.max_ctx,
+                slots.data_ptr(), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+                v.stride(0), v.stride(1), v.stride(2), kv["ks"].data_ptr(), kv["vs"].data_ptr(), T, self.hq,
+                self.hkv, d, bs, KV_FP8_E4M3 if k.dtype == torch.float8_e4m3fn else KV_BF16, st),
+                "b200kv_rope_kv_write")
+            q = qkv[:, :self.hq * d].unflatten(1, (self.hq, d))
+            fp8kv_prefill.prefill_attention(q, k, v, attn, cu, lens, self.block_table, kv["ks"], kv["vs"],
+                                            d ** -0.5, max_qlen=P)
+            _gemm(attn.view(T, self.hq * d), lay["o"], o)
+            red(o)
+            norm(o, lay["post_norm"])
+            _gemm(x, lay["gate_up"], gu)
+            check(lib.b200kv_swiglu(gu.data_ptr(), act.data_ptr(), T, cfg.inter // self.tp, st), "b200kv_swiglu")
+            _gemm(act, lay["down"], dn)
+            red(dn)
+            norm(dn, self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm)
+        last = x.view(B, P, H)[:, P - 1].contiguous()
+        self.logits.copy_(torch.mm(last, self.lm_head.t(), out_dtype=torch.float32))
+        self.tokens.copy_(self._argmax())
+        self.positions.fill_(P)
+        return self.tokens
+
+    def _argmax(self):
+        """Greedy token per sequence from this rank's logits (vocab-parallel
+        under tensor parallelism: local (max, index), then a gather)."""
+        val, idx = self.logits.max(dim=1)
+        if self.tp > 1:
+            B, vl = self.B, self.cfg.vocab // self.tp
+            mine = torch.stack([val, (idx + self.rank * vl).float()], 1)  # exact below 2^24
+            allv = torch.empty(self.tp, B, 2, dtype=torch.float32, device=self.dev)
+            self.gather(allv, mine)
+            best = allv[:, :, 0].argmax(0)  # first maximum = lowest vocab index on ties
+            idx = allv[:, :, 1].gather(0, best.unsqueeze(0)).squeeze(0).long()
+        return idx
+
     # ---- one decode step --------------------------------------------------------
     def step(self):
         """Embed self.tokens at self.positions, run the layers, write this
@@ -235,14 +315,6 @@ class MXFP4Decoder:
             self._rmsnorm(b["dn"], nxt)
         # bf16 lm_head on cuBLAS (a plain library GEMM), fp32 logits
         self.logits.copy_(torch.mm(b["x"], self.lm_head.t(), out_dtype=torch.float32))
-        val, idx = self.logits.max(dim=1)
-        if self.tp > 1:
-            vl = self.cfg.vocab // self.tp
-            mine = torch.stack([val, (idx + self.rank * vl).float()], 1)  # exact below 2^24
-            allv = torch.empty(self.tp, B, 2, dtype=torch.float32, device=self.dev)
-            self.gather(allv, mine)
-            best = allv[:, :, 0].argmax(0)  # first maximum = lowest vocab index on ties
-            idx = allv[:, :, 1].gather(0, best.unsqueeze(0)).squeeze(0).long()
-        self.tokens.copy_(idx)
+        self.tokens.copy_(self._argmax())
         self.positions.add_(1)
         return self.tokens

@@ -10,14 +10,24 @@ With FP8KV_HIPW4=1 the CUDA implementation of the op radiance::mxfp4_linear
   * the checkpoint's scale layout [K/32, N] is repacked once and cached by
     (data_ptr, shape), never while a CUDA graph is being captured
     (fp8kv_hipw4.py:32-43): into tensor-core scale atoms for the block-scaled
-    tcgen05 kernels (h4mv.mxfp4_gemm) when K % 128 == 0 (K % 256 for the
-    M <= 8 kernel) and no scale byte is 0 or 255, else into [N, K/32] for the
-    CUDA-core kernel (h4mv.mxfp4_gemv);
+    tcgen05 kernels (h4mv.mxfp4_gemm) when K % 128 == 0 and no scale byte is
+    0 or 255, else into [N, K/32] for the CUDA-core kernel (h4mv.mxfp4_gemv);
+    prepack() does this at load time (the reference's "P2 load-time repack",
+    docs/06-w4gemm-hip-roadmap.md:54-55);
   * out = torch.empty(M, N, bf16) and one launch on the current stream;
   * everything else goes to the op's original CUDA body.
 
 FP8KV_HIPW4_MAX_M keeps the reference's default of 4; the B200 kernel itself
 handles M <= 8 (the reference capped at 4 because of a gfx1201 M=8 cliff).
+
+Stock vLLM 0.22 has no caller of radiance::mxfp4_linear (the reference's fork
+routed its MXFP4 linear method there); its Quark OCP-MX scheme runs W4A16
+MXFP4 layers in emulation, whose dequantization needs the amd-quark package.
+With FP8KV_HIPW4=1 install_quark_hook() therefore also hooks that scheme:
+process_weights_after_loading keeps the scales in the op's [K/32, N] layout
+and prepacks them, so a CUDA-graph capture of a freshly loaded model never
+reaches the lazy repack, and apply_weights sends bf16 activations of those
+layers through the op (other layers and dtypes keep the scheme's own path).
 
 The reference stole the body of the radiance fork's op once that module
 appeared (a 1500 x 0.2 s poll, fp8kv_hipw4.py:45-59).  The fork is not part
@@ -85,6 +95,67 @@ def packed_scales_for(s, N, K):
         _repack_cache.clear()
     _repack_cache[key] = (s, packed)
     return packed
+
+
+def prepack(weight, weight_scale):
+    """Load-time repack of one MXFP4 weight (weight uint8 [N, K/2], weight_scale
+    uint8 [K/32, N], the op's layout) into the caches the op reads: the
+    tensor-core scale atoms, or the [N, K/32] transpose for weights off the
+    tensor-core path.  Call outside CUDA-graph capture; returns True when the
+    tensor-core atoms were packed."""
+    N, K = weight.shape[0], weight.shape[1] * 2
+    packed = packed_scales_for(weight_scale, N, K) if weight.data_ptr() % 16 == 0 else False
+    if packed is False:
+        scale_t_for(weight_scale)
+    return packed is not None and packed is not False
+
+
+QUARK_MODULE = "vllm.model_executor.layers.quantization.quark.schemes.quark_ocp_mx"
+
+
+def _w4a16_mxfp4(scheme):
+    """vLLM's Quark OCP-MX scheme with MXFP4 weights and unquantized activations."""
+    return getattr(scheme, "weight_dtype", None) == "mxfp4" and getattr(scheme, "input_dtype", "") is None
+
+
+def install_quark_hook():
+    """Hook vLLM's QuarkOCP_MX for W4A16 MXFP4 layers (idempotent): the scales
+    are kept in the op's [K/32, N] layout and prepacked when the weights are
+    loaded, and bf16 activations go through radiance::mxfp4_linear.  Returns
+    False when vLLM's scheme cannot be imported."""
+    try:
+        import importlib
+        cls = importlib.import_module(QUARK_MODULE).QuarkOCP_MX
+    except Exception:
+        return False
+    if getattr(cls, "_b200kv_hooked", False):
+        return True
+    orig_process, orig_apply = cls.process_weights_after_loading, cls.apply_weights
+
+    def process_weights_after_loading(self, layer):
+        orig_process(self, layer)
+        if _w4a16_mxfp4(self) and layer.weight.is_cuda and layer.weight.dtype == __import__("torch").uint8:
+            ws = layer.weight_scale.data
+            K = layer.weight.shape[1] * 2
+            ckpt = ws if ws.shape[0] == K // 32 else ws.t().contiguous()  # -> [K/32, N]
+            layer._b200kv_scale_ckpt = ckpt
+            prepack(layer.weight.data, ckpt)
+
+    def apply_weights(self, layer, x, bias=None):
+        import torch
+        ckpt = getattr(layer, "_b200kv_scale_ckpt", None)
+        if ckpt is not None and x.is_cuda and x.dtype == torch.bfloat16:
+            w = layer.weight
+            y = torch.ops.radiance.mxfp4_linear(x.reshape(-1, x.shape[-1]).contiguous(), w, ckpt, w)
+            y = y.reshape(*x.shape[:-1], w.shape[0])
+            return y + bias if bias is not None else y
+        return orig_apply(self, layer, x, bias)
+
+    cls.process_weights_after_loading = process_weights_after_loading
+    cls.apply_weights = apply_weights
+    cls._b200kv_hooked = True
+    sys.stderr.write("[hipw4] quark W4A16 MXFP4 hook installed\n")
+    return True
 
 
 def eligible(x, weight, weight_scale, m_limit):
@@ -161,10 +232,8 @@ def make_patched(body, m_limit):
             if eligible(x, weight, weight_scale, m_limit):
                 N, K = weight.shape[0], weight.shape[1] * 2
                 packed = packed_scales_for(weight_scale, N, K) if weight.data_ptr() % 16 == 0 else False
-                if packed is not None and packed is not False and (K % 256 == 0 or x.shape[0] > h4mv.MAX_M):
+                if packed is not None and packed is not False:
                     out = h4mv.mxfp4_gemm(x, weight, packed)
-                elif packed is not None and packed is not False:
-                    out = h4mv.mxfp4_gemv(x, weight, scale_t_for(weight_scale))
                 else:
                     st = scale_t_for(weight_scale) if packed is False else None
                     out = h4mv.mxfp4_gemv(x, weight, st) if st is not None else None
@@ -216,6 +285,7 @@ def _install():
         else:
             _override(mxfp4_linear_chunked)
             sys.stderr.write("[hipw4] installed\n")
+        install_quark_hook()
         return True
 
     def _poll():

@@ -110,11 +110,8 @@ def test_rope_kv_write(cuda):
     assert int(vcg.view(4 * bs, -1)[~written].count_nonzero()) == 0
 
 
-@pytest.mark.parametrize("batch,kernel", [(1, "auto"), (2, "auto"), (2, "mma.sync")])
-def test_decoder_steps_match_oracle(cuda, batch, kernel):
+def _steps_match_oracle(cfg, cuda, batch, kernel, seed, max_ctx, steps):
     import decoder
-    cfg = _cfg()
-    seed, max_ctx, steps = 5, 64, 6
     dec = decoder.MXFP4Decoder(cfg, cuda, batch, max_ctx, seed=seed, gen_device="cpu",
                                mxfp4_kernel=kernel)
     # the oracle's copy of the same weights (checkpoint scale layout [K/32, N])
@@ -150,6 +147,23 @@ def test_decoder_steps_match_oracle(cuda, batch, kernel):
     assert _b200kv.device_status() == 0
 
 
+@pytest.mark.parametrize("batch,kernel", [(1, "auto"), (2, "auto"), (2, "mma.sync")])
+def test_decoder_steps_match_oracle(cuda, batch, kernel):
+    _steps_match_oracle(_cfg(), cuda, batch, kernel, seed=5, max_ctx=64, steps=6)
+
+
+def test_decoder_7b_width_steps_match_oracle(cuda):
+    """The 7B geometry config 4 times (hidden 4096, 32 q / 8 kv heads,
+    intermediate 14336, vocab 128256, RoPE theta 1e6) with 2 of its 32 layers,
+    batch 2, four decode steps: logits within 2e-2 of their maximum and greedy
+    tokens equal where the oracle's top two are separated."""
+    import dataclasses
+
+    import decoder
+    cfg = dataclasses.replace(decoder.SEVEN_B, layers=2)
+    _steps_match_oracle(cfg, cuda, 2, "auto", seed=6, max_ctx=64, steps=4)
+
+
 def test_decoder_step_in_cuda_graph(cuda):
     """Replaying a captured step continues the sequence exactly as eager steps."""
     import decoder
@@ -175,3 +189,57 @@ def test_decoder_step_in_cuda_graph(cuda):
         toks_b.append(b.tokens.clone())
     for x, y in zip(toks_a, toks_b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("batch,P", [(1, 40), (3, 33)])
+def test_decoder_prefill_then_decode_matches_oracle(cuda, batch, P):
+    """prefill() (wide MXFP4 GEMMs at M = batch * P, RoPE + fp8 KV write of the
+    prompt, varlen causal prefill attention) against the oracle stepping the
+    prompt token by token: the last prompt token's logits within 2e-2 of their
+    maximum, greedy tokens equal where separated; then three decode steps that
+    read the cache the prefill wrote, same bounds.
+
+    The weights use e8m0 scales 2^-10..2^-7. With the default 2^-8..2^-2 this
+    random 2-layer model turns the last-ulp differences between the prefill
+    and decode attention kernels (different key-block splits of the same
+    softmax) into fp8 KV codes that differ in layer 1 and logits 5% apart,
+    the GPU prefill against the GPU decode path alone; with the narrower
+    scales the two GPU paths agree to 1e-3."""
+    import decoder
+    cfg = _cfg()
+    seed, max_ctx = 8, 64
+    scales = (117, 121)
+    dec = decoder.MXFP4Decoder(cfg, cuda, batch, max_ctx, seed=seed, gen_device="cpu", scales=scales)
+    layers = []
+    for li in range(cfg.layers):
+        lay = decoder.random_layer(cfg, li, seed, "cpu", scales)
+        layers.append({k: ((v[0], v[1].t().contiguous()) if isinstance(v, tuple) else v) for k, v in lay.items()})
+    weights = dict(decoder.random_head(cfg, seed, "cpu"), layers=layers)
+    nb = batch * dec.maxblk
+    caches = [{"k": torch.zeros(nb, cfg.block_size, cfg.kv_heads, cfg.head_dim, dtype=torch.float8_e4m3fn),
+               "v": torch.zeros(nb, cfg.block_size, cfg.kv_heads, cfg.head_dim, dtype=torch.float8_e4m3fn),
+               "ks": 1 / 8, "vs": 1 / 8} for _ in range(cfg.layers)]
+    table = DO.rope_table(max_ctx, cfg.head_dim, cfg.rope_theta)
+    bt = dec.block_table.cpu()
+    prompts = torch.randint(0, cfg.vocab, (batch, P), generator=torch.Generator().manual_seed(P))
+    for i in range(P):
+        want = DO.decode_step(cfg, weights, caches, prompts[:, i], torch.full((batch,), i, dtype=torch.int32), bt,
+                              table)
+    nxt = dec.prefill(prompts.to(cuda)).cpu()
+    positions = torch.full((batch,), P, dtype=torch.int32)
+    for step in range(4):
+        got = dec.logits.cpu()
+        err = (got - want).abs().max() / want.abs().max()
+        assert float(err) < 2e-2, (step, float(err))
+        top2 = want.topk(2, dim=1).values
+        sep = (top2[:, 0] - top2[:, 1]) > 4 * float((got - want).abs().max())
+        assert torch.equal(nxt[sep], want.argmax(1)[sep]), step
+        if step == 3:
+            break
+        tokens = nxt.clone()
+        want = DO.decode_step(cfg, weights, caches, tokens, positions, bt, table)
+        nxt = dec.step().cpu()
+        positions = positions + 1
+    torch.cuda.synchronize()
+    import _b200kv
+    assert _b200kv.device_status() == 0

@@ -147,3 +147,40 @@ def test_radiance_op_routes_to_b200_matvec(cuda, monkeypatch):
             assert hw._state["fast"] == fast0 + 1
         else:
             assert hw._state["slow"] == slow0 + 1
+
+
+def test_quark_w4a16_layer_prepacked_at_load_and_graph_capturable(cuda, monkeypatch):
+    """vLLM's Quark OCP-MX scheme on a W4A16 MXFP4 layer as the engine loads it
+    (weight [N, K/2], scales [N, K/32]): process_weights_after_loading (hooked)
+    packs the scale atoms, so a CUDA-graph capture of apply_weights needs no
+    lazy repack; results within the reference's tolerance of the oracle for
+    M = 1, 4 and a 3-D batch of 12 tokens, bias added."""
+    monkeypatch.setenv("FP8KV_HIPW4", "1")
+    import fp8kv_hipw4 as hw
+    assert hw._install() and hw.install_quark_hook()
+    from vllm.model_executor.layers.quantization.quark.schemes.quark_ocp_mx import QuarkOCP_MX
+    scheme = QuarkOCP_MX({"dtype": "fp4", "qscheme": "per_group", "group_size": 32}, None)
+    N, K = 1024, 2048
+    W, S, St, _ = MO.make_case(N, K, 1, seed=3)
+    layer = torch.nn.Module()
+    layer.weight = torch.nn.Parameter(W.to(cuda), requires_grad=False)
+    layer.weight_scale = torch.nn.Parameter(St.to(cuda), requires_grad=False)
+    scheme.process_weights_after_loading(layer)
+    ckpt = layer._b200kv_scale_ckpt
+    assert tuple(ckpt.shape) == (K // 32, N)
+    assert ("p", ckpt.data_ptr(), tuple(ckpt.shape), ckpt.device) in hw._repack_cache
+    bias = torch.randn(N, device=cuda).to(torch.bfloat16)
+    for shape in ((1, K), (4, K), (3, 4, K)):
+        x = torch.randn(*shape).to(torch.bfloat16).to(cuda)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                y = scheme.apply_weights(layer, x, bias)
+        torch.cuda.current_stream().wait_stream(s)
+        graph.replay()
+        torch.cuda.synchronize()
+        assert tuple(y.shape) == shape[:-1] + (N,)
+        ref = MO.mxfp4_linear_reference(W, S, x.reshape(-1, K).cpu()) + bias.float().cpu()
+        assert MO.rel_to_max_err(y.reshape(-1, N).float().cpu(), ref) < 5e-3, shape

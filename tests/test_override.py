@@ -358,3 +358,24 @@ def test_wide_workspace_is_never_freed_when_outgrown(libpath, monkeypatch):
     c = h4mv.wide_workspace(100, 256, _Dev(), _Stream())
     assert b.numel() > a.numel() and c is b
     assert any(t is a for t in h4mv._outgrown)
+
+
+def test_hipw4_hooks_vllm_quark_w4a16_scheme():
+    """With FP8KV_HIPW4=1 the module also hooks vLLM's Quark OCP-MX scheme
+    (W4A16 MXFP4 layers: load-time prepack, apply through the op); the hook is
+    idempotent and leaves CPU layers to the scheme's own path."""
+    env = dict(os.environ, FP8KV_HIPW4="1", FP8KV_OVERRIDE="0", PYTHONPATH=PKG)
+    code = ("import torch, fp8kv_hipw4 as hw; "
+            "from vllm.model_executor.layers.quantization.quark.schemes.quark_ocp_mx import QuarkOCP_MX as Q; "
+            "assert Q._b200kv_hooked and hw.install_quark_hook(); "
+            "s = Q({'dtype': 'fp4', 'qscheme': 'per_group', 'group_size': 32}, None); "
+            "assert hw._w4a16_mxfp4(s); "
+            "l = torch.nn.Module(); "
+            "l.weight = torch.nn.Parameter(torch.zeros(64, 128, dtype=torch.uint8), requires_grad=False); "
+            "l.weight_scale = torch.nn.Parameter(torch.zeros(64, 8, dtype=torch.uint8), requires_grad=False); "
+            "s.process_weights_after_loading(l); "
+            "print('CKPT', hasattr(l, '_b200kv_scale_ckpt'))")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "CKPT False" in r.stdout
+    assert "[hipw4] quark W4A16 MXFP4 hook installed" in r.stderr
