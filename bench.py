@@ -411,7 +411,7 @@ def serving_part(args, dev, barrier, layers=32, steps=2):
     qkv = torch.empty(T, (hq + 2 * hkv) * D, dtype=torch.bfloat16, device=dev)
     attn = torch.empty(T, hq, D, dtype=torch.bfloat16, device=dev)
     o = torch.empty(T, 4096, dtype=torch.bfloat16, device=dev)
-    gu = torch.empty(T, 2 * inter, dtype=torch.bfloat16, device=dev)
+    act = torch.empty(T, inter, dtype=torch.bfloat16, device=dev)
     dn = torch.empty(T, 4096, dtype=torch.bfloat16, device=dev)
     q = qkv[:, :hq * D].view(T, hq, D)
     kn = qkv[:, hq * D:(hq + hkv) * D].view(T, hkv, D)
@@ -448,8 +448,8 @@ def serving_part(args, dev, barrier, layers=32, steps=2):
                 h4mv.mxfp4_gemm_wide(attn.view(T, hq * D), *L["o"], out=o)
                 if allreduce:
                     allreduce(o)
-                h4mv.mxfp4_gemm_wide(o, *L["gate_up"], out=gu)
-                h4mv.mxfp4_gemm_wide(gu[:, :inter], *L["down"], out=dn)  # stand-in for SwiGLU(gu)
+                h4mv.mxfp4_gemm_swiglu(o, *L["gate_up"], out=act)  # gate_up with the SwiGLU epilogue
+                h4mv.mxfp4_gemm_wide(act, *L["down"], out=dn)
                 if allreduce:
                     allreduce(dn)
 
@@ -1037,8 +1037,8 @@ def run_b200(args):
                         "rows to the decode kernel, prefills to the varlen kernel, split on the device); "
                         "split = the same two kernels as two calls on host-known row ranges; one_call = "
                         "the varlen kernel for the whole batch; "
-                        "attention_ms includes the KV write; the down GEMM reads half of gate_up's output "
-                        "in place of SwiGLU (same bytes and FLOPs); per rank under tensor parallelism"}
+                        "attention_ms includes the KV write; gate_up runs with the SwiGLU epilogue "
+                        "(b200kv_mxfp4_gemm_wide_swiglu); per rank under tensor parallelism"}
         if ms_comm is not None:
             result["parts"]["allreduce"] = {
                 "us_per_step": ms_comm * 1e3, "calls_per_step": 2 * args.layers,

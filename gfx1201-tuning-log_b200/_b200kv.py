@@ -114,6 +114,11 @@ lib.b200kv_mxfp4_gemm_wide_workspace_bytes.restype = ctypes.c_size_t
 lib.b200kv_mxfp4_gemm_wide_workspace_bytes.argtypes = [_i32, _i32]
 lib.b200kv_mxfp4_gemm_wide.restype = _i32
 lib.b200kv_mxfp4_gemm_wide.argtypes = [_vp, _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp, _i32, _i32, _i32, _vp]
+lib.b200kv_mxfp4_gemm_swiglu.restype = _i32
+lib.b200kv_mxfp4_gemm_swiglu.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]
+lib.b200kv_mxfp4_gemm_wide_swiglu.restype = _i32
+lib.b200kv_mxfp4_gemm_wide_swiglu.argtypes = [_vp, _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp, _i32, _i32, _i32,
+                                              _vp]
 lib.b200kv_mxfp4_gemm_wide_noalloc.restype = _i32
 lib.b200kv_mxfp4_gemm_wide_noalloc.argtypes = [_vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _vp]
 

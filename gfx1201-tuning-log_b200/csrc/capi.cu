@@ -91,12 +91,12 @@ size_t mxfp4_packed_scales_bytes(int N, int K);
 int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, int* edge_flag,
                              void* stream);
 int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
-                     void* stream);
+                     int epilogue, void* stream);
 size_t mxfp4_gemm_wide_workspace_bytes(int M, int K);
 size_t mxfp4_chain_workspace_bytes(const b200kv_chain_op* ops, int nops, int M);
 int mxfp4_chain_launch(const b200kv_chain_op* ops, int nops, int M, void* ws, size_t ws_bytes, void* stream);
 int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* ws,
-                           size_t ws_bytes, void* Out, int N, int K, int M, void* stream);
+                           size_t ws_bytes, void* Out, int N, int K, int M, int epilogue, void* stream);
 int mxfp4_gemm_wide_noalloc_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* Out, int N,
                                    int K, int M, void* stream);
 
@@ -237,7 +237,12 @@ int b200kv_mxfp4_pack_scales(const void* scales, int layout, void* packed, int N
 
 int b200kv_mxfp4_gemm(const void* W, const void* packed_scales, const void* X, void* out, int N,
                       int K, int M, void* stream) {
-  return b200kv::mxfp4_mma_launch(W, packed_scales, X, out, N, K, M, stream);
+  return b200kv::mxfp4_mma_launch(W, packed_scales, X, out, N, K, M, 0, stream);
+}
+
+int b200kv_mxfp4_gemm_swiglu(const void* W, const void* packed_scales, const void* X, void* act, int N, int K,
+                             int M, void* stream) {
+  return b200kv::mxfp4_mma_launch(W, packed_scales, X, act, N, K, M, 1, stream);
 }
 
 size_t b200kv_mxfp4_gemm_wide_workspace_bytes(int M, int K) {
@@ -248,7 +253,14 @@ int b200kv_mxfp4_gemm_wide(const void* W, const void* packed_scales, const void*
                            void* workspace, size_t workspace_bytes, void* out, int N, int K, int M,
                            void* stream) {
   return b200kv::mxfp4_gemm_wide_launch(W, packed_scales, X, x_stride, workspace, workspace_bytes, out, N,
-                                        K, M, stream);
+                                        K, M, 0, stream);
+}
+
+int b200kv_mxfp4_gemm_wide_swiglu(const void* W, const void* packed_scales, const void* X, int64_t x_stride,
+                                  void* workspace, size_t workspace_bytes, void* act, int N, int K, int M,
+                                  void* stream) {
+  return b200kv::mxfp4_gemm_wide_launch(W, packed_scales, X, x_stride, workspace, workspace_bytes, act, N,
+                                        K, M, 1, stream);
 }
 
 int b200kv_mxfp4_gemm_wide_noalloc(const void* W, const void* packed_scales, const void* X, int64_t x_stride,

@@ -155,7 +155,10 @@ struct GemmArgs {
   int ttiles;          // ceil(M / 64)
   int vec_out;         // Out 16-byte aligned and N % 8 == 0: 16-byte output stores
   int n256;            // NT = 2: both token tiles in one N = 256 MMA (B200KV_GEMM_N256=0: two of 128)
+  int swiglu;          // Out [M, N / 2] = SwiGLU of row-interleaved gate_up weights (K unsplit, vec_out)
 };
+
+__device__ __forceinline__ float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // Dynamic shared memory: the stage ring, then (ks > 1) the receive area of the
 // K-slice reduction, recv[src rank][band row][tokens] in fp32, whose 16-byte
@@ -400,7 +403,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     tc::fence_before_sync();
-    if (ksz == 1 && a.vec_out) {
+    if (ksz == 1 && a.vec_out && a.swiglu) {
+      // weight tile w holds gate rows 64 w .. 64 w + 63, then the same up rows:
+      // 8 gate and the 8 matching up values of a token give one 16-byte chunk
+      // of act[m, 64 w + c] = bf16(bf16(silu(g)) * u), g and u the bf16 products
+      named_bar_sync(1, 128);
+      const uint4* tile = reinterpret_cast<const uint4*>(dsm);
+      constexpr int kCh = MT * kRows / 8;  // 16-byte chunks per token row of the tile
+      constexpr int kChS = kCh / 2;        // output chunks per token row
+      const int half = a.N / 2;
+      for (int idx = et; idx < kT * kChS; idx += 128) {
+        const int tok = idx / kChS, c = idx % kChS;
+        const int mt = c / 8, j = c % 8;
+        const int m = tt0 * kTok + tok, wt = wt0 + mt;
+        if (m < a.M && wt * kRows < a.N) {  // N % 128 == 0: a weight tile lies wholly inside or outside
+          const uint4 g4 = tile[(size_t)tok * kCh + mt * 16 + j], u4 = tile[(size_t)tok * kCh + mt * 16 + 8 + j];
+          const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(&g4);
+          const __nv_bfloat16* u = reinterpret_cast<const __nv_bfloat16*>(&u4);
+          uint4 o4;
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&o4);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float gv = __bfloat162float(g[e]);
+            const float sv = round_bf(gv / (1.f + __expf(-gv)));
+            o[e] = __float2bfloat16_rn(sv * __bfloat162float(u[e]));
+          }
+          *reinterpret_cast<uint4*>(a.Out + (size_t)m * half + (size_t)wt * 64 + 8 * j) = o4;
+        }
+      }
+    } else if (ksz == 1 && a.vec_out) {
       // the tile's token rows are contiguous runs of output: coalesced 16-byte stores
       named_bar_sync(1, 128);
       const uint4* tile = reinterpret_cast<const uint4*>(dsm);
@@ -597,12 +628,14 @@ size_t mxfp4_gemm_wide_workspace_bytes(int M, int K) {
 }
 
 int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t x_ld, void* ws,
-                           size_t ws_bytes, void* Out, int N, int K, int M, void* stream) {
+                           size_t ws_bytes, void* Out, int N, int K, int M, int epilogue, void* stream) {
   if (!W || !Sp || !X || !Out) return B200KV_ERR_INVALID_ARG;
   if (N <= 0 || K <= 0 || M <= 0 || x_ld < K) return B200KV_ERR_INVALID_ARG;
-  if (K % kKStep) return B200KV_ERR_UNSUPPORTED;
+  if (epilogue != 0 && epilogue != 1) return B200KV_ERR_INVALID_ARG;
+  if (K % kKStep || (epilogue == 1 && N % kRows)) return B200KV_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(Sp) & 15) ||
-      (reinterpret_cast<uintptr_t>(X) & 15) || (x_ld & 7) || (reinterpret_cast<uintptr_t>(ws) & 127))
+      (reinterpret_cast<uintptr_t>(X) & 15) || (x_ld & 7) || (reinterpret_cast<uintptr_t>(ws) & 127) ||
+      (epilogue == 1 && (reinterpret_cast<uintptr_t>(Out) & 15)))
     return B200KV_ERR_MISALIGNED;
   const size_t need = mxfp4_gemm_wide_workspace_bytes(M, K);
   if (!ws || ws_bytes < need) return B200KV_ERR_WORKSPACE;
@@ -623,10 +656,13 @@ int mxfp4_gemm_wide_launch(const void* W, const void* Sp, const void* X, int64_t
   a.Out = static_cast<__nv_bfloat16*>(Out);
   a.n256 = env_int("B200KV_GEMM_N256", 1) != 0;
   a.vec_out = (reinterpret_cast<uintptr_t>(Out) & 15) == 0 && N % 8 == 0;
+  a.swiglu = epilogue;
 
-  // plan: tile shape (MT weight tiles x NT token tiles), K-split, ring depth
+  // plan: tile shape (MT weight tiles x NT token tiles), K-split, ring depth;
+  // the SwiGLU epilogue pairs rows of one CTA tile, so it takes K unsplit
   const int force_mt = env_int("B200KV_GEMM_MT", 0), force_nt = env_int("B200KV_GEMM_NT", 0);
-  const int force_ks = env_int("B200KV_GEMM_KSPLIT", 0), force_st = env_int("B200KV_GEMM_STAGES", 0);
+  const int force_ks = epilogue == 1 ? 1 : env_int("B200KV_GEMM_KSPLIT", 0);
+  const int force_st = env_int("B200KV_GEMM_STAGES", 0);
   const int force_kb = env_int("B200KV_GEMM_KB", 0);
   Plan p;
   double cost = 1e30;
@@ -731,7 +767,7 @@ int mxfp4_gemm_wide_noalloc_launch(const void* W, const void* Sp, const void* X,
     ptr = g_scratch_ptr[dev];
   }
   // the pre-pass rewrites every byte the GEMM reads: nothing needs clearing
-  return mxfp4_gemm_wide_launch(W, Sp, X, x_ld, ptr, kNoAllocBytes, Out, N, K, M, stream);
+  return mxfp4_gemm_wide_launch(W, Sp, X, x_ld, ptr, kNoAllocBytes, Out, N, K, M, 0, stream);
 }
 
 }  // namespace b200kv

@@ -90,7 +90,17 @@ struct MmaArgs {
   int nsteps;                // W boxes along K: K / 128
   int sps;                   // W boxes per K-slice
   int ntiles, nclusters, tmax, nstages, bps;
+  int epilogue;              // kEpiStore: out[M, N]; kEpiSwiglu: out[M, N / 2] (see below)
 };
+
+// Epilogues.  kEpiSwiglu takes gate_up weights whose 128-row tiles hold 64
+// gate rows and then the 64 matching up rows (tile i: gate rows 64 i .. 64 i + 63,
+// then the same up rows) and writes act[m, 64 i + r] = bf16(bf16(silu(g)) * u)
+// with g, u the bf16-rounded products, HF Llama's act_fn(gate) * up with the
+// rounding of b200kv_swiglu.
+constexpr int kEpiStore = 0, kEpiSwiglu = 1;
+
+__device__ __forceinline__ float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // Dynamic shared memory: the stage ring (a stage: bps W boxes, then their bps
 // scale atoms), x's terms (B operand, one 2 KB box per W box of the slice) and
@@ -400,14 +410,38 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
     }
 
     // finish the owned tiles: fixed-order sum over the ranks' partials
-    if (owned > 0 && (recv_bytes == 0 || mbar_wait_bounded(&recv_bar, 0))) {
-      for (int t = 0; t < owned; ++t) {
-        const int n = (cid + (rank + t * ksz) * a.nclusters) * kTile + row;
-        const float* rs = recv + ((size_t)t * ksz * kTile + row) * a.M;
-        for (int m = 0; m < a.M; ++m) {
-          float acc = 0.f;
-          for (int q = 0; q < ksz; ++q) acc += rs[(size_t)q * kTile * a.M + m];
-          if (n < a.N) a.Out[(size_t)m * a.N + n] = __float2bfloat16_rn(acc);
+    if (owned > 0) {
+      bool ok = recv_bytes == 0 || mbar_wait_bounded(&recv_bar, 0);
+      if (a.epilogue == kEpiStore) {
+        for (int t = 0; ok && t < owned; ++t) {
+          const int n = (cid + (rank + t * ksz) * a.nclusters) * kTile + row;
+          const float* rs = recv + ((size_t)t * ksz * kTile + row) * a.M;
+          for (int m = 0; m < a.M; ++m) {
+            float acc = 0.f;
+            for (int q = 0; q < ksz; ++q) acc += rs[(size_t)q * kTile * a.M + m];
+            if (n < a.N) a.Out[(size_t)m * a.N + n] = __float2bfloat16_rn(acc);
+          }
+        }
+      } else {
+        // the up row of gate row r is row r + 64 of the same tile, whose local
+        // partial another warp wrote: one barrier of the four epilogue warps,
+        // which also makes the decision to store uniform
+        ok = named_bar_and(1, 128, ok);
+        const int half = a.N / 2;
+        for (int t = 0; ok && row < 64 && t < owned; ++t) {
+          const int tile = cid + (rank + t * ksz) * a.nclusters;
+          const float* rg = recv + ((size_t)t * ksz * kTile + row) * a.M;
+          const float* ru = rg + (size_t)64 * a.M;
+          for (int m = 0; m < a.M; ++m) {
+            float g = 0.f, u = 0.f;
+            for (int q = 0; q < ksz; ++q) {
+              g += rg[(size_t)q * kTile * a.M + m];
+              u += ru[(size_t)q * kTile * a.M + m];
+            }
+            const float gv = round_bf(g), uv = round_bf(u);
+            const float sv = round_bf(gv / (1.f + __expf(-gv)));
+            a.Out[(size_t)m * half + tile * 64 + row] = __float2bfloat16_rn(sv * uv);
+          }
         }
       }
     }
@@ -677,9 +711,11 @@ int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, 
 }
 
 int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
-                     void* stream) {
+                     int epilogue, void* stream) {
   if (!W || !Sp || !X || !Out) return B200KV_ERR_INVALID_ARG;
   if (N <= 0 || K <= 0 || M <= 0) return B200KV_ERR_INVALID_ARG;
+  if (epilogue != kEpiStore && epilogue != kEpiSwiglu) return B200KV_ERR_INVALID_ARG;
+  if (epilogue == kEpiSwiglu && N % kTile) return B200KV_ERR_UNSUPPORTED;
   if (M > kMaxM || K % kStep) return B200KV_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(Sp) & 15) ||
       (reinterpret_cast<uintptr_t>(X) & 15))
@@ -696,6 +732,7 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
   a.M = M;
   a.nsteps = K / kStep;
   a.ntiles = cdiv(N, kTile);
+  a.epilogue = epilogue;
 
   CUtensorMap wm;
   if (!encode_e2m1_unpacked_2d(&wm, W, (uint64_t)K, (uint64_t)N, (uint64_t)(K / 2), kTile))

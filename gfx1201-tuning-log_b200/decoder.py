@@ -117,6 +117,29 @@ def _linear(W, St, device, kernel="auto"):
     return ("mv", W, St)
 
 
+def _gate_up_linear(W, St, inter, device, kernel="auto", fuse=True):
+    """gate_up ([gate | up] rows, `inter` each) prepared for the GEMM with the
+    SwiGLU epilogue when the tensor-core kernels take it: rows (and their
+    scales) permuted once to h4mv.gate_up_row_order, kind "tcsw".  Otherwise
+    the plain layout, and the SwiGLU runs as its own kernel."""
+    if fuse and kernel == "auto" and inter % 64 == 0 and W.shape[0] == 2 * inter:
+        order = h4mv.gate_up_row_order(inter, W.device)
+        lin = _linear(W.index_select(0, order), St.index_select(0, order), device, kernel)
+        if lin[0] == "tc":
+            return ("tcsw",) + lin[1:]
+    return _linear(W, St, device, kernel)
+
+
+def _gate_up(x, lin, gu, act, inter, stream):
+    """act = SwiGLU(x @ gate_up^T): one launch on "tcsw" weights, else the
+    product into gu and the SwiGLU kernel."""
+    if lin[0] == "tcsw":
+        return h4mv.mxfp4_gemm_swiglu(x, lin[1], lin[2], out=act)
+    _gemm(x, lin, gu)
+    check(lib.b200kv_swiglu(gu.data_ptr(), act.data_ptr(), x.shape[0], inter, stream), "b200kv_swiglu")
+    return act
+
+
 def _gemm(x, lin, out):
     kind, W, S = lin
     if kind == "tc":  # M > 8 goes to the wide-batch GEMM
@@ -136,11 +159,13 @@ class MXFP4Decoder:
     tp/rank/allreduce: this rank's part of a tensor-parallel group (allreduce
     sums a bf16 tensor in place over the group, e.g. tp.PeerAllreduce;
     gather(out, inp) all-gathers a float32 tensor, for the argmax).  Weights are
-    drawn on `gen_device` (CPU in tests, so the oracle sees the same numbers)."""
+    drawn on `gen_device` (CPU in tests, so the oracle sees the same numbers).
+    fuse_swiglu: gate_up runs with the SwiGLU epilogue (rows permuted at load
+    time) wherever the tensor-core kernels take the weights."""
 
     def __init__(self, cfg, device, batch, max_ctx, seed=0, tp=1, rank=0, allreduce=None,
                  gather=None, kv_scale=1.0 / 8, gen_device=None, layers=None, mxfp4_kernel="auto",
-                 scales=CONFIG2_SCALES):
+                 scales=CONFIG2_SCALES, fuse_swiglu=True):
         self.cfg, self.dev, self.B, self.tp, self.rank = cfg, device, batch, tp, rank
         self.allreduce = allreduce if allreduce is not None else (lambda t: t)
         self.gather = gather
@@ -154,8 +179,9 @@ class MXFP4Decoder:
         for li in range(nlayers):
             sh = shard_layer(random_layer(cfg, li, seed, gdev, scales), cfg, rank, tp)
             lin = lambda name: _linear(*sh[name], device, mxfp4_kernel)  # noqa: E731
+            gate_up = _gate_up_linear(*sh["gate_up"], cfg.inter // tp, device, mxfp4_kernel, fuse_swiglu)
             self.layers.append({
-                "qkv": lin("qkv"), "o": lin("o"), "gate_up": lin("gate_up"), "down": lin("down"),
+                "qkv": lin("qkv"), "o": lin("o"), "gate_up": gate_up, "down": lin("down"),
                 "in_norm": sh["in_norm"].to(device), "post_norm": sh["post_norm"].to(device)})
         head = random_head(cfg, seed, gdev)
         vl = cfg.vocab // tp
@@ -205,11 +231,6 @@ class MXFP4Decoder:
             kv["ks"].data_ptr(), kv["vs"].data_ptr(), self.B, self.hq, self.hkv, self.cfg.head_dim,
             self.cfg.block_size, KV_FP8_E4M3 if k.dtype == torch.float8_e4m3fn else KV_BF16,
             _stream(b["qkv"])), "b200kv_rope_kv_write")
-
-    def _swiglu(self):
-        b = self.buf
-        check(lib.b200kv_swiglu(b["gu"].data_ptr(), b["act"].data_ptr(), self.B, self.cfg.inter // self.tp,
-                                _stream(b["gu"])), "b200kv_swiglu")
 
     # ---- prompt ----------------------------------------------------------------
     def prefill(self, prompts, allreduce=None):
@@ -261,8 +282,7 @@ class MXFP4Decoder:
             _gemm(attn.view(T, self.hq * d), lay["o"], o)
             red(o)
             norm(o, lay["post_norm"])
-            _gemm(x, lay["gate_up"], gu)
-            check(lib.b200kv_swiglu(gu.data_ptr(), act.data_ptr(), T, cfg.inter // self.tp, st), "b200kv_swiglu")
+            _gate_up(x, lay["gate_up"], gu, act, cfg.inter // self.tp, st)
             _gemm(act, lay["down"], dn)
             red(dn)
             norm(dn, self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm)
@@ -307,8 +327,7 @@ class MXFP4Decoder:
             _gemm(b["attn"].view(B, self.hq * d), lay["o"], b["o"])
             self.allreduce(b["o"])
             self._rmsnorm(b["o"], lay["post_norm"])
-            _gemm(b["x"], lay["gate_up"], b["gu"])
-            self._swiglu()
+            _gate_up(b["x"], lay["gate_up"], b["gu"], b["act"], cfg.inter // self.tp, _stream(b["x"]))
             _gemm(b["act"], lay["down"], b["dn"])
             self.allreduce(b["dn"])
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm

@@ -1,6 +1,8 @@
 """fp8 paged-KV split-K decode attention -- drop-in for the reference module
-vllm-fp8kv/fp8kv_v3.py (`run` at :116-139), backed by the sm_100a kernel in
-csrc/decode_attn.cu instead of the two Triton kernels.
+vllm-fp8kv/fp8kv_v3.py (`run` at :116-139), backed by sm_100a kernels instead
+of the two Triton kernels: csrc/decode_tma.cu (TMA page tiles) for fp8 caches,
+csrc/decode_attn.cu (per-row gathers) for bf16 caches and for fp8 layouts that
+no tensor map describes.
 
 Same signature and argument meaning.  Differences a caller can observe:
   * TILE / warps / stages are accepted and ignored (they tuned the Triton

@@ -77,7 +77,7 @@ def pack_scales(scales, N, K, layout=SCALES_TRANSPOSED):
 
 def mxfp4_gemm(x, weight, packed_scales, out=None):
     """out[M, N] = x[M, K] @ dequant(weight, scales)^T on block-scaled tcgen05
-    MMAs with scales packed by pack_scales(): 1 <= M <= 8 (K % 256 == 0) on the
+    MMAs with scales packed by pack_scales(): 1 <= M <= 8 (K % 128 == 0) on the
     skinny kernel, larger M on mxfp4_gemm_wide (K % 128 == 0)."""
     if x.dtype != torch.bfloat16 or x.dim() != 2 or not x.is_contiguous():
         raise ValueError("x must be a contiguous 2-D bfloat16 tensor")
@@ -148,12 +148,45 @@ def mxfp4_gemm_wide(x, weight, packed_scales, out=None, workspace=None):
     return out
 
 
-# ---- chains of dependent matvecs in one persistent launch ----------------------------
+def mxfp4_gemm_swiglu(x, weight, packed_scales, out=None, workspace=None):
+    """act[M, I] = bf16(bf16(silu(g)) * u) of the gate_up projection, the
+    activation applied in the GEMM's epilogue: `weight` is the [2 I, K/2] gate
+    and up rows in gate_up_row_order(I) (scales packed after the permutation).
+    Bit for bit mxfp4_gemm on the unpermuted weight followed by the SwiGLU
+    kernel.  1 <= M <= 8 on the skinny kernel, larger M on the wide GEMM."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be a 2-D bfloat16 tensor with unit inner stride")
+    if weight.dtype != torch.uint8 or not weight.is_contiguous():
+        raise TypeError("weight must be a contiguous uint8 tensor")
+    M, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] * 2 != K:
+        raise ValueError(f"shape mismatch x={tuple(x.shape)} w={tuple(weight.shape)}")
+    if N % 128:
+        raise ValueError(f"SwiGLU epilogue needs 2 I % 128 == 0 (N={N})")
+    if out is None:
+        out = torch.empty((M, N // 2), device=x.device, dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream(x.device)
+    if M <= MAX_M and x.is_contiguous():
+        check(lib.b200kv_mxfp4_gemm_swiglu(weight.data_ptr(), packed_scales.data_ptr(), x.data_ptr(),
+                                           out.data_ptr(), N, K, M, stream.cuda_stream),
+              "b200kv_mxfp4_gemm_swiglu")
+        return out
+    if workspace is None:
+        workspace = wide_workspace(M, K, x.device, stream)
+    check(lib.b200kv_mxfp4_gemm_wide_swiglu(weight.data_ptr(), packed_scales.data_ptr(), x.data_ptr(),
+                                            x.stride(0), workspace.data_ptr(), workspace.numel(),
+                                            out.data_ptr(), N, K, M, stream.cuda_stream),
+          "b200kv_mxfp4_gemm_wide_swiglu")
+    return out
+
+
 def gate_up_row_order(inter, device=None):
     """Row order of a fused [gate; up] weight ([2 inter, K], gate rows first) for
-    the chain's SwiGLU epilogue: blocks of 64 gate rows followed by the matching
-    64 up rows.  Apply once at load time to the weight's rows (and to its scales
-    before packing); inter % 64 == 0."""
+    the SwiGLU epilogues (mxfp4_gemm_swiglu, the chain's CHAIN_SWIGLU): blocks
+    of 64 gate rows followed by the matching 64 up rows.  Apply once at load
+    time to the weight's rows (and to its scales before packing);
+    inter % 64 == 0."""
     if inter % 64:
         raise ValueError(f"SwiGLU interleave needs inter % 64 == 0 (inter={inter})")
     t = torch.arange(inter // 64, device=device)
@@ -162,6 +195,7 @@ def gate_up_row_order(inter, device=None):
     return torch.stack([gate, gate + inter], dim=1).reshape(-1)
 
 
+# ---- chains of dependent matvecs in one persistent launch ----------------------------
 class MXFP4Chain:
     """A fixed list of dependent MXFP4 matvecs (1 <= M <= 8) run by one
     persistent launch (b200kv_mxfp4_chain).  Each op is a dict with

@@ -143,11 +143,12 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
 /* ---- MXFP4 on block-scaled tensor cores (load-time packed scales) -------------
  *
  * The same product as b200kv_mxfp4_gemv, computed by tcgen05
- * kind::mxf4.block_scale MMAs: the packed e2m1 weights go to the tensor core
- * straight from memory and the MMA applies the e8m0 scales itself.  The scales
- * must first be packed once per weight (a load-time repack, as the reference
- * transposes its scales once, h4mv/fp8kv_hipw4.py:32-43) into 512-byte atoms,
- * one per (128 rows x 4 groups).  No counterpart call in the reference.
+ * kind::mxf8f6f4.block_scale MMAs: the packed e2m1 weights go to the tensor
+ * core straight from memory (unpacked to one code per byte by the TMA) and the
+ * MMA applies the e8m0 scales itself.  The scales must first be packed once per
+ * weight (a load-time repack, as the reference transposes its scales once,
+ * h4mv/fp8kv_hipw4.py:32-43) into 512-byte atoms, one per (128 rows x 4
+ * groups).  No counterpart call in the reference.
  *
  *   b200kv_mxfp4_packed_scales_bytes  size of the packed buffer (0 if K % 128).
  *   b200kv_mxfp4_pack_scales  scales: layout 0 = St [N, K/32] (transposed, as
@@ -155,16 +156,33 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
  *       *edge_flag (device int, set to 1, never cleared) reports scale bytes 0
  *       or 255, whose meaning differs between the MMA (2^-127, NaN) and the
  *       reference kernel (0.0, inf): such weights belong on b200kv_mxfp4_gemv.
- *   b200kv_mxfp4_gemm  out[M, N] bf16 for 1 <= M <= 8, K % 256 == 0, W 16-byte
- *       aligned.  x enters as four e2m1 terms with per-32 block scales (about
- *       95 % of bf16 values exact, the rest within 5e-4 of their block
- *       maximum); fp32 accumulation.
+ *   b200kv_mxfp4_gemm  out[M, N] bf16 for 1 <= M <= 8, K % 128 == 0, W 16-byte
+ *       aligned.  x enters as two e4m3 terms with per-32 block scales, split
+ *       inside the kernel (every bf16 element within 2^-13 of its block
+ *       maximum is exact, smaller ones within 2^-21 of it); fp32 accumulation.
  */
 size_t b200kv_mxfp4_packed_scales_bytes(int N, int K);
 int b200kv_mxfp4_pack_scales(const void* scales, int layout, void* packed, int N, int K,
                              int* edge_flag, void* stream);
 int b200kv_mxfp4_gemm(const void* W, const void* packed_scales, const void* X, void* out, int N,
                       int K, int M, void* stream);
+
+/* The gate_up projection with the MLP activation as its epilogue (the
+ * reference's engine fuses the same SiLU * mul into its linear).  W holds the
+ * 2 I gate and up rows interleaved in 64-row groups: its 128-row tile w is gate
+ * rows 64 w .. 64 w + 63 followed by the same up rows (a load-time row
+ * permutation; pack the scales after permuting).  act[M, I] =
+ * bf16(bf16(silu(g)) * u), g and u the bf16-rounded products: bit for bit the
+ * plain GEMM followed by b200kv_swiglu on the unpermuted weights, when the
+ * plain GEMM splits K the same way (the order of the fp32 sum).  N = 2 I,
+ * N % 128 == 0.  b200kv_mxfp4_gemm_swiglu: 1 <= M <= 8, as b200kv_mxfp4_gemm,
+ * with the same plan; b200kv_mxfp4_gemm_wide_swiglu: any M, as
+ * b200kv_mxfp4_gemm_wide with K unsplit across CTAs; act 16-byte aligned. */
+int b200kv_mxfp4_gemm_swiglu(const void* W, const void* packed_scales, const void* X, void* act, int N,
+                             int K, int M, void* stream);
+int b200kv_mxfp4_gemm_wide_swiglu(const void* W, const void* packed_scales, const void* X, int64_t x_stride,
+                                  void* workspace, size_t workspace_bytes, void* act, int N, int K, int M,
+                                  void* stream);
 
 /* Wide batches (prefill chunks, batched decode; any M >= 1, meant for M > 8):
  * the same product on tcgen05 kind::mxf8f6f4.block_scale MMAs, weights as e2m1

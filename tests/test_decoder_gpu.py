@@ -243,3 +243,24 @@ def test_decoder_prefill_then_decode_matches_oracle(cuda, batch, P):
     torch.cuda.synchronize()
     import _b200kv
     assert _b200kv.device_status() == 0
+
+
+def test_decoder_swiglu_epilogue_bit_equal_to_separate_kernel(cuda, monkeypatch):
+    """gate_up with the SwiGLU epilogue (rows permuted at load time) against
+    the same model with gate_up and the SwiGLU kernel as two launches: equal
+    logits bit for bit through a prompt pass and decode steps (the prompt
+    pass's wide GEMMs at K-split 1, the split the wide epilogue takes)."""
+    import decoder
+    monkeypatch.setenv("B200KV_GEMM_KSPLIT", "1")
+    cfg = _cfg()
+    a = decoder.MXFP4Decoder(cfg, cuda, 2, 64, seed=7, gen_device="cpu")
+    b = decoder.MXFP4Decoder(cfg, cuda, 2, 64, seed=7, gen_device="cpu", fuse_swiglu=False)
+    assert a.layers[0]["gate_up"][0] == "tcsw" and b.layers[0]["gate_up"][0] == "tc"
+    prompts = torch.randint(0, cfg.vocab, (2, 20), generator=torch.Generator().manual_seed(1)).to(cuda)
+    a.prefill(prompts)
+    b.prefill(prompts)
+    assert torch.equal(a.logits, b.logits)
+    for _ in range(3):
+        a.step()
+        b.step()
+        assert torch.equal(a.logits, b.logits)
