@@ -49,6 +49,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// SiLU of a bf16 value g, rounded to bf16: the activation of HF Llama's
+// act_fn(gate) * up as the decoder rounds it (every SwiGLU in this library
+// uses it, so fused and separate paths agree bit for bit).  g / (1 + e^-g)
+// with the fast division: within 2 ulp of the fp32 quotient before the bf16
+// rounding, and 0 for g < -87 (where 1 + e^-g passes 2^126 and SiLU(g) is
+// below 1e-36 in magnitude).  An IEEE division here made the SwiGLU epilogue
+// of the wide GEMM five times as long.
+__device__ __forceinline__ float silu_bf16(float g) {
+  return __bfloat162float(__float2bfloat16_rn(__fdividef(g, 1.f + __expf(-g))));
+}
+
 // Named barrier over `count` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

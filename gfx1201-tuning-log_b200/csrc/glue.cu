@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const float gv = bf(g, e);
-      const float s = round_bf(gv / (1.f + __expf(-gv)));
+      const float s = silu_bf16(gv);
       o[e] = s * bf(u, e);
     }
     reinterpret_cast<uint32_t*>(act + (size_t)r * inter)[i] = pack_bf2(o[0], o[1]);

@@ -497,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row < 64) {
           for (int mm = 0; mm < M; ++mm) {
             const float gv = round_bf(v[mm]), uv = round_bf(exg[(row + 64) * kMaxM + mm]);
-            const float sv = round_bf(gv / (1.f + __expf(-gv)));
+            const float sv = silu_bf16(gv);
             op.Out[(size_t)mm * op.out_ld + tile * 64 + row] = __float2bfloat16_rn(sv * uv);
           }
         }

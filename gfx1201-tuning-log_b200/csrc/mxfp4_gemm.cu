@@ -158,7 +158,6 @@ struct GemmArgs {
   int swiglu;          // Out [M, N / 2] = SwiGLU of row-interleaved gate_up weights (K unsplit, vec_out)
 };
 
-__device__ __forceinline__ float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // Dynamic shared memory: the stage ring, then (ks > 1) the receive area of the
 // K-slice reduction, recv[src rank][band row][tokens] in fp32, whose 16-byte
@@ -425,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float gv = __bfloat162float(g[e]);
-            const float sv = round_bf(gv / (1.f + __expf(-gv)));
+            const float sv = silu_bf16(gv);
             o[e] = __float2bfloat16_rn(sv * __bfloat162float(u[e]));
           }
           *reinterpret_cast<uint4*>(a.Out + (size_t)m * half + (size_t)wt * 64 + 8 * j) = o4;

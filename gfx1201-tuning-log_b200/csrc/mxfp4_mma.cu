@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
               u += ru[(size_t)q * kTile * a.M + m];
             }
             const float gv = round_bf(g), uv = round_bf(u);
-            const float sv = round_bf(gv / (1.f + __expf(-gv)));
+            const float sv = silu_bf16(gv);
             a.Out[(size_t)m * half + tile * 64 + row] = __float2bfloat16_rn(sv * uv);
           }
         }
