@@ -75,7 +75,9 @@ def workload_config(args):
                              "terms), scales packed at load" if args.gemv == "tc" else "CUDA-core mma.sync"),
             "l2": "inputs larger than L2 (distinct weights/KV per layer), no flush",
             "parallelism": (f"tp{args.tp}: attention by kv head, qkv/gate_up column-parallel, "
-                            f"o/down row-parallel + {args.allreduce} allreduce (in the CUDA graph)"
+                            + ("o/down row-parallel with the allreduce in their epilogue (peer memory)"
+                               if args.allreduce == "fused" else
+                               f"o/down row-parallel + {args.allreduce} allreduce (in the CUDA graph)")
                             if args.tp > 1 else f"replicas x{args.gpus}")}
 
 
@@ -215,6 +217,16 @@ def run_step(layers, bufs, args, which=("gemv", "attn", "comm")):
     sm = D ** -0.5
     gemv = h4mv.mxfp4_gemm if args.gemv == "tc" else h4mv.mxfp4_gemv
     do_g, do_a, do_c = "gemv" in which, "attn" in which, "comm" in which and args.tp > 1
+    # o and down with the allreduce in their epilogue: the GEMV part carries it
+    fused = args.tp > 1 and args.allreduce == "fused"
+    if fused:
+        do_c = False
+
+    def row_parallel(x, lin, out):
+        if fused:
+            args.allreduce_fn.gemm(x, *lin, out=out)
+        else:
+            gemv(x, *lin, out=out)
     for lay in layers:
         if do_g:
             gemv(lay["x"], *lay["qkv"], out=bufs["qkv"])
@@ -223,12 +235,12 @@ def run_step(layers, bufs, args, which=("gemv", "attn", "comm")):
             fp8kv_v3.run(q, lay["k"], lay["v"], bufs["attn"], bufs["qsl"], bufs["slens"], lay["bt"],
                          lay["ks"], lay["vs"], sm, max_seq_len=args.ctx)
         if do_g:
-            gemv(bufs["attn"].view(B, hq * D), *lay["o"], out=bufs["o"])
+            row_parallel(bufs["attn"].view(B, hq * D), lay["o"], bufs["o"])
         if do_c:
             args.allreduce_fn(bufs["o"])
         if do_g:
             gemv(bufs["o"], *lay["gate_up"], out=bufs["gate_up"])
-            gemv(lay["act"], *lay["down"], out=bufs["down"])
+            row_parallel(lay["act"], lay["down"], bufs["down"])
         if do_c:
             args.allreduce_fn(bufs["down"])
 
@@ -503,7 +515,8 @@ def decode_7b_part(args, dev, barrier, allreduce, B):
         def big_allreduce(t):  # the prompt's [B x 4096, 4096] partials: NCCL
             dist.all_reduce(t)
     dec = decoder.MXFP4Decoder(cfg, dev, B, DECODE_PROMPT + DECODE_TOKENS + 16, seed=7, tp=args.tp,
-                               rank=args.rank, allreduce=allreduce, gather=gather)
+                               rank=args.rank, allreduce=allreduce, gather=gather,
+                               fuse_allreduce=args.allreduce == "fused")
     g = torch.Generator(device=dev).manual_seed(11)  # the same prompts on every rank
     prompts = torch.randint(0, cfg.vocab, (B, DECODE_PROMPT), device=dev, generator=g)
     dec.prefill(prompts[:, :64].contiguous(), allreduce=big_allreduce)  # warm-up (kernels, workspaces)
@@ -799,7 +812,7 @@ def run_b200(args):
     comm = None
     if args.tp > 1:
         import tp
-        if args.allreduce == "peer":
+        if args.allreduce in ("peer", "fused"):
             comm = tp.PeerAllreduce()
             args.allreduce_fn = comm
         else:
@@ -812,7 +825,8 @@ def run_b200(args):
     g_step = capture(lambda: run_step(layers, bufs, args))
     g_gemv = capture(lambda: run_step(layers, bufs, args, which=("gemv",)))
     g_attn = capture(lambda: run_step(layers, bufs, args, which=("attn",)))
-    g_comm = capture(lambda: run_step(layers, bufs, args, which=("comm",))) if args.tp > 1 else None
+    g_comm = (capture(lambda: run_step(layers, bufs, args, which=("comm",)))
+              if args.tp > 1 and args.allreduce != "fused" else None)
 
     # ---- timed region: whole steps (graph replay), clocks sampled meanwhile --
     clocks = ClockSampler(local)
@@ -1073,8 +1087,9 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--parallel", choices=("tp", "replicas"), default="tp",
                     help="N > 1: tensor parallelism over the N GPUs (default) or N full replicas")
-    ap.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
-                    help="tensor-parallel allreduce: b200kv's peer-memory kernel or NCCL")
+    ap.add_argument("--allreduce", choices=("fused", "peer", "nccl"), default="fused",
+                    help="tensor-parallel allreduce: in the o/down GEMV's epilogue over peer memory "
+                         "(default), b200kv's one-shot peer-memory kernel after it, or NCCL")
     ap.add_argument("--serving", choices=("on", "off"), default="on",
                     help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1)")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",

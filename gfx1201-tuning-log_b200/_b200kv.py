@@ -119,6 +119,8 @@ lib.b200kv_mxfp4_gemm_swiglu.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _
 lib.b200kv_mxfp4_gemm_wide_swiglu.restype = _i32
 lib.b200kv_mxfp4_gemm_wide_swiglu.argtypes = [_vp, _vp, _vp, _i64, _vp, ctypes.c_size_t, _vp, _i32, _i32, _i32,
                                               _vp]
+lib.b200kv_mxfp4_gemm_allreduce.restype = _i32
+lib.b200kv_mxfp4_gemm_allreduce.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32, _i32, _vp]
 lib.b200kv_mxfp4_gemm_wide_noalloc.restype = _i32
 lib.b200kv_mxfp4_gemm_wide_noalloc.argtypes = [_vp, _vp, _vp, _i64, _vp, _i32, _i32, _i32, _vp]
 

@@ -3,24 +3,10 @@
 // row-parallel o and down projections of the tensor-parallel 7B step (one
 // [M, 4096] partial per rank, M <= 8).
 //
-// Every rank owns a communication buffer (cudaMalloc, shared with the peers
-// through CUDA IPC handles):
-//   [0, 256)       call counters, one per CTA (read and advanced only by it)
-//   [256, ...)     lines[2][8][kMaxElems / 2] of 8 bytes: {4 data bytes, flag}
-// The vector is split into chunks of kLinesPerCta lines, one CTA each (the
-// grid depends only on n, so every call of a size uses the same chunks and
-// counters).  Call k of a chunk (its counter value k, parity p = k & 1) on
-// rank r: the CTA writes its chunk into lines[p][r] of every rank, two bf16
-// and the flag k + 1 per
-// 8-byte store (one NVLink transaction, so a reader that sees the flag sees the
-// data: no fence and no separate flag round trip -- the "low-latency" line
-// format), then polls its own lines[p][*] until every flag reads k + 1
-// (bounded by %globaltimer) and writes the sum over ranks in rank order (fp32,
-// then bf16): every rank produces identical bytes.
-// Reusing parity p at call k + 2 is safe: rank r starts call k + 2 only after
-// its call k + 1 saw every peer's lines of call k + 1, which each peer wrote
-// after it had finished reading its lines of call k.  No multicast objects, no
-// NCCL.
+// The buffer layout and the line protocol are in peer_comm.cuh; here the
+// vector is split into chunks of kLinesPerCta lines, one CTA each (the grid
+// depends only on n, so every call of a size uses the same chunks and
+// counters).  No multicast objects, no NCCL.
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -29,36 +15,23 @@
 
 #include "b200kv.h"
 #include "b200kv_common.cuh"
+#include "peer_comm.cuh"
 
 namespace b200kv {
 namespace {
 
-constexpr int kMaxRanks = 8;
-constexpr int kMaxElems = 8 * 4096;     // bf16 elements per partial
+constexpr int kMaxRanks = kCommMaxRanks;
+constexpr int kMaxElems = kCommMaxElems;
 constexpr int kArThreads = 256;
 constexpr int kLinesPerCta = 256;        // one line per thread
 constexpr int kMaxCtas = kMaxElems / 2 / kLinesPerCta;
-constexpr size_t kCtrlBytes = 256;
-constexpr size_t kLines = kMaxElems / 2;  // 8-byte lines per rank slot
-constexpr size_t kBufBytes = kCtrlBytes + (size_t)2 * kMaxRanks * kLines * 8;
-static_assert(kMaxCtas * 4 <= (int)kCtrlBytes, "one counter per CTA in the control block");
-constexpr unsigned long long kTimeoutNs = 200ull * 1000 * 1000;  // 200 ms
+constexpr size_t kBufBytes = kCommBufBytes;
+static_assert(kMaxCtas <= kCommCounters, "one counter per CTA in the control block");
+constexpr unsigned long long kTimeoutNs = kCommTimeoutNs;
 
-struct PeerBufs {
-  uint8_t* p[kMaxRanks];
-};
-
-__device__ __forceinline__ uint2* lines(uint8_t* buf, int parity, int r) {
-  return reinterpret_cast<uint2*>(buf + kCtrlBytes) + ((size_t)parity * kMaxRanks + r) * kLines;
-}
-__device__ __forceinline__ void st_line(uint2* p, uint32_t data, uint32_t flag) {
-  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(flag) : "memory");
-}
-__device__ __forceinline__ uint2 ld_line(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-  return v;
-}
+__device__ __forceinline__ uint2* lines(uint8_t* buf, int parity, int r) { return comm_lines(buf, parity, r); }
+__device__ __forceinline__ void st_line(uint2* p, uint32_t data, uint32_t flag) { comm_st_line(p, data, flag); }
+__device__ __forceinline__ uint2 ld_line(const uint2* p) { return comm_ld_line(p); }
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -91,16 +64,23 @@ __global__ void __launch_bounds__(kArThreads, 1)
     for (int r = 0; r < tp; ++r) st_line(lines(peers.p[r], par, rank) + i, d, flag);
   }
 
-  // poll the local slots, fixed-order sum (identical on every rank)
+  // poll the local slots, fixed-order sum (identical on every rank): the
+  // first load of every rank's line is issued at once (one round trip for
+  // all of them), only lines not yet written are loaded again
   bool late = false;
   for (int i = i0 + tid; i < nl; i += kArThreads) {
+    uint2 v[kMaxRanks];
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r)
+      if (r < tp) v[r] = ld_line(lines(mine, par, r) + i);
     float a0 = 0.f, a1 = 0.f;
-    for (int r = 0; r < tp; ++r) {
-      const uint2* l = lines(mine, par, r) + i;
-      uint2 v = ld_line(l);
-      if (v.y != flag && !late) {
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r >= tp) continue;
+      if (v[r].y != flag && !late) {
+        const uint2* l = lines(mine, par, r) + i;
         const unsigned long long t0 = globaltimer();
-        while ((v = ld_line(l)).y != flag) {
+        while ((v[r] = ld_line(l)).y != flag) {
           if (globaltimer() - t0 > kTimeoutNs) {
             atomicExch(&g_device_status, kDevPeerTimeout);
             late = true;
@@ -108,8 +88,8 @@ __global__ void __launch_bounds__(kArThreads, 1)
           }
         }
       }
-      a0 += __uint_as_float(v.x << 16);
-      a1 += __uint_as_float(v.x & 0xFFFF0000u);
+      a0 += __uint_as_float(v[r].x << 16);
+      a1 += __uint_as_float(v[r].x & 0xFFFF0000u);
     }
     const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
     reinterpret_cast<uint32_t*>(out)[i] = *reinterpret_cast<const uint32_t*>(&h);

@@ -91,7 +91,7 @@ size_t mxfp4_packed_scales_bytes(int N, int K);
 int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, int* edge_flag,
                              void* stream);
 int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
-                     int epilogue, void* stream);
+                     int epilogue, void* stream, void* const* comm_bufs = nullptr, int rank = 0, int tp = 1);
 size_t mxfp4_gemm_wide_workspace_bytes(int M, int K);
 size_t mxfp4_chain_workspace_bytes(const b200kv_chain_op* ops, int nops, int M);
 int mxfp4_chain_launch(const b200kv_chain_op* ops, int nops, int M, void* ws, size_t ws_bytes, void* stream);
@@ -243,6 +243,11 @@ int b200kv_mxfp4_gemm(const void* W, const void* packed_scales, const void* X, v
 int b200kv_mxfp4_gemm_swiglu(const void* W, const void* packed_scales, const void* X, void* act, int N, int K,
                              int M, void* stream) {
   return b200kv::mxfp4_mma_launch(W, packed_scales, X, act, N, K, M, 1, stream);
+}
+
+int b200kv_mxfp4_gemm_allreduce(const void* W, const void* packed_scales, const void* X, void* out, int N,
+                                int K, int M, void* const* comm_bufs, int rank, int tp, void* stream) {
+  return b200kv::mxfp4_mma_launch(W, packed_scales, X, out, N, K, M, 2, stream, comm_bufs, rank, tp);
 }
 
 size_t b200kv_mxfp4_gemm_wide_workspace_bytes(int M, int K) {

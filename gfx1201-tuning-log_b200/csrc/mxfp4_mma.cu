@@ -54,6 +54,7 @@
 #include "b200kv.h"
 #include "b200kv_common.cuh"
 #include "mxfp4_tc.cuh"
+#include "peer_comm.cuh"
 #include "tcgen05.cuh"
 #include "tma.cuh"
 
@@ -90,7 +91,9 @@ struct MmaArgs {
   int nsteps;                // W boxes along K: K / 128
   int sps;                   // W boxes per K-slice
   int ntiles, nclusters, tmax, nstages, bps;
-  int epilogue;              // kEpiStore: out[M, N]; kEpiSwiglu: out[M, N / 2] (see below)
+  int epilogue;              // kEpiStore: out[M, N]; kEpiSwiglu: out[M, N / 2]; kEpiAllreduce (below)
+  PeerBufs peers;            // kEpiAllreduce: every rank's communication buffer (peer_comm.cuh)
+  int rank, tp;
 };
 
 // Epilogues.  kEpiSwiglu takes gate_up weights whose 128-row tiles hold 64
@@ -98,7 +101,17 @@ struct MmaArgs {
 // then the same up rows) and writes act[m, 64 i + r] = bf16(bf16(silu(g)) * u)
 // with g, u the bf16-rounded products, HF Llama's act_fn(gate) * up with the
 // rounding of b200kv_swiglu.
-constexpr int kEpiStore = 0, kEpiSwiglu = 1;
+//
+// kEpiAllreduce is the row-parallel product of tensor parallelism with its
+// allreduce: every rank computes its [M, N] partial over its share of K, and
+// as each 128-row tile is finished its bf16 partial goes straight into every
+// rank's communication buffer (the line protocol of peer_comm.cuh, with one
+// call counter per output tile), after which the same threads poll the
+// local buffer for the other ranks' partials of that tile and store the sum
+// in rank order -- bit for bit the plain product followed by the one-shot
+// allreduce, without its launch, and with the transfer of a tile overlapping
+// the products of the tiles still in flight.
+constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiAllreduce = 2;
 
 __device__ __forceinline__ float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -198,7 +211,7 @@ __device__ __forceinline__ void split_terms(const MmaArgs& a, int et, int s_begi
   }
 }
 
-template <int NI>
+template <int NI, bool AR>
 __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
     mxfp4_mma_kernel(const __grid_constant__ CUtensorMap wmap, const MmaArgs a) {
   using R = Roles<NI>;
@@ -412,7 +425,7 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
     // finish the owned tiles: fixed-order sum over the ranks' partials
     if (owned > 0) {
       bool ok = recv_bytes == 0 || mbar_wait_bounded(&recv_bar, 0);
-      if (a.epilogue == kEpiStore) {
+      if (!AR && a.epilogue == kEpiStore) {
         for (int t = 0; ok && t < owned; ++t) {
           const int n = (cid + (rank + t * ksz) * a.nclusters) * kTile + row;
           const float* rs = recv + ((size_t)t * ksz * kTile + row) * a.M;
@@ -421,6 +434,83 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
             for (int q = 0; q < ksz; ++q) acc += rs[(size_t)q * kTile * a.M + m];
             if (n < a.N) a.Out[(size_t)m * a.N + n] = __float2bfloat16_rn(acc);
           }
+        }
+      } else if constexpr (AR) {
+        // lanes 2j and 2j + 1 hold output rows n and n + 1 of a tile: the even
+        // lane sends the lines {out[m][n], out[m][n + 1]} of even m, the odd
+        // lane those of odd m (line index (m N + n) / 2, the one-shot kernel's)
+        const bool odd = (lane & 1) != 0;
+        for (int t = 0; t < owned; ++t) {
+          const int tile = cid + (rank + t * ksz) * a.nclusters;
+          const int n = tile * kTile + row;
+          const float* rs = recv + ((size_t)t * ksz * kTile + row) * a.M;
+          volatile uint32_t* ctr = reinterpret_cast<volatile uint32_t*>(a.peers.p[a.rank]) + tile;
+          const uint32_t call = *ctr;  // every thread reads it before the barrier below
+          const uint32_t flag = call + 1;
+          const int par = (int)(call & 1u);
+          uint32_t mine[kMaxM];
+#pragma unroll
+          for (int m = 0; m < kMaxM; ++m) {
+            float acc = 0.f;
+            if (m < a.M)
+              for (int q = 0; q < ksz; ++q) acc += rs[(size_t)q * kTile * a.M + m];
+            mine[m] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(acc));
+          }
+          uint32_t data[kMaxM / 2];
+#pragma unroll
+          for (int m = 0; m < kMaxM; ++m) {
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine[m], 1);
+            if ((m & 1) == (int)odd) data[m / 2] = odd ? (other | (mine[m] << 16)) : (mine[m] | (other << 16));
+          }
+          const int nl = (a.M + (odd ? 0 : 1)) / 2;  // lines of this lane: m = odd, odd + 2, ... < M
+          for (int r = 0; r < a.tp; ++r) {
+            uint2* dst = comm_lines(a.peers.p[r], par, a.rank);
+#pragma unroll
+            for (int j = 0; j < kMaxM / 2; ++j) {
+              const int m = 2 * j + (odd ? 1 : 0);
+              if (j < nl) comm_st_line(dst + ((size_t)m * a.N + (n & ~1)) / 2, data[j], flag);
+            }
+          }
+          // poll: the first load of every (line, rank) is issued at once, so
+          // one round trip covers them all; only lines not yet written are
+          // loaded again (bounded by %globaltimer)
+          uint8_t* own = a.peers.p[a.rank];
+          uint2 v[kMaxM / 2][kCommMaxRanks];
+#pragma unroll
+          for (int j = 0; j < kMaxM / 2; ++j)
+#pragma unroll
+            for (int r = 0; r < kCommMaxRanks; ++r)
+              if (j < nl && r < a.tp)
+                v[j][r] = comm_ld_line(comm_lines(own, par, r) + ((size_t)(2 * j + (odd ? 1 : 0)) * a.N + (n & ~1)) / 2);
+          bool late = false;
+#pragma unroll
+          for (int j = 0; j < kMaxM / 2; ++j) {
+            if (j >= nl) continue;
+            const int m = 2 * j + (odd ? 1 : 0);
+            const size_t li = ((size_t)m * a.N + (n & ~1)) / 2;
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int r = 0; r < kCommMaxRanks; ++r) {
+              if (r >= a.tp) continue;
+              if (v[j][r].y != flag && !late) {
+                const uint2* l = comm_lines(own, par, r) + li;
+                const unsigned long long t0 = globaltimer_ns();
+                while ((v[j][r] = comm_ld_line(l)).y != flag) {
+                  if (globaltimer_ns() - t0 > kCommTimeoutNs) {
+                    atomicExch(&g_device_status, kDevPeerTimeout);
+                    late = true;
+                    break;
+                  }
+                }
+              }
+              a0 += __uint_as_float(v[j][r].x << 16);
+              a1 += __uint_as_float(v[j][r].x & 0xFFFF0000u);
+            }
+            const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+            *reinterpret_cast<__nv_bfloat162*>(a.Out + (size_t)m * a.N + (n & ~1)) = h;
+          }
+          named_bar_sync(1, 128);  // every thread has read the tile's counter
+          if (row == 0) *ctr = flag;
         }
       } else {
         // the up row of gate row r is row r + 64 of the same tile, whose local
@@ -480,23 +570,23 @@ __global__ void pack_scales_kernel(const uint8_t* __restrict__ S, int layout, ui
 
 // The kernel's dynamic shared-memory limit, raised on demand (per process and
 // instantiation; the attribute is per function, the same value on every device).
-template <int NI>
+template <int NI, bool AR>
 cudaError_t raise_smem_limit(size_t smem) {
   static std::mutex mu;
   static size_t limit = 0;
   std::lock_guard<std::mutex> g(mu);
   if (smem <= limit) return cudaSuccess;
   const cudaError_t e =
-      cudaFuncSetAttribute(mxfp4_mma_kernel<NI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      cudaFuncSetAttribute(mxfp4_mma_kernel<NI, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) limit = smem;
   return e;
 }
 
-template <int NI>
+template <int NI, bool AR>
 cudaError_t launch_mma(const CUtensorMap& wm, const MmaArgs& a, int ks, cudaStream_t st) {
   const MmaLayout L{a.sps, a.tmax, a.nstages, ks, a.bps};
   const size_t smem = L.bytes(a.M);
-  const cudaError_t e = raise_smem_limit<NI>(smem);
+  const cudaError_t e = raise_smem_limit<NI, AR>(smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ks, a.nclusters, 1);
@@ -512,7 +602,7 @@ cudaError_t launch_mma(const CUtensorMap& wm, const MmaArgs& a, int ks, cudaStre
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, mxfp4_mma_kernel<NI>, wm, a);
+  return cudaLaunchKernelEx(&cfg, mxfp4_mma_kernel<NI, AR>, wm, a);
 }
 
 int env_or(const char* name, int dflt) {
@@ -522,7 +612,7 @@ int env_or(const char* name, int dflt) {
 
 // Clusters of ks CTAs with `smem` bytes each that the device can hold at once
 // (cached per device, instantiation, size and smem).
-template <int NI>
+template <int NI, bool AR>
 int max_active_clusters(int ks, size_t smem) {
   static std::mutex mu;
   static std::map<std::tuple<int, int, size_t>, int> cache;
@@ -534,7 +624,7 @@ int max_active_clusters(int ks, size_t smem) {
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
-  if (raise_smem_limit<NI>(smem) != cudaSuccess) {
+  if (raise_smem_limit<NI, AR>(smem) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
@@ -550,7 +640,7 @@ int max_active_clusters(int ks, size_t smem) {
   cfg.attrs = at;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, mxfp4_mma_kernel<NI>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, mxfp4_mma_kernel<NI, AR>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = 0;
   }
@@ -602,26 +692,26 @@ const PlanHint* find_hint(int N, int K, int M) {
   return fallback;
 }
 
-template <int NI>
+template <int NI, bool AR>
 MmaPlan plan_mma_forced(const MmaArgs& a, int sms, int force_ks, int force_st, int force_bps);
 
 // The measured plan of the shape when there is one and it fits (more
 // activation rows need more shared memory), else the cost model's.
-template <int NI>
+template <int NI, bool AR>
 MmaPlan plan_mma(const MmaArgs& a, int sms) {
   const int force_ks = env_or("B200KV_MMA_KSPLIT", 0);
   const int force_st = env_or("B200KV_MMA_STAGES", 0);
   const int force_bps = env_or("B200KV_MMA_BPS", 0);
   if (!force_ks && !force_st && !force_bps && env_or("B200KV_MMA_HINTS", 1)) {
     if (const PlanHint* h = find_hint(a.N, a.K, a.M)) {
-      const MmaPlan p = plan_mma_forced<NI>(a, sms, h->ks, h->nst, h->bps);
+      const MmaPlan p = plan_mma_forced<NI, AR>(a, sms, h->ks, h->nst, h->bps);
       if (p.ks) return p;
     }
   }
-  return plan_mma_forced<NI>(a, sms, force_ks, force_st, force_bps);
+  return plan_mma_forced<NI, AR>(a, sms, force_ks, force_st, force_bps);
 }
 
-template <int NI>
+template <int NI, bool AR>
 MmaPlan plan_mma_forced(const MmaArgs& a, int sms, int force_ks, int force_st, int force_bps) {
   // a footprint cap below half an SM lets the next kernel's CTAs share the SM
   // and start streaming while this one finishes
@@ -646,7 +736,7 @@ MmaPlan plan_mma_forced(const MmaArgs& a, int sms, int force_ks, int force_st, i
         if (tmem_cols_needed<NI>(nst, bps) > 256) continue;
         const size_t smem = MmaLayout{sps, tslots, nst, ks, bps}.bytes(a.M);
         if (smem > std::min((size_t)kSmemMax, smem_cap)) continue;
-        const int nc = min(a.ntiles, min(nc0, max_active_clusters<NI>(ks, smem)));
+        const int nc = min(a.ntiles, min(nc0, max_active_clusters<NI, AR>(ks, smem)));
         if (nc <= 0) continue;
         const int waves = cdiv(a.ntiles, nc);
         if (waves > tslots) continue;
@@ -671,9 +761,9 @@ MmaPlan plan_mma_forced(const MmaArgs& a, int sms, int force_ks, int force_st, i
   return best;
 }
 
-template <int NI>
+template <int NI, bool AR>
 int run_mma(const CUtensorMap& wm, MmaArgs a, int N, int K, int M, int sms, cudaStream_t st) {
-  const MmaPlan p = plan_mma<NI>(a, sms);
+  const MmaPlan p = plan_mma<NI, AR>(a, sms);
   if (p.ks == 0) return B200KV_ERR_UNSUPPORTED;
   a.nclusters = p.nc;
   a.sps = cdiv(a.nsteps, p.ks);
@@ -685,7 +775,7 @@ int run_mma(const CUtensorMap& wm, MmaArgs a, int N, int K, int M, int sms, cuda
             "[b200kv] mxfp4_gemm N=%d K=%d M=%d: issuers=%d ks=%d clusters=%d stages=%d boxes/stage=%d "
             "tiles/cluster=%d boxes/slice=%d\n",
             N, K, M, NI, p.ks, a.nclusters, a.nstages, a.bps, a.tmax, a.sps);
-  const cudaError_t e = launch_mma<NI>(wm, a, p.ks, st);
+  const cudaError_t e = launch_mma<NI, AR>(wm, a, p.ks, st);
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;
 }
 
@@ -711,11 +801,23 @@ int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, 
 }
 
 int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
-                     int epilogue, void* stream) {
+                     int epilogue, void* stream, void* const* comm_bufs, int rank, int tp) {
   if (!W || !Sp || !X || !Out) return B200KV_ERR_INVALID_ARG;
   if (N <= 0 || K <= 0 || M <= 0) return B200KV_ERR_INVALID_ARG;
-  if (epilogue != kEpiStore && epilogue != kEpiSwiglu) return B200KV_ERR_INVALID_ARG;
+  if (epilogue != kEpiStore && epilogue != kEpiSwiglu && epilogue != kEpiAllreduce) return B200KV_ERR_INVALID_ARG;
   if (epilogue == kEpiSwiglu && N % kTile) return B200KV_ERR_UNSUPPORTED;
+  PeerBufs pb = {};
+  if (epilogue == kEpiAllreduce) {
+    if (!comm_bufs || tp < 1 || tp > kCommMaxRanks || rank < 0 || rank >= tp) return B200KV_ERR_INVALID_ARG;
+    for (int r = 0; r < tp; ++r) {
+      if (!comm_bufs[r]) return B200KV_ERR_INVALID_ARG;
+      pb.p[r] = static_cast<uint8_t*>(comm_bufs[r]);
+    }
+    // whole tiles (the line pairs and the per-tile counters), the partial within the line area
+    if (N % kTile || N / kTile > kCommCounters || (size_t)M * N > (size_t)kCommMaxElems)
+      return B200KV_ERR_UNSUPPORTED;
+    if (reinterpret_cast<uintptr_t>(Out) & 3) return B200KV_ERR_MISALIGNED;
+  }
   if (M > kMaxM || K % kStep) return B200KV_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(Sp) & 15) ||
       (reinterpret_cast<uintptr_t>(X) & 15))
@@ -733,15 +835,25 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
   a.nsteps = K / kStep;
   a.ntiles = cdiv(N, kTile);
   a.epilogue = epilogue;
+  a.peers = pb;
+  a.rank = rank;
+  a.tp = tp;
 
   CUtensorMap wm;
   if (!encode_e2m1_unpacked_2d(&wm, W, (uint64_t)K, (uint64_t)N, (uint64_t)(K / 2), kTile))
     return B200KV_ERR_UNSUPPORTED;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int ni = env_or("B200KV_MMA_ISSUERS", 4);
-  if (ni == 1) return run_mma<1>(wm, a, N, K, M, sms, st);
-  if (ni == 2) return run_mma<2>(wm, a, N, K, M, sms, st);
-  return run_mma<4>(wm, a, N, K, M, sms, st);
+  // the allreduce epilogue is its own instantiation: its batched peer polls
+  // take registers the other epilogues should not pay for
+  if (epilogue == kEpiAllreduce) {
+    if (ni == 1) return run_mma<1, true>(wm, a, N, K, M, sms, st);
+    if (ni == 2) return run_mma<2, true>(wm, a, N, K, M, sms, st);
+    return run_mma<4, true>(wm, a, N, K, M, sms, st);
+  }
+  if (ni == 1) return run_mma<1, false>(wm, a, N, K, M, sms, st);
+  if (ni == 2) return run_mma<2, false>(wm, a, N, K, M, sms, st);
+  return run_mma<4, false>(wm, a, N, K, M, sms, st);
 }
 
 }  // namespace b200kv

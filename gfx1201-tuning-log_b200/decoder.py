@@ -161,13 +161,17 @@ class MXFP4Decoder:
     gather(out, inp) all-gathers a float32 tensor, for the argmax).  Weights are
     drawn on `gen_device` (CPU in tests, so the oracle sees the same numbers).
     fuse_swiglu: gate_up runs with the SwiGLU epilogue (rows permuted at load
-    time) wherever the tensor-core kernels take the weights."""
+    time) wherever the tensor-core kernels take the weights.  fuse_allreduce:
+    under tensor parallelism with a tp.PeerAllreduce, the decode step's o and
+    down products run with the allreduce in their epilogue (one launch each,
+    bit for bit the product followed by the allreduce)."""
 
     def __init__(self, cfg, device, batch, max_ctx, seed=0, tp=1, rank=0, allreduce=None,
                  gather=None, kv_scale=1.0 / 8, gen_device=None, layers=None, mxfp4_kernel="auto",
-                 scales=CONFIG2_SCALES, fuse_swiglu=True):
+                 scales=CONFIG2_SCALES, fuse_swiglu=True, fuse_allreduce=True):
         self.cfg, self.dev, self.B, self.tp, self.rank = cfg, device, batch, tp, rank
         self.allreduce = allreduce if allreduce is not None else (lambda t: t)
+        self._fused_ar = fuse_allreduce and tp > 1 and hasattr(allreduce, "gemm")
         self.gather = gather
         if cfg.heads % tp or cfg.kv_heads % tp or cfg.inter % tp or cfg.vocab % tp:
             raise ValueError("model does not divide over tp")
@@ -231,6 +235,14 @@ class MXFP4Decoder:
             kv["ks"].data_ptr(), kv["vs"].data_ptr(), self.B, self.hq, self.hkv, self.cfg.head_dim,
             self.cfg.block_size, KV_FP8_E4M3 if k.dtype == torch.float8_e4m3fn else KV_BF16,
             _stream(b["qkv"])), "b200kv_rope_kv_write")
+
+    def _row_parallel(self, x, lin, out):
+        """out = the allreduced row-parallel product x @ W^T (o, down)."""
+        if self._fused_ar and lin[0] == "tc" and x.shape[0] <= h4mv.MAX_M:
+            return self.allreduce.gemm(x, lin[1], lin[2], out)
+        _gemm(x, lin, out)
+        self.allreduce(out)
+        return out
 
     # ---- prompt ----------------------------------------------------------------
     def prefill(self, prompts, allreduce=None):
@@ -324,12 +336,10 @@ class MXFP4Decoder:
             q = b["qkv"][:, :self.hq * d].unflatten(1, (self.hq, d))
             fp8kv_v3.run(q, kv["k"], kv["v"], b["attn"], self.qsl, self.seq_lens, self.block_table,
                          kv["ks"], kv["vs"], d ** -0.5, max_seq_len=self.max_ctx)
-            _gemm(b["attn"].view(B, self.hq * d), lay["o"], b["o"])
-            self.allreduce(b["o"])
+            self._row_parallel(b["attn"].view(B, self.hq * d), lay["o"], b["o"])
             self._rmsnorm(b["o"], lay["post_norm"])
             _gate_up(b["x"], lay["gate_up"], b["gu"], b["act"], cfg.inter // self.tp, _stream(b["x"]))
-            _gemm(b["act"], lay["down"], b["dn"])
-            self.allreduce(b["dn"])
+            self._row_parallel(b["act"], lay["down"], b["dn"])
             nxt = self.layers[li + 1]["in_norm"] if li + 1 < len(self.layers) else self.final_norm
             self._rmsnorm(b["dn"], nxt)
         # bf16 lm_head on cuBLAS (a plain library GEMM), fp32 logits

@@ -85,22 +85,31 @@ class PeerAllreduce:
         self._lib, self._check, self._ct = lib, check, ctypes
         self.rank = dist.get_rank(group)
         self.tp = dist.get_world_size(group)
-        own = ctypes.c_void_p()
-        handle = (ctypes.c_char * 64)()
-        check(lib.b200kv_comm_alloc(ctypes.byref(own), handle), "b200kv_comm_alloc")
-        handles = [None] * self.tp
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        ptrs, self._peers = [], []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(own.value)
-                continue
-            p = ctypes.c_void_p()
-            check(lib.b200kv_comm_open(h, ctypes.byref(p)), "b200kv_comm_open")
-            ptrs.append(p.value)
-            self._peers.append(p.value)
-        self._own = own.value
-        self._bufs = (ctypes.c_void_p * self.tp)(*ptrs)
+        # two buffer sets: the one-shot kernel's and the fused GEMV's (their
+        # call counters count different things)
+        owns, handles = [], []
+        for _ in range(2):
+            own = ctypes.c_void_p()
+            handle = (ctypes.c_char * 64)()
+            check(lib.b200kv_comm_alloc(ctypes.byref(own), handle), "b200kv_comm_alloc")
+            owns.append(own.value)
+            handles.append(bytes(handle))
+        everyone = [None] * self.tp
+        dist.all_gather_object(everyone, handles, group=group)
+        self._peers, sets = [], []
+        for k in range(2):
+            ptrs = []
+            for r in range(self.tp):
+                if r == self.rank:
+                    ptrs.append(owns[k])
+                    continue
+                p = ctypes.c_void_p()
+                check(lib.b200kv_comm_open(everyone[r][k], ctypes.byref(p)), "b200kv_comm_open")
+                ptrs.append(p.value)
+                self._peers.append(p.value)
+            sets.append((ctypes.c_void_p * self.tp)(*ptrs))
+        self._owns = owns
+        self._bufs, self._gemm_bufs = sets
         dist.barrier(group=group)
 
     def __call__(self, t):
@@ -111,11 +120,26 @@ class PeerAllreduce:
             torch.cuda.current_stream(t.device).cuda_stream), "b200kv_allreduce_oneshot")
         return t
 
+    def gemm(self, x, weight, packed_scales, out):
+        """out[M, N] = the sum over ranks of x @ dequant(weight)^T, the
+        row-parallel MXFP4 product with the allreduce in its epilogue
+        (b200kv_mxfp4_gemm_allreduce, M <= 8): bit for bit h4mv.mxfp4_gemm
+        followed by this allreduce, in one launch."""
+        M, K = x.shape
+        N = weight.shape[0]
+        if x.dtype != torch.bfloat16 or not x.is_contiguous() or out.shape != (M, N) or not out.is_contiguous():
+            raise ValueError("gemm takes contiguous bf16 x [M, K] and out [M, N]")
+        self._check(self._lib.b200kv_mxfp4_gemm_allreduce(
+            weight.data_ptr(), packed_scales.data_ptr(), x.data_ptr(), out.data_ptr(), N, K, M,
+            self._gemm_bufs, self.rank, self.tp, torch.cuda.current_stream(x.device).cuda_stream),
+            "b200kv_mxfp4_gemm_allreduce")
+        return out
+
     def close(self):
         """Unmap the peers' buffers and free this rank's; call after every rank
         has finished its last allreduce (e.g. after a barrier)."""
         for p in self._peers:
             self._lib.b200kv_comm_close(p)
-        if self._own:
-            self._lib.b200kv_comm_free(self._own)
-        self._peers, self._own = [], None
+        for p in self._owns:
+            self._lib.b200kv_comm_free(p)
+        self._peers, self._owns = [], []

@@ -394,6 +394,21 @@ int b200kv_comm_free(void* buf);
 int b200kv_allreduce_oneshot(const void* in, void* out, int n, void* const* bufs, int rank, int tp,
                              void* stream);
 
+/* The row-parallel MXFP4 product with its allreduce in the epilogue (o and
+ * down under tensor parallelism, 1 <= M <= 8): each rank passes its K shard
+ * (W [N, K/2], packed scales, X [M, K]) and every rank gets out[M, N] = the sum
+ * over ranks of the partials, bit for bit b200kv_mxfp4_gemm followed by
+ * b200kv_allreduce_oneshot.  Each finished 128-row tile's bf16 partial goes
+ * into every rank's buffer as the tile completes, and the tile's threads then
+ * sum the ranks' partials in rank order; one launch, no allreduce kernel.
+ * comm_bufs: tp buffers from b200kv_comm_alloc / _open as for the one-shot
+ * allreduce, but a set of its own (its counters are per output tile).  N %
+ * 128 == 0, N <= 8192, M N <= 32768, out 4-byte aligned.  All ranks make the
+ * same sequence of calls; a rank waits at most 200 ms for a peer's tile, then
+ * reports B200KV_DEV_PEER_TIMEOUT.  Capturable in CUDA graphs. */
+int b200kv_mxfp4_gemm_allreduce(const void* W, const void* packed_scales, const void* X, void* out, int N,
+                                int K, int M, void* const* comm_bufs, int rank, int tp, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
