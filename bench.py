@@ -1087,9 +1087,9 @@ def main():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--parallel", choices=("tp", "replicas"), default="tp",
                     help="N > 1: tensor parallelism over the N GPUs (default) or N full replicas")
-    ap.add_argument("--allreduce", choices=("fused", "peer", "nccl"), default="fused",
-                    help="tensor-parallel allreduce: in the o/down GEMV's epilogue over peer memory "
-                         "(default), b200kv's one-shot peer-memory kernel after it, or NCCL")
+    ap.add_argument("--allreduce", choices=("peer", "fused", "nccl"), default="peer",
+                    help="tensor-parallel allreduce: b200kv's one-shot peer-memory kernel after the o/down "
+                         "GEMV (default), in the GEMV's epilogue over peer memory, or NCCL")
     ap.add_argument("--serving", choices=("on", "off"), default="on",
                     help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1)")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",

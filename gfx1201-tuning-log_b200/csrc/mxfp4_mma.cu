@@ -471,31 +471,21 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
               if (j < nl) comm_st_line(dst + ((size_t)m * a.N + (n & ~1)) / 2, data[j], flag);
             }
           }
-          // poll: the first load of every (line, rank) is issued at once, so
-          // one round trip covers them all; only lines not yet written are
-          // loaded again (bounded by %globaltimer)
+          // poll the local buffer, line by line (a batched first load of every
+          // (line, rank) took 161 registers and was slower: the CTA's footprint
+          // matters more here than the round trips)
           uint8_t* own = a.peers.p[a.rank];
-          uint2 v[kMaxM / 2][kCommMaxRanks];
-#pragma unroll
-          for (int j = 0; j < kMaxM / 2; ++j)
-#pragma unroll
-            for (int r = 0; r < kCommMaxRanks; ++r)
-              if (j < nl && r < a.tp)
-                v[j][r] = comm_ld_line(comm_lines(own, par, r) + ((size_t)(2 * j + (odd ? 1 : 0)) * a.N + (n & ~1)) / 2);
           bool late = false;
-#pragma unroll
-          for (int j = 0; j < kMaxM / 2; ++j) {
-            if (j >= nl) continue;
+          for (int j = 0; j < nl; ++j) {
             const int m = 2 * j + (odd ? 1 : 0);
             const size_t li = ((size_t)m * a.N + (n & ~1)) / 2;
             float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-            for (int r = 0; r < kCommMaxRanks; ++r) {
-              if (r >= a.tp) continue;
-              if (v[j][r].y != flag && !late) {
-                const uint2* l = comm_lines(own, par, r) + li;
+            for (int r = 0; r < a.tp; ++r) {
+              const uint2* l = comm_lines(own, par, r) + li;
+              uint2 v = comm_ld_line(l);
+              if (v.y != flag && !late) {
                 const unsigned long long t0 = globaltimer_ns();
-                while ((v[j][r] = comm_ld_line(l)).y != flag) {
+                while ((v = comm_ld_line(l)).y != flag) {
                   if (globaltimer_ns() - t0 > kCommTimeoutNs) {
                     atomicExch(&g_device_status, kDevPeerTimeout);
                     late = true;
@@ -503,8 +493,8 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
                   }
                 }
               }
-              a0 += __uint_as_float(v[j][r].x << 16);
-              a1 += __uint_as_float(v[j][r].x & 0xFFFF0000u);
+              a0 += __uint_as_float(v.x << 16);
+              a1 += __uint_as_float(v.x & 0xFFFF0000u);
             }
             const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
             *reinterpret_cast<__nv_bfloat162*>(a.Out + (size_t)m * a.N + (n & ~1)) = h;
