@@ -130,12 +130,27 @@ def _install_impl():
     import fp8kv_prefill
     import fp8kv_v3
 
-    counts = {"decode": 0, "prefill": 0, "fallback": 0}
+    counts = {"decode": 0, "prefill": 0, "fallback": 0, "fallback_reasons": {}}
     prefill_on = os.environ.get("FP8KV_PREFILL", "0") == "1"
     decode_on = os.environ.get("FP8KV_OVERRIDE", "1") == "1"
     _state["counts"] = counts
     orig = TritonAttentionImpl.forward
     engaged = [0]
+
+    # On CUDA, vLLM 0.22 quantises the query to fp8 before the backend when the
+    # KV cache is fp8 and the backend says it takes such queries
+    # (supports_quant_query_input, true on CUDA, false on ROCm where the
+    # reference ran).  The kernels here take bf16 queries, as the reference's
+    # did, so the layers are built without query quantisation; vLLM's own
+    # Triton kernel, the fallback, takes bf16 queries too.
+    orig_init = TritonAttentionImpl.__init__
+
+    def _init(self, *args, **kwargs):
+        orig_init(self, *args, **kwargs)
+        self.supports_quant_query_input = False
+
+    _init._b200kv_orig = orig_init
+    TritonAttentionImpl.__init__ = _init
 
     def _forward(self, layer, query, key, value, kv_cache, attn_metadata, output,
                  output_scale=None, output_block_scale=None):
@@ -146,7 +161,7 @@ def _install_impl():
             why = "prefill (FP8KV_PREFILL off)"
         if why is None and attn_metadata.max_query_len == 1 and not decode_on:
             why = "decode (FP8KV_OVERRIDE off)"
-        if engaged[0] == 0:
+        if engaged[0] == 0 and attn_metadata is not None:  # the first real batch (not the profiling run)
             engaged[0] = -1
             sys.stderr.write(f"[fp8kv-override] diag: mode={getattr(self, '_kv_quant_mode', None)!r} "
                              f"maxq={getattr(attn_metadata, 'max_query_len', None)} "
@@ -154,6 +169,10 @@ def _install_impl():
                              f"{'' if why is None else ' (' + why + ')'}\n")
         if why is not None:
             counts["fallback"] += 1
+            reasons = counts["fallback_reasons"]
+            if why not in reasons and why != "no metadata" and len(reasons) < 16:
+                sys.stderr.write(f"[fp8kv-override] fallback: {why}\n")
+            reasons[why] = reasons.get(why, 0) + 1
             return orig(self, layer, query, key, value, kv_cache, attn_metadata, output,
                         output_scale, output_block_scale)
         try:
@@ -250,6 +269,8 @@ def uninstall():
     f = TritonAttentionImpl.forward
     if getattr(TritonAttentionImpl, "_b200kv_patched", False) and hasattr(f, "_b200kv_orig"):
         TritonAttentionImpl.forward = f._b200kv_orig
+        if hasattr(TritonAttentionImpl.__init__, "_b200kv_orig"):
+            TritonAttentionImpl.__init__ = TritonAttentionImpl.__init__._b200kv_orig
         TritonAttentionImpl._b200kv_patched = False
         _state["installed"] = False
     w = getattr(TritonAttentionImpl, "do_kv_cache_update", None)

@@ -379,3 +379,18 @@ def test_hipw4_hooks_vllm_quark_w4a16_scheme():
     assert r.returncode == 0, r.stderr[-2000:]
     assert "CKPT False" in r.stdout
     assert "[hipw4] quark W4A16 MXFP4 hook installed" in r.stderr
+
+
+def test_layers_keep_bf16_queries(override):
+    """vLLM 0.22 on CUDA would quantise the query to fp8 before an fp8-KV
+    backend that reports supports_quant_query_input (true on CUDA, false on
+    the reference's ROCm); the installed patch builds every impl with it off,
+    so the kernels get bf16 queries, and uninstall restores vLLM's __init__."""
+    mod, cls, _ = override
+    assert hasattr(cls.__init__, "_b200kv_orig")
+    impl = cls(num_heads=4, head_size=128, scale=0.088, num_kv_heads=1, alibi_slopes=None,
+               sliding_window=None, kv_cache_dtype="fp8")
+    assert impl.supports_quant_query_input is False
+    orig = cls.__init__._b200kv_orig
+    mod.uninstall()
+    assert cls.__init__ is orig
