@@ -185,10 +185,15 @@ def _install_impl():
                 out = out.view(n, -1, hs)
             if q.dim() == 2:
                 q = q.view(n, -1, hs)
+            # the split count is sized from the longest context on the host; a CUDA
+            # graph keeps the count it was captured with, so under capture size it
+            # for the block table's full width (any context a replay can see)
+            import torch
+            hint = 0 if torch.cuda.is_current_stream_capturing() else attn_metadata.max_seq_len
             if attn_metadata.max_query_len == 1:
                 fp8kv_v3.run(q, kc, vc, out, attn_metadata.query_start_loc, attn_metadata.seq_lens,
                              attn_metadata.block_table, layer._k_scale, layer._v_scale, self.scale,
-                             max_seq_len=attn_metadata.max_seq_len)
+                             max_seq_len=hint)
                 counts["decode"] += 1
             else:
                 # decode tokens of a mixed batch go to the split-K decode kernel,
@@ -196,7 +201,7 @@ def _install_impl():
                 fp8kv_prefill.mixed_attention(
                     q, kc, vc, out, attn_metadata.query_start_loc, attn_metadata.seq_lens,
                     attn_metadata.block_table, layer._k_scale, layer._v_scale, self.scale,
-                    max_qlen=attn_metadata.max_query_len, max_seq_len=attn_metadata.max_seq_len)
+                    max_qlen=attn_metadata.max_query_len, max_seq_len=hint)
                 counts["prefill"] += 1
             if engaged[0] <= 0:
                 engaged[0] = 1

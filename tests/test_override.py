@@ -394,3 +394,17 @@ def test_layers_keep_bf16_queries(override):
     orig = cls.__init__._b200kv_orig
     mod.uninstall()
     assert cls.__init__ is orig
+
+
+def test_split_hint_dropped_under_graph_capture(override, monkeypatch):
+    """Under CUDA-graph capture the host's max_seq_len is the capture batch's,
+    and a replay keeps the split count it sizes; the patch passes no hint then,
+    so the kernel sizes the split for the block table's full width."""
+    mod, cls, calls = override
+    q, kv, out, layer = _tensors(2)
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
+    cls.forward(_impl(), layer, q, None, None, kv, _meta(ns=2, maxq=1), out)
+    assert calls["decode"][-1][1]["max_seq_len"] == 0
+    monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+    cls.forward(_impl(), layer, q, None, None, kv, _meta(ns=2, maxq=1), out)
+    assert calls["decode"][-1][1]["max_seq_len"] == 100
