@@ -189,7 +189,8 @@ def _install_impl():
             # graph keeps the count it was captured with, so under capture size it
             # for the block table's full width (any context a replay can see)
             import torch
-            hint = 0 if torch.cuda.is_current_stream_capturing() else attn_metadata.max_seq_len
+            capturing = torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+            hint = 0 if capturing else attn_metadata.max_seq_len
             if attn_metadata.max_query_len == 1:
                 fp8kv_v3.run(q, kc, vc, out, attn_metadata.query_start_loc, attn_metadata.seq_lens,
                              attn_metadata.block_table, layer._k_scale, layer._v_scale, self.scale,

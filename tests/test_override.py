@@ -402,6 +402,7 @@ def test_split_hint_dropped_under_graph_capture(override, monkeypatch):
     so the kernel sizes the split for the block table's full width."""
     mod, cls, calls = override
     q, kv, out, layer = _tensors(2)
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
     monkeypatch.setattr(torch.cuda, "is_current_stream_capturing", lambda: True)
     cls.forward(_impl(), layer, q, None, None, kv, _meta(ns=2, maxq=1), out)
     assert calls["decode"][-1][1]["max_seq_len"] == 0
