@@ -90,7 +90,7 @@ lib.b200kv_prefill_attn.argtypes = (
      _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
      _i32, _i32, _i32, _i32,          # num_seqs, max_qlen, q0_single, qlen_single
      _i32, _i32, _i32, _i32,          # hq, hkv, head_dim, block_size
-     _i32, _i32,                      # num_blocks, kv_dtype
+     _i32, _i32, _i32,                # num_blocks, kv_dtype, num_tokens
      _vp])
 lib.b200kv_attn_varlen_mixed.restype = _i32
 lib.b200kv_attn_varlen_mixed.argtypes = (
@@ -101,7 +101,7 @@ lib.b200kv_attn_varlen_mixed.argtypes = (
      _vp, _vp, _f32,                  # k_scale, v_scale, sm_scale
      _i32, _i32, _i32,                # num_seqs, max_qlen, max_seq_len
      _i32, _i32, _i32, _i32,          # hq, hkv, head_dim, block_size
-     _i32, _i32, _i32,                # num_blocks, max_blocks_per_seq, kv_dtype
+     _i32, _i32, _i32, _i32,          # num_blocks, max_blocks_per_seq, kv_dtype, num_tokens
      _vp])
 
 lib.b200kv_mxfp4_packed_scales_bytes.restype = ctypes.c_size_t

@@ -107,7 +107,8 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int hq, int hkv, int head_dim,
-                        int block_size, int num_blocks, int kv_dtype, int only_multi, void* stream);
+                        int block_size, int num_blocks, int kv_dtype, int only_multi, void* stream,
+                        int total_q);
 
 void set_last_error(int e) { t_last_error = e; }
 
@@ -191,13 +192,13 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int num_q_heads, int num_kv_heads,
-                        int head_dim, int block_size, int num_blocks, int kv_dtype,
+                        int head_dim, int block_size, int num_blocks, int kv_dtype, int num_tokens,
                         void* stream) {
   return b200kv::prefill_attn_launch(
       q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
       out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
       v_scale, sm_scale, num_seqs, max_qlen, q0_single, qlen_single, num_q_heads, num_kv_heads,
-      head_dim, block_size, num_blocks, kv_dtype, 0, stream);
+      head_dim, block_size, num_blocks, kv_dtype, 0, stream, num_tokens);
 }
 
 int b200kv_attn_varlen_mixed(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
@@ -209,7 +210,7 @@ int b200kv_attn_varlen_mixed(const void* q, int64_t q_stride_tok, int64_t q_stri
                              const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                              int max_seq_len, int num_q_heads, int num_kv_heads, int head_dim,
                              int block_size, int num_blocks, int max_blocks_per_seq, int kv_dtype,
-                             void* stream) {
+                             int num_tokens, void* stream) {
   if (!cu_seqlens_q || !seq_lens || max_qlen < 1) return B200KV_ERR_INVALID_ARG;
   // one-token sequences on the split-K decode kernel (output row = the token's row)
   int r = b200kv::decode_attn_launch(
@@ -223,7 +224,7 @@ int b200kv_attn_varlen_mixed(const void* q, int64_t q_stride_tok, int64_t q_stri
       q, q_stride_tok, q_stride_head, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2, out,
       out_stride_tok, out_stride_head, cu_seqlens_q, seq_lens, block_table, bt_stride, k_scale,
       v_scale, sm_scale, num_seqs, max_qlen, 0, 0, num_q_heads, num_kv_heads, head_dim, block_size,
-      num_blocks, kv_dtype, 1, stream);
+      num_blocks, kv_dtype, 1, stream, num_tokens);
 }
 
 size_t b200kv_mxfp4_packed_scales_bytes(int N, int K) {

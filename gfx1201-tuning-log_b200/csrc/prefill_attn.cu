@@ -375,7 +375,7 @@ int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                        const float* v_scale, float sm_scale, int num_seqs, int qmax,
                        int q0_single, int qlen_single, int gqa, int hkv, int block_size,
-                       int num_blocks, int only_multi, void* stream);
+                       int num_blocks, int only_multi, void* stream, int total_q);
 
 int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                         const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
@@ -384,7 +384,8 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                         const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                         const float* v_scale, float sm_scale, int num_seqs, int max_qlen,
                         int q0_single, int qlen_single, int hq, int hkv, int head_dim,
-                        int block_size, int num_blocks, int kv_dtype, int only_multi, void* stream) {
+                        int block_size, int num_blocks, int kv_dtype, int only_multi, void* stream,
+                        int total_q) {
   if (!q || !k_cache || !v_cache || !out || !block_table) return B200KV_ERR_INVALID_ARG;
   if (num_seqs <= 0 || hq <= 0 || hkv <= 0 || block_size <= 0 || num_blocks < 0 || hq % hkv)
     return B200KV_ERR_INVALID_ARG;
@@ -412,7 +413,7 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
                                      out, o_st, o_sh, cu_seqlens_q, seq_lens, block_table,
                                      bt_stride, k_scale, v_scale, sm_scale, num_seqs, qmax,
                                      q0_single, qlen_single, gqa, hkv, block_size, num_blocks,
-                                     only_multi, stream);
+                                     only_multi, stream, total_q);
     if (r >= 0) return r;
   }
   PrefillParams p;

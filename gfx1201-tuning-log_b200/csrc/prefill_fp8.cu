@@ -97,6 +97,8 @@ struct Fp8PrefillParams {
   int q0_single, qlen_single;
   int qpairs;      // gridDim.x: pairs of 128-row query tiles
   int only_multi;  // skip one-token sequences (the decode kernel's, in a mixed batch)
+  int compact;     // gridDim.x enumerates the (sequence, tile pair) items of the batch (gridDim.z = 1)
+  int num_seqs;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -192,9 +194,54 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int seq = blockIdx.z;
   const int kh = blockIdx.y;
-  const int pair = p.qpairs - 1 - (int)blockIdx.x;  // longest causal rows first
+  int seq = blockIdx.z;
+  int pair = p.qpairs - 1 - (int)blockIdx.x;  // longest causal rows first
+  if (p.compact) {
+    // The grid holds about as many CTAs (per kv head) as the batch has tile
+    // pairs, not sequences x the longest sequence's pairs: a mixed batch's
+    // one-token sequences, and the short ones of a ragged batch, then cost no
+    // CTA that only returns (those CTAs, one per SM at a time, had delayed the
+    // real ones).  Warp 0 finds the item of this CTA: a scan of the
+    // sequences' pair counts, 32 sequences at a time.
+    __shared__ int s_item[2];
+    if (warp == 0) {
+      const int target = blockIdx.x;
+      int base = 0, fseq = -1, fpair = 0;
+      for (int s0 = 0; s0 < p.num_seqs && fseq < 0; s0 += 32) {
+        const int s = s0 + lane;
+        int cnt = 0;
+        if (s < p.num_seqs) {
+          const int ql = p.cu_q[s + 1] - p.cu_q[s];
+          cnt = (ql <= 0 || (p.only_multi && ql == 1)) ? 0 : (ql + 2 * TPT - 1) / (2 * TPT);
+        }
+        int incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        if (target < base + total) {
+          const unsigned hit = __ballot_sync(0xffffffffu, target >= base + incl - cnt && target < base + incl);
+          const int src = __ffs(hit) - 1;
+          const int first = base + __shfl_sync(0xffffffffu, incl - cnt, src);
+          const int npairs = __shfl_sync(0xffffffffu, cnt, src);
+          fseq = s0 + src;
+          fpair = npairs - 1 - (target - first);  // longest causal rows first within a sequence
+        }
+        base += total;
+      }
+      if (lane == 0) {
+        s_item[0] = fseq;
+        s_item[1] = fpair;
+      }
+    }
+    __syncthreads();
+    seq = s_item[0];
+    pair = s_item[1];
+    if (seq < 0) return;  // past the batch's items (CTA-uniform)
+  }
 
   const int qstart = p.cu_q ? p.cu_q[seq] : 0;
   const int qlen = p.cu_q ? p.cu_q[seq + 1] - qstart : p.qlen_single;
@@ -529,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int GQA>
 cudaError_t launch_fp8(const CUtensorMap& km, const CUtensorMap& vm, const Fp8PrefillParams& p,
-                       int hkv, int ns, cudaStream_t st) {
+                       int gx, int hkv, int gz, cudaStream_t st) {
   const size_t smem = (size_t)kSmemBytes + 1024;
   static bool attr = false;
   if (!attr) {
@@ -538,7 +585,7 @@ cudaError_t launch_fp8(const CUtensorMap& km, const CUtensorMap& vm, const Fp8Pr
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  prefill_fp8_kernel<GQA><<<dim3(p.qpairs, hkv, ns), kThreads, smem, st>>>(km, vm, p);
+  prefill_fp8_kernel<GQA><<<dim3(gx, hkv, gz), kThreads, smem, st>>>(km, vm, p);
   return cudaGetLastError();
 }
 
@@ -553,7 +600,7 @@ int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
                        const int32_t* block_table, int64_t bt_stride, const float* k_scale,
                        const float* v_scale, float sm_scale, int num_seqs, int qmax,
                        int q0_single, int qlen_single, int gqa, int hkv, int block_size,
-                       int num_blocks, int only_multi, void* stream) {
+                       int num_blocks, int only_multi, void* stream, int total_q) {
   if (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128) return -1;
   if (num_blocks <= 0) return -1;
   CUtensorMap km, vm;
@@ -581,13 +628,20 @@ int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
   p.qlen_single = qlen_single;
   p.qpairs = cdiv(qmax, 2 * (kRows / gqa));
   p.only_multi = only_multi;
+  p.num_seqs = num_seqs;
+  // with the batch's token count known, the grid enumerates its tile pairs:
+  // at most total / (2 tokens per tile x tiles) + one partial pair per sequence
+  const int64_t dense = (int64_t)p.qpairs * num_seqs;
+  const int64_t items = cu_seqlens_q && total_q > 0 ? cdiv(total_q, 2 * (kRows / gqa)) + (int64_t)num_seqs : dense;
+  p.compact = items < dense && items <= 0x7fffffff;
+  int grid_x = p.compact ? (int)items : p.qpairs, grid_z = p.compact ? 1 : num_seqs;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (gqa) {
-    case 1: e = launch_fp8<1>(km, vm, p, hkv, num_seqs, st); break;
-    case 2: e = launch_fp8<2>(km, vm, p, hkv, num_seqs, st); break;
-    case 4: e = launch_fp8<4>(km, vm, p, hkv, num_seqs, st); break;
-    case 8: e = launch_fp8<8>(km, vm, p, hkv, num_seqs, st); break;
+    case 1: e = launch_fp8<1>(km, vm, p, grid_x, hkv, grid_z, st); break;
+    case 2: e = launch_fp8<2>(km, vm, p, grid_x, hkv, grid_z, st); break;
+    case 4: e = launch_fp8<4>(km, vm, p, grid_x, hkv, grid_z, st); break;
+    case 8: e = launch_fp8<8>(km, vm, p, grid_x, hkv, grid_z, st); break;
     default: return -1;
   }
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;

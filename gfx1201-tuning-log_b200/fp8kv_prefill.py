@@ -51,6 +51,7 @@ def _launch(q, k_cache, v_cache, out, cu, lens, bt, kscale, vscale, sm_scale, nu
         bt.data_ptr(), bt.stride(0), ks.data_ptr(), vs.data_ptr(), float(sm_scale),
         num_seqs, max_qlen, q0_single, qlen_single, q.shape[1], k_cache.shape[2], q.shape[2],
         k_cache.shape[1], k_cache.shape[0], _kv_dtype(k_cache),
+        q.shape[0] if cu is not None else 0,  # rows of q bound the batch's query rows
         torch.cuda.current_stream(dev).cuda_stream),
         "b200kv_prefill_attn")
     return out
@@ -105,7 +106,7 @@ def mixed_attention(q, k_cache, v_cache, out, cu_seqlens_q, seq_lens, block_tabl
         ks.data_ptr(), vs.data_ptr(), float(sm_scale),
         num_seqs, int(max_qlen), int(max_seq_len), q.shape[1], k_cache.shape[2], q.shape[2],
         k_cache.shape[1], min(k_cache.shape[0], v_cache.shape[0]), block_table.shape[1],
-        _kv_dtype(k_cache), torch.cuda.current_stream(dev).cuda_stream),
+        _kv_dtype(k_cache), q.shape[0], torch.cuda.current_stream(dev).cuda_stream),
         "b200kv_attn_varlen_mixed")
     return out
 

@@ -280,6 +280,10 @@ int b200kv_mxfp4_chain(const b200kv_chain_op* ops, int nops, int M, void* worksp
  *              ignored in the single-sequence form.
  *   num_blocks number of blocks in the cache (its first dimension): block
  *              ids outside [0, num_blocks) read as zeros on the fp8 path.
+ *   num_tokens the batch's query rows, cu_seqlens_q[num_seqs] (0 if not
+ *              known on the host): sizes the grid to the batch's query tiles
+ *              instead of num_seqs x max_qlen's, so short and one-token
+ *              sequences cost no CTAs.
  */
 int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                         const void* k_cache, const void* v_cache,
@@ -291,7 +295,7 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         const float* k_scale, const float* v_scale, float sm_scale,
                         int num_seqs, int max_qlen, int q0_single, int qlen_single,
                         int num_q_heads, int num_kv_heads, int head_dim, int block_size,
-                        int num_blocks, int kv_dtype, void* stream);
+                        int num_blocks, int kv_dtype, int num_tokens, void* stream);
 
 /* Mixed batches (decode tokens and prefills in one varlen batch, as vLLM's
  * TritonAttentionImpl.forward receives them, vllm-fp8kv/fp8kv_prefill.py:156-198
@@ -303,8 +307,9 @@ int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_he
  * kernel; each kernel leaves the other's sequences untouched (two launches on
  * `stream`).  No counterpart call in the reference.
  *   max_seq_len  upper bound of seq_lens (sizes the decode kernel's split);
- *   max_blocks_per_seq  block_table row capacity;  other arguments as
- *   b200kv_prefill_attn's varlen form (cu_seqlens_q and seq_lens required). */
+ *   max_blocks_per_seq  block_table row capacity;  other arguments (num_tokens
+ *   included) as b200kv_prefill_attn's varlen form (cu_seqlens_q and seq_lens
+ *   required). */
 int b200kv_attn_varlen_mixed(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                              const void* k_cache, const void* v_cache,
                              int64_t sk0, int64_t sk1, int64_t sk2,
@@ -315,7 +320,8 @@ int b200kv_attn_varlen_mixed(const void* q, int64_t q_stride_tok, int64_t q_stri
                              const float* k_scale, const float* v_scale, float sm_scale,
                              int num_seqs, int max_qlen, int max_seq_len,
                              int num_q_heads, int num_kv_heads, int head_dim, int block_size,
-                             int num_blocks, int max_blocks_per_seq, int kv_dtype, void* stream);
+                             int num_blocks, int max_blocks_per_seq, int kv_dtype, int num_tokens,
+                             void* stream);
 
 /* ---- paged KV-cache write ------------------------------------------------------
  *

@@ -109,7 +109,7 @@ def _mixed_call(lib, cu=0x10000, lens=0x10000, maxq=4, q=0x10000, hq=32, d=128, 
     A = 0x10000  # never dereferenced: every call below fails validation first
     return lib.b200kv_attn_varlen_mixed(q, 32 * 128, 128, A, A, 16 * 8 * 128, 8 * 128, 128,
                                         16 * 8 * 128, 8 * 128, 128, A, 32 * 128, 128, cu, lens, A, 8,
-                                        A, A, 0.088, 2, maxq, 100, hq, 8, d, 16, 64, maxblk, 0, None)
+                                        A, A, 0.088, 2, maxq, 100, hq, 8, d, 16, 64, maxblk, 0, 16, None)
 
 
 def test_mixed_attention_argument_validation(b200):

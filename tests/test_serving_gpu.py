@@ -26,12 +26,13 @@ def _check(got, ref):
     assert err < ATOL and rel < RTOL, (err, rel)
 
 
-def _serving_case(ctx, prefills, seed):
-    """Decode rows at contexts `ctx` (one new token each) and new prefills of
-    lengths `prefills`, pages of every sequence drawn from one permutation."""
+def _serving_case(ctx, prefills, seed, prefill_ctx=()):
+    """Decode rows at contexts `ctx` (one new token each), new prefills of
+    lengths `prefills` and continued prefills (kv length, query rows) in
+    `prefill_ctx`, pages of every sequence drawn from one permutation."""
     g = torch.Generator().manual_seed(seed)
-    seq = [c + 1 for c in ctx] + list(prefills)
-    qlens = [1] * len(ctx) + list(prefills)
+    seq = [c + 1 for c in ctx] + list(prefills) + [L for L, _ in prefill_ctx]
+    qlens = [1] * len(ctx) + list(prefills) + [ql for _, ql in prefill_ctx]
     nblk = [math.ceil(L / PBLK) for L in seq]
     nb = sum(nblk) + 5
     k = (torch.randn(nb, PBLK, HKV, D, generator=g) * 2).to(torch.float8_e4m3fn)
@@ -112,3 +113,35 @@ def test_device_split_all_decode_and_all_prefill(cuda):
                                       bt.to(cuda), 1.0, 1.0, D ** -0.5, max_qlen=max(pre, default=1),
                                       max_seq_len=int(lens.max()))
         _check(out, FO.prefill_reference(q, k, v, cu, lens, bt, 1.0, 1.0, D ** -0.5))
+
+
+def _prefill_raw(cuda, q, k, v, out, cu, lens, bt, num_tokens, max_qlen):
+    """b200kv_prefill_attn's varlen form with an explicit num_tokens (0 = the
+    dense grid of num_seqs x max_qlen's tile pairs)."""
+    from _b200kv import KV_FP8_E4M3, check, lib
+    ks = torch.tensor([0.9], device=cuda)
+    vs = torch.tensor([1.2], device=cuda)
+    check(lib.b200kv_prefill_attn(
+        q.data_ptr(), q.stride(0), q.stride(1), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+        v.stride(0), v.stride(1), v.stride(2), out.data_ptr(), out.stride(0), out.stride(1), cu.data_ptr(),
+        lens.data_ptr(), bt.data_ptr(), bt.stride(0), ks.data_ptr(), vs.data_ptr(), D ** -0.5,
+        bt.shape[0], max_qlen, 0, 0, q.shape[1], k.shape[2], q.shape[2], k.shape[1], k.shape[0], KV_FP8_E4M3,
+        num_tokens, torch.cuda.current_stream(cuda).cuda_stream), "b200kv_prefill_attn")
+    return out
+
+
+@pytest.mark.parametrize("qlens", [[1, 700, 1, 1, 65, 64, 63, 1, 2], [5] * 40 + [300], [1] * 37 + [129, 1, 2]])
+def test_compact_grid_equals_dense_grid(cuda, qlens):
+    """With the batch's token count the varlen kernel's grid enumerates the
+    batch's (sequence, tile pair) items instead of num_seqs x the longest
+    sequence's pairs: every item is computed as before, so the outputs are
+    bit for bit those of the dense grid (ragged, one-token and more than 32
+    sequences, so the item scan crosses its chunks of 32)."""
+    ctx = [q + 37 * (i % 5) for i, q in enumerate(qlens)]
+    q, k, v, bt, cu, lens = _serving_case([], [], seed=7, prefill_ctx=list(zip(ctx, qlens)))
+    qd, kd, vd, btd, lensd, cud = q.to(cuda), k.to(cuda), v.to(cuda), bt.to(cuda), lens.to(cuda), cu.to(cuda)
+    dense = _prefill_raw(cuda, qd, kd, vd, torch.full_like(qd, float("nan")), cud, lensd, btd, 0, max(qlens))
+    compact = _prefill_raw(cuda, qd, kd, vd, torch.full_like(qd, float("nan")), cud, lensd, btd, q.shape[0],
+                           max(qlens))
+    assert torch.equal(dense, compact)
+    _check(compact, FO.prefill_reference(q, k, v, cu, lens, bt, 0.9, 1.2, D ** -0.5))
