@@ -488,7 +488,7 @@ int decode_tma_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_c
                       const int32_t* qsl, const int32_t* seq_lens, const int32_t* bt,
                       int64_t bt_stride, const float* k_scale, const float* v_scale,
                       float sm_scale, int num_seqs, int hkv, int gqa, int block_size,
-                      int num_blocks, int out_by_qsl, int csize, void* stream);
+                      int num_blocks, int out_by_qsl, int csize, int ctx_bound, void* stream);
 
 // Cluster size (CTAs per (sequence, kv head)): the largest power of two <= 16
 // that keeps the grid within two CTAs per SM, but at least one CTA per 4096
@@ -546,7 +546,7 @@ int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
     const int r = decode_tma_launch(q, q_st, q_sh, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2,
                                     out, o_st, o_sh, qsl, seq_lens, bt, bt_stride, k_scale, v_scale,
                                     sm_scale, num_seqs, hkv, gqa, block_size, num_blocks, out_by_qsl,
-                                    cs, stream);
+                                    cs, ctx, stream);
     if (r != B200KV_ERR_UNSUPPORTED) return r;
   }
 

@@ -25,14 +25,23 @@
 //    merge through distributed shared memory and the numerics (q pre-scaled to
 //    f16 by an exact power of two per head, P rounded to f16, fp32
 //    accumulation) are those of decode_attn.cu.
-// One CTA = 4 compute warps (32 tokens of each 128-token stage apiece) + the
-// producer warp; kStages stages of (K, V) = 32 KB each.
+// One CTA = CW compute warps (ST / CW tokens of each stage apiece) + the
+// producer warp; 3 stages of (K, V) pages of ST tokens each.  Ring shapes:
+// ST = 128 with 4 or 8 compute warps (96 KB in flight per CTA) and ST = 64
+// with 4 (48 KB), whose CTA fits in the shared memory an MXFP4 GEMV CTA
+// leaves free, so that under programmatic dependent launch it becomes
+// resident while the GEMV that produces q still runs: its block-table reads
+// and the L2 prefetch of its pages then overlap that GEMV, and the next
+// GEMV's CTAs fit beside it in turn.  The launcher picks the shape from the
+// grid and the share of each CTA.
 
 #include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "b200kv.h"
 #include "b200kv_common.cuh"
@@ -46,15 +55,25 @@ namespace b200kv {
 namespace {
 
 constexpr int kHD = 128;           // head_dim (bytes per fp8 row)
-constexpr int kStageTok = 128;     // tokens per stage
-constexpr int kStages = 3;
-constexpr int kCWarps = 4;         // compute warps
-constexpr int kThreadsT = (kCWarps + 1) * 32;
+constexpr int kMaxStages = 4;
+constexpr int kMaxCWarps = 8;      // compute warps: 4 or 8 (+ the producer warp)
 constexpr int kMaxCS = 16;         // cluster size bound
-constexpr int kHalfStage = kStageTok * kHD;  // K (or V) bytes of one stage
-constexpr int kStageBytes = 2 * kHalfStage;
-constexpr int kDynSmem = kStages * kStageBytes + 1024;  // + alignment slack
 constexpr float kLog2eT = 1.4426950408889634f;
+
+// ring of NS stages of ST tokens (K and V pages of one kv head), CW compute warps
+template <int ST, int NS, int CW>
+struct Ring {
+  static_assert(ST == 64 || ST == 128, "stage tokens");
+  static_assert(NS >= 2 && NS <= kMaxStages, "stages");
+  static_assert((CW == 4 || CW == 8) && ST / CW >= 16, "compute warps");
+  static constexpr int kThreads = (CW + 1) * 32;
+  static constexpr int kStageTok = ST;
+  static constexpr int kStages = NS;
+  static constexpr int kTPW = ST / CW;             // tokens of a stage per compute warp
+  static constexpr int kHalfStage = ST * kHD;      // K (or V) bytes of one stage
+  static constexpr int kStageBytes = 2 * kHalfStage;
+  static constexpr int kDynSmem = NS * kStageBytes + 1024;  // + alignment slack
+};
 
 struct TmaDecodeParams {
   const __nv_bfloat16* q;
@@ -75,12 +94,12 @@ struct TmaDecodeParams {
 template <int GQA>
 struct TmaShared {
   alignas(16) float part_o[GQA][kHD];  // this CTA's unnormalised o (read by peers)
-  float wm[kCWarps][8], wl[kCWarps][8];
+  float wm[kMaxCWarps][8], wl[kMaxCWarps][8];
   float part_m[8], part_l[8];
   alignas(16) float inbox_o[GQA * kHD];     // [source rank][the elements this rank finishes]
   float inbox_ml[kMaxCS][2][8];             // every rank's (m, l) per head
   float rw[kMaxCS][8];                      // every rank's weight in the output
-  uint64_t full_bar[kStages], empty_bar[kStages], inbox_bar;
+  uint64_t full_bar[kMaxStages], empty_bar[kMaxStages], inbox_bar;
 };
 
 // byte offset of (row, byte b) in a 128-byte-swizzled tile (1024-byte aligned)
@@ -88,10 +107,16 @@ __device__ __forceinline__ uint32_t swz(int row, int b) {
   return (uint32_t)(row * 128 + ((((b >> 4) ^ row) & 7) << 4) + (b & 15));
 }
 
-template <int GQA>
-__global__ void __launch_bounds__(kThreadsT)
+template <int GQA, int ST, int NS, int CW>
+__global__ void __launch_bounds__((CW + 1) * 32)
     decode_tma_kernel(const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap, const TmaDecodeParams p) {
+  using RG = Ring<ST, NS, CW>;
+  constexpr int kCWarps = CW, kThreadsT = RG::kThreads;
+  constexpr int kStageTok = RG::kStageTok, kStages = RG::kStages, kTPW = RG::kTPW;
+  constexpr int kHalfStage = RG::kHalfStage, kStageBytes = RG::kStageBytes;
+  constexpr int kNT8 = kTPW / 8;    // 8-token MMA tiles of S^T per warp and stage
+  constexpr int kNJ = kTPW / 16;    // 16-token slices of P^T per warp and stage
   extern __shared__ uint8_t dsm_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
   __shared__ TmaShared<GQA> S;
@@ -162,7 +187,7 @@ __global__ void __launch_bounds__(kThreadsT)
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
     }
-    if (lane < min(npages, kStages * ppc)) {
+    if (lane < npages) {  // every page of the first window (all of a short share)
       tma_prefetch_l2_4d(&kmap, 0, kh, 0, e_cur);
       tma_prefetch_l2_4d(&vmap, 0, kh, 0, e_cur);
     }
@@ -236,20 +261,20 @@ __global__ void __launch_bounds__(kThreadsT)
       uint8_t* kst = smem + (size_t)s * kStageBytes;
       uint8_t* vst = kst + kHalfStage;
       const int nt = min(kStageTok, hi - (lo + ch * kStageTok));
-      const int w0 = warp * 32;
-      const int ntw = max(0, min(32, nt - w0));
+      const int w0 = warp * kTPW;
+      const int ntw = max(0, min(kTPW, nt - w0));
       if (ntw > 0) {
-        if (ntw < 32) {
+        if (ntw < kTPW) {
           // rows past the share hold other tokens or stale bytes (possibly NaN
           // codes): zero this warp's V rows there so that 0 * V stays 0
-          for (int i = lane; i < (32 - ntw) * 8; i += 32)
+          for (int i = lane; i < (kTPW - ntw) * 8; i += 32)
             *reinterpret_cast<uint4*>(vst + (w0 + ntw + (i >> 3)) * kHD + (i & 7) * 16) = make_uint4(0, 0, 0, 0);
           __syncwarp();
         }
-        // ---- S^T = q K^T over 4 token tiles of 8 ----------------------------------
-        float sfr[4][4];
+        // ---- S^T = q K^T over the warp's token tiles of 8 --------------------------
+        float sfr[kNT8][4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kNT8; ++t) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) sfr[t][e] = 0.f;
           const int row = w0 + 8 * t + g;
@@ -263,7 +288,7 @@ __global__ void __launch_bounds__(kThreadsT)
         // ---- online softmax for head g over this warp's tokens --------------------
         float mx = -INFINITY;
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
+        for (int t = 0; t < kNT8; ++t)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int tok = 8 * t + 2 * c + e;
@@ -277,9 +302,9 @@ __global__ void __launch_bounds__(kThreadsT)
         const float alpha = exp2f(m_run - m_new);
         m_run = m_new;
         float psum = 0.f;
-        uint32_t pb[4];
+        uint32_t pb[kNT8];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kNT8; ++t) {
           const float p0 = exp2f(sfr[t][0] - m_new);
           const float p1 = exp2f(sfr[t][1] - m_new);
           psum += p0 + p1;
@@ -292,12 +317,12 @@ __global__ void __launch_bounds__(kThreadsT)
         for (int i = 0; i < 8; ++i) {
           o[i][0] *= a0; o[i][1] *= a1; o[i][2] *= a0; o[i][3] *= a1;
         }
-        // ---- O^T += V^T P^T: 2 token slices of 16 x 4 dim groups of 32 ------------
+        // ---- O^T += V^T P^T: token slices of 16 x 4 dim groups of 32 --------------
         // ldmatrix.trans over rows viewed as 16-bit pairs: matrix m (lanes 8m..8m+7
         // give its rows) = tokens 8*(m&1).., dims 16*(m>>1).. of the group; thread
         // (g, c) gets bytes {V[2c][2g], V[2c][2g+1], V[2c+1][2g], V[2c+1][2g+1]}.
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < kNJ; ++j) {
           const int vrow = w0 + 16 * j + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
           for (int i2 = 0; i2 < 4; ++i2) {
@@ -317,7 +342,7 @@ __global__ void __launch_bounds__(kThreadsT)
         }
       }
       __syncwarp();
-      if (ntw > 0 && ntw < 32)  // generic writes before any later TMA write of the stage
+      if (ntw > 0 && ntw < kTPW)  // generic writes before any later TMA write of the stage
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       if (lane == 0) mbar_arrive(&S.empty_bar[s]);
     }
@@ -440,21 +465,22 @@ __global__ void __launch_bounds__(kThreadsT)
   }
 }
 
-template <int GQA>
+template <int GQA, int ST, int NS, int CW>
 cudaError_t launch_tma(const CUtensorMap& km, const CUtensorMap& vm, const TmaDecodeParams& p,
                        int csize, int hkv, int num_seqs, cudaStream_t stream) {
-  static_assert(kStages * kStageBytes >= kCWarps * GQA * kHD * 4, "stages must hold the merge");
-  cudaError_t e = cudaFuncSetAttribute(decode_tma_kernel<GQA>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kDynSmem);
+  using RG = Ring<ST, NS, CW>;
+  static_assert(NS * RG::kStageBytes >= CW * GQA * kHD * 4, "stages must hold the merge");
+  auto kern = decode_tma_kernel<GQA, ST, NS, CW>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, RG::kDynSmem);
   if (e != cudaSuccess) return e;
   if (csize > 8) {
-    e = cudaFuncSetAttribute(decode_tma_kernel<GQA>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
   }
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(csize, hkv, num_seqs);
-  lc.blockDim = dim3(kThreadsT, 1, 1);
-  lc.dynamicSmemBytes = kDynSmem;
+  lc.blockDim = dim3(RG::kThreads, 1, 1);
+  lc.dynamicSmemBytes = RG::kDynSmem;
   lc.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -465,7 +491,16 @@ cudaError_t launch_tma(const CUtensorMap& km, const CUtensorMap& vm, const TmaDe
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&lc, decode_tma_kernel<GQA>, km, vm, p);
+  return cudaLaunchKernelEx(&lc, kern, km, vm, p);
+}
+
+// Ring shapes (tokens per stage, compute warps): 0 = (128, 4), 1 = (128, 8), 2 = (64, 4).
+template <int GQA>
+cudaError_t launch_ring(int ring, const CUtensorMap& km, const CUtensorMap& vm, const TmaDecodeParams& p,
+                        int csize, int hkv, int num_seqs, cudaStream_t stream) {
+  if (ring == 2) return launch_tma<GQA, 64, 3, 4>(km, vm, p, csize, hkv, num_seqs, stream);
+  if (ring == 1) return launch_tma<GQA, 128, 3, 8>(km, vm, p, csize, hkv, num_seqs, stream);
+  return launch_tma<GQA, 128, 3, 4>(km, vm, p, csize, hkv, num_seqs, stream);
 }
 
 }  // namespace
@@ -478,7 +513,7 @@ int decode_tma_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_c
                       const int32_t* qsl, const int32_t* seq_lens, const int32_t* bt,
                       int64_t bt_stride, const float* k_scale, const float* v_scale,
                       float sm_scale, int num_seqs, int hkv, int gqa, int block_size,
-                      int num_blocks, int out_by_qsl, int csize, void* stream) {
+                      int num_blocks, int out_by_qsl, int csize, int ctx_bound, void* stream) {
   if (block_size != 16 && block_size != 32 && block_size != 64 && block_size != 128)
     return B200KV_ERR_UNSUPPORTED;
   if (num_blocks <= 0 || csize < 1 || csize > kMaxCS) return B200KV_ERR_UNSUPPORTED;
@@ -506,13 +541,39 @@ int decode_tma_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_c
   p.sm_scale = sm_scale;
   p.bs_shift = __builtin_ctz((unsigned)block_size);
   p.out_by_qsl = out_by_qsl;
+  // Ring shape, from the grid G = CTAs of the launch and a CTA's share of the
+  // context bound (measured on B200 in 32-layer decode steps of the 7B model
+  // at context 4096, where these kernels alternate with MXFP4 GEMVs):
+  //  * G above the SM count and shares of at most four 128-token stages:
+  //    64-token stages.  Two or more CTAs per SM then fit beside a GEMV CTA
+  //    and start early (batch 2: 2516 -> 2328 us a step; batch 4: 2295 -> 2142),
+  //    where longer shares want the deeper ring (batch 8: 2688 vs 2915);
+  //  * G at most half the SM count: 128-token stages and eight compute warps
+  //    (tensor-parallel shards at batch 1: TP2 1224 -> 1181 us, TP8 810 -> 795);
+  //  * otherwise 128-token stages and four compute warps (batch 1, one GPU).
+  // Pages of 128 tokens need the 128-token stage.  B200KV_DECODE_RING =
+  // 128 | 128w8 | 64 forces one.
+  const int sms = num_sms_current_device() > 0 ? num_sms_current_device() : 148;
+  const int64_t grid = (int64_t)csize * hkv * num_seqs;
+  const int share = cdiv(ctx_bound, csize);
+  int ring = 0;
+  if (grid > sms && share <= 4 * 128 && block_size <= 64)
+    ring = 2;
+  else if (2 * grid <= sms)
+    ring = 1;
+  const char* renv = getenv("B200KV_DECODE_RING");
+  if (renv && renv[0]) {
+    ring = 0;
+    if (!strcmp(renv, "128w8")) ring = 1;
+    else if (!strcmp(renv, "64") && block_size <= 64) ring = 2;
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (gqa) {
-    case 1: e = launch_tma<1>(km, vm, p, csize, hkv, num_seqs, st); break;
-    case 2: e = launch_tma<2>(km, vm, p, csize, hkv, num_seqs, st); break;
-    case 4: e = launch_tma<4>(km, vm, p, csize, hkv, num_seqs, st); break;
-    case 8: e = launch_tma<8>(km, vm, p, csize, hkv, num_seqs, st); break;
+    case 1: e = launch_ring<1>(ring, km, vm, p, csize, hkv, num_seqs, st); break;
+    case 2: e = launch_ring<2>(ring, km, vm, p, csize, hkv, num_seqs, st); break;
+    case 4: e = launch_ring<4>(ring, km, vm, p, csize, hkv, num_seqs, st); break;
+    case 8: e = launch_ring<8>(ring, km, vm, p, csize, hkv, num_seqs, st); break;
     default: return B200KV_ERR_UNSUPPORTED;
   }
   return e == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;

@@ -266,3 +266,18 @@ def test_nan_codes_past_the_sequence(cuda, pblk):
     assert torch.isfinite(out.float()).all()
     _check(out, _oracle(c))
 
+
+@pytest.mark.parametrize("ring", ["64", "128", "128w8"])
+@pytest.mark.parametrize("pblk", [16, 32, 64])
+def test_ring_shapes(cuda, monkeypatch, ring, pblk):
+    """Every ring shape of the TMA kernel (128-token stages with four or eight
+    compute warps, 64-token stages with four) over ragged lengths, partial
+    stages and one- and many-stage shares."""
+    monkeypatch.setenv("B200KV_DECODE_RING", ring)
+    lens = [1, 47, 63, 64, 65, 129, 1000, 4096]
+    c = FO.make_decode_case(len(lens), lens, pblk=pblk, seed=130 + pblk)
+    _check(_run_v3(c, cuda), _oracle(c))
+    for nsplit in (1, 16):
+        c1 = FO.make_decode_case(1, [4096], seed=140 + nsplit)
+        _check(_run_v3(c1, cuda, nsplit=nsplit), _oracle(c1))
+
