@@ -57,6 +57,13 @@ lib.b200kv_decode_attn.argtypes = (
      _i32, _i32, _i32,                # kv_dtype, out_by_qsl, num_splits
      _vp])                            # stream
 
+lib.b200kv_mxfp4_gemm_rope_kv.restype = _i32
+lib.b200kv_mxfp4_gemm_rope_kv.argtypes = (
+    [_vp, _vp, _vp, _vp, _i32, _i32, _i32,      # W, packed scales, x, qkv, N, K, M
+     _vp, _vp, _i32, _vp, _vp, _vp,            # positions, cos_sin, max_pos, slots, k/v cache
+     _i64, _i64, _i64, _i64, _i64, _i64,      # cache strides (elements)
+     _vp, _vp, _i32, _i32, _i32, _i32, _vp])  # k/v scale, hq, hkv, block_size, kv_dtype, stream
+
 lib.b200kv_rmsnorm_residual.restype = _i32
 lib.b200kv_rmsnorm_residual.argtypes = [_vp, _vp, _vp, _vp, _i32, _i32, _f32, _vp]
 lib.b200kv_rope_kv_write.restype = _i32

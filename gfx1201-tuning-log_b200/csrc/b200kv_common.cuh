@@ -60,6 +60,15 @@ __device__ __forceinline__ float silu_bf16(float g) {
   return __bfloat162float(__float2bfloat16_rn(__fdividef(g, 1.f + __expf(-g))));
 }
 
+// Neox rotary embedding of one pair (x1 at dim j, x2 at dim j + d/2 of a head;
+// c, s the cosine and sine of the pair's angle), the products rounded before
+// the sum (no fused multiply-add): the arithmetic of the RoPE + KV-write
+// kernel and of the qkv GEMV's RoPE epilogue, which so agree bit for bit.
+__device__ __forceinline__ void rope_pair(float x1, float x2, float c, float s, float& y1, float& y2) {
+  y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+  y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+}
+
 // Named barrier over `count` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -92,6 +92,12 @@ int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, 
                              void* stream);
 int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
                      int epilogue, void* stream, void* const* comm_bufs = nullptr, int rank = 0, int tp = 1);
+int mxfp4_mma_rope_kv_launch(const void* W, const void* Sp, const void* X, void* qkv, int N, int K, int M,
+                             const int32_t* positions, const float* cos_sin, int max_pos,
+                             const int64_t* slots, void* k_cache, void* v_cache, int64_t sk0, int64_t sk1,
+                             int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2, const float* k_scale,
+                             const float* v_scale, int hq, int hkv, int block_size, int kv_dtype,
+                             void* stream);
 size_t mxfp4_gemm_wide_workspace_bytes(int M, int K);
 size_t mxfp4_chain_workspace_bytes(const b200kv_chain_op* ops, int nops, int M);
 int mxfp4_chain_launch(const b200kv_chain_op* ops, int nops, int M, void* ws, size_t ws_bytes, void* stream);
@@ -244,6 +250,19 @@ int b200kv_mxfp4_gemm(const void* W, const void* packed_scales, const void* X, v
 int b200kv_mxfp4_gemm_swiglu(const void* W, const void* packed_scales, const void* X, void* act, int N, int K,
                              int M, void* stream) {
   return b200kv::mxfp4_mma_launch(W, packed_scales, X, act, N, K, M, 1, stream);
+}
+
+int b200kv_mxfp4_gemm_rope_kv(const void* W, const void* packed_scales, const void* X, void* qkv, int N,
+                              int K, int M, const int32_t* positions, const float* cos_sin, int max_pos,
+                              const int64_t* slot_mapping, void* k_cache, void* v_cache, int64_t sk0,
+                              int64_t sk1, int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2,
+                              const float* k_scale, const float* v_scale, int num_q_heads, int num_kv_heads,
+                              int block_size, int kv_dtype, void* stream) {
+  // cache strides in elements, as b200kv_rope_kv_write (fp8: bytes)
+  return b200kv::mxfp4_mma_rope_kv_launch(W, packed_scales, X, qkv, N, K, M, positions, cos_sin, max_pos,
+                                          slot_mapping, k_cache, v_cache, sk0, sk1, sk2, sv0, sv1, sv2,
+                                          k_scale, v_scale, num_q_heads, num_kv_heads, block_size, kv_dtype,
+                                          stream);
 }
 
 int b200kv_mxfp4_gemm_allreduce(const void* W, const void* packed_scales, const void* X, void* out, int N,

@@ -128,8 +128,8 @@ __global__ void __launch_bounds__(256) rope_kv_write_kernel(const RopeKvParams p
     const int head = i / half, j = i - head * half;
     __nv_bfloat16* hp = row + (size_t)head * p.d;
     const float x1 = __bfloat162float(hp[j]), x2 = __bfloat162float(hp[j + half]);
-    const float c = cs[j], s = cs[half + j];
-    const float y1 = x1 * c - x2 * s, y2 = x2 * c + x1 * s;
+    float y1, y2;
+    rope_pair(x1, x2, cs[j], cs[half + j], y1, y2);
     if (head < p.hq) {
       hp[j] = __float2bfloat16_rn(y1);
       hp[j + half] = __float2bfloat16_rn(y2);

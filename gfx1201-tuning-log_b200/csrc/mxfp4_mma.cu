@@ -42,6 +42,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -83,6 +84,25 @@ struct Roles {
   static constexpr int kAtomCol = 2 * kDStride;  // scale atoms of the ring after the accumulators
 };
 
+// kEpiRopeKv: the qkv projection of a decode step with the rotary embedding
+// and the paged KV-cache write as its epilogue (HF Llama, neox rotate_half,
+// head_dim 128, fp8 e4m3 cache).  Tile i of the output is head i: q heads
+// first, then k, then v.  q heads are rotated and stored; k heads are rotated
+// and v heads taken as they are, both quantised (x / scale, satfinite, RN) into
+// the cache slot of their token.
+struct RopeKvArgs {
+  const int32_t* pos;      // [M] token positions
+  const float* cos_sin;    // [max_pos][128]: cos of the 64 frequencies, then sin
+  int max_pos;
+  const int64_t* slots;    // [M] cache slots (block * block_size + offset), < 0 skips
+  uint8_t* kc;
+  uint8_t* vc;
+  int64_t sk0, sk1, sk2, sv0, sv1, sv2;  // bytes: block, slot in block, kv head
+  const float* k_scale;
+  const float* v_scale;
+  int hq, hkv, block_size;
+};
+
 struct MmaArgs {
   const uint8_t* Sp;         // packed scale atoms [ntiles][K/128][512]
   const __nv_bfloat16* X;    // [M, K]
@@ -94,6 +114,7 @@ struct MmaArgs {
   int epilogue;              // kEpiStore: out[M, N]; kEpiSwiglu: out[M, N / 2]; kEpiAllreduce (below)
   PeerBufs peers;            // kEpiAllreduce: every rank's communication buffer (peer_comm.cuh)
   int rank, tp;
+  RopeKvArgs rope;           // kEpiRopeKv
 };
 
 // Epilogues.  kEpiSwiglu takes gate_up weights whose 128-row tiles hold 64
@@ -111,7 +132,11 @@ struct MmaArgs {
 // in rank order -- bit for bit the plain product followed by the one-shot
 // allreduce, without its launch, and with the transfer of a tile overlapping
 // the products of the tiles still in flight.
-constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiAllreduce = 2;
+constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiAllreduce = 2, kEpiRopeKv = 3;
+
+__device__ __forceinline__ uint8_t q8_e4m3(float v, float scale) {
+  return (uint8_t)__nv_cvt_float_to_fp8(__fdiv_rn(v, scale), __NV_SATFINITE, __NV_E4M3);
+}
 
 __device__ __forceinline__ float round_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -502,6 +527,48 @@ __global__ void __launch_bounds__(Roles<NI>::kThreads, 1)
           named_bar_sync(1, 128);  // every thread has read the tile's counter
           if (row == 0) *ctr = flag;
         }
+      } else if (a.epilogue == kEpiRopeKv) {
+        // dims r and r + 64 of a head are a rotary pair: rows r and r + 64 of
+        // its tile, the second written by another warp (one barrier of the four
+        // epilogue warps, which also makes the decision to store uniform); the
+        // sums and roundings are the plain store's, then b200kv_rope_kv_write's
+        ok = named_bar_and(1, 128, ok);
+        const RopeKvArgs& R = a.rope;
+        const float ks = __ldg(R.k_scale), vs = __ldg(R.v_scale);
+        for (int t = 0; ok && row < 64 && t < owned; ++t) {
+          const int tile = cid + (rank + t * ksz) * a.nclusters;  // head
+          const float* r1 = recv + ((size_t)t * ksz * kTile + row) * a.M;
+          const float* r2 = r1 + (size_t)64 * a.M;
+          for (int m = 0; m < a.M; ++m) {
+            float s1 = 0.f, s2 = 0.f;
+            for (int q = 0; q < ksz; ++q) {
+              s1 += r1[(size_t)q * kTile * a.M + m];
+              s2 += r2[(size_t)q * kTile * a.M + m];
+            }
+            const float x1 = round_bf(s1), x2 = round_bf(s2);
+            const int64_t slot = R.slots[m];
+            if (tile < R.hq + R.hkv) {
+              const int pos = min(max(R.pos[m], 0), R.max_pos - 1);
+              const float* cs = R.cos_sin + (size_t)pos * kTile;
+              float y1, y2;
+              rope_pair(x1, x2, cs[row], cs[64 + row], y1, y2);
+              if (tile < R.hq) {
+                a.Out[(size_t)m * a.N + tile * kTile + row] = __float2bfloat16_rn(y1);
+                a.Out[(size_t)m * a.N + tile * kTile + 64 + row] = __float2bfloat16_rn(y2);
+              } else if (slot >= 0) {
+                uint8_t* dst = R.kc + (slot / R.block_size) * R.sk0 + (slot % R.block_size) * R.sk1 +
+                               (int64_t)(tile - R.hq) * R.sk2;
+                dst[row] = q8_e4m3(round_bf(y1), ks);
+                dst[64 + row] = q8_e4m3(round_bf(y2), ks);
+              }
+            } else if (slot >= 0) {
+              uint8_t* dst = R.vc + (slot / R.block_size) * R.sv0 + (slot % R.block_size) * R.sv1 +
+                             (int64_t)(tile - R.hq - R.hkv) * R.sv2;
+              dst[row] = q8_e4m3(x1, vs);
+              dst[64 + row] = q8_e4m3(x2, vs);
+            }
+          }
+        }
       } else {
         // the up row of gate row r is row r + 64 of the same tile, whose local
         // partial another warp wrote: one barrier of the four epilogue warps,
@@ -790,12 +857,19 @@ int mxfp4_pack_scales_launch(const void* S, int layout, void* Sp, int N, int K, 
   return cudaGetLastError() == cudaSuccess ? B200KV_OK : B200KV_ERR_LAUNCH;
 }
 
-int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
-                     int epilogue, void* stream, void* const* comm_bufs, int rank, int tp) {
+namespace {
+
+int mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M, int epilogue,
+               void* stream, void* const* comm_bufs, int rank, int tp, const RopeKvArgs* rope) {
   if (!W || !Sp || !X || !Out) return B200KV_ERR_INVALID_ARG;
   if (N <= 0 || K <= 0 || M <= 0) return B200KV_ERR_INVALID_ARG;
-  if (epilogue != kEpiStore && epilogue != kEpiSwiglu && epilogue != kEpiAllreduce) return B200KV_ERR_INVALID_ARG;
+  if (epilogue != kEpiStore && epilogue != kEpiSwiglu && epilogue != kEpiAllreduce && epilogue != kEpiRopeKv)
+    return B200KV_ERR_INVALID_ARG;
   if (epilogue == kEpiSwiglu && N % kTile) return B200KV_ERR_UNSUPPORTED;
+  if (epilogue == kEpiRopeKv) {
+    if (!rope) return B200KV_ERR_INVALID_ARG;
+    if (N != (rope->hq + 2 * rope->hkv) * kTile) return B200KV_ERR_UNSUPPORTED;  // head_dim 128
+  }
   PeerBufs pb = {};
   if (epilogue == kEpiAllreduce) {
     if (!comm_bufs || tp < 1 || tp > kCommMaxRanks || rank < 0 || rank >= tp) return B200KV_ERR_INVALID_ARG;
@@ -828,6 +902,7 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
   a.peers = pb;
   a.rank = rank;
   a.tp = tp;
+  if (rope) a.rope = *rope;
 
   CUtensorMap wm;
   if (!encode_e2m1_unpacked_2d(&wm, W, (uint64_t)K, (uint64_t)N, (uint64_t)(K / 2), kTile))
@@ -844,6 +919,41 @@ int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, in
   if (ni == 1) return run_mma<1, false>(wm, a, N, K, M, sms, st);
   if (ni == 2) return run_mma<2, false>(wm, a, N, K, M, sms, st);
   return run_mma<4, false>(wm, a, N, K, M, sms, st);
+}
+
+}  // namespace
+
+int mxfp4_mma_launch(const void* W, const void* Sp, const void* X, void* Out, int N, int K, int M,
+                     int epilogue, void* stream, void* const* comm_bufs, int rank, int tp) {
+  if (epilogue == kEpiRopeKv) return B200KV_ERR_INVALID_ARG;  // mxfp4_mma_rope_kv_launch
+  return mma_launch(W, Sp, X, Out, N, K, M, epilogue, stream, comm_bufs, rank, tp, nullptr);
+}
+
+int mxfp4_mma_rope_kv_launch(const void* W, const void* Sp, const void* X, void* qkv, int N, int K, int M,
+                             const int32_t* positions, const float* cos_sin, int max_pos,
+                             const int64_t* slots, void* k_cache, void* v_cache, int64_t sk0, int64_t sk1,
+                             int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2, const float* k_scale,
+                             const float* v_scale, int hq, int hkv, int block_size, int kv_dtype,
+                             void* stream) {
+  if (!positions || !cos_sin || !slots || !k_cache || !v_cache || !k_scale || !v_scale)
+    return B200KV_ERR_INVALID_ARG;
+  if (hq <= 0 || hkv <= 0 || block_size <= 0 || max_pos <= 0) return B200KV_ERR_INVALID_ARG;
+  if (kv_dtype != B200KV_KV_FP8_E4M3) return B200KV_ERR_UNSUPPORTED;
+  RopeKvArgs r;
+  r.pos = positions;
+  r.cos_sin = cos_sin;
+  r.max_pos = max_pos;
+  r.slots = slots;
+  r.kc = static_cast<uint8_t*>(k_cache);
+  r.vc = static_cast<uint8_t*>(v_cache);
+  r.sk0 = sk0; r.sk1 = sk1; r.sk2 = sk2;
+  r.sv0 = sv0; r.sv1 = sv1; r.sv2 = sv2;
+  r.k_scale = k_scale;
+  r.v_scale = v_scale;
+  r.hq = hq;
+  r.hkv = hkv;
+  r.block_size = block_size;
+  return mma_launch(W, Sp, X, qkv, N, K, M, kEpiRopeKv, stream, nullptr, 0, 1, &r);
 }
 
 }  // namespace b200kv

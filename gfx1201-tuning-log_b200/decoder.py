@@ -165,14 +165,18 @@ class MXFP4Decoder:
     under tensor parallelism with a tp.PeerAllreduce, the decode step's o and
     down products run with the allreduce in their epilogue (one launch each,
     bit for bit the product followed by the allreduce); off by default, as it
-    measured slower than the product followed by the one-shot allreduce."""
+    measured slower than the product followed by the one-shot allreduce.
+    fuse_rope: the decode step's qkv product runs with the rotary embedding and
+    the fp8 KV write in its epilogue (one launch, bit for bit the product
+    followed by b200kv_rope_kv_write) wherever the tensor-core kernel takes it."""
 
     def __init__(self, cfg, device, batch, max_ctx, seed=0, tp=1, rank=0, allreduce=None,
                  gather=None, kv_scale=1.0 / 8, gen_device=None, layers=None, mxfp4_kernel="auto",
-                 scales=CONFIG2_SCALES, fuse_swiglu=True, fuse_allreduce=False):
+                 scales=CONFIG2_SCALES, fuse_swiglu=True, fuse_allreduce=False, fuse_rope=True):
         self.cfg, self.dev, self.B, self.tp, self.rank = cfg, device, batch, tp, rank
         self.allreduce = allreduce if allreduce is not None else (lambda t: t)
         self._fused_ar = fuse_allreduce and tp > 1 and hasattr(allreduce, "gemm")
+        self._fuse_rope = fuse_rope
         self.gather = gather
         if cfg.heads % tp or cfg.kv_heads % tp or cfg.inter % tp or cfg.vocab % tp:
             raise ValueError("model does not divide over tp")
@@ -236,6 +240,24 @@ class MXFP4Decoder:
             kv["ks"].data_ptr(), kv["vs"].data_ptr(), self.B, self.hq, self.hkv, self.cfg.head_dim,
             self.cfg.block_size, KV_FP8_E4M3 if k.dtype == torch.float8_e4m3fn else KV_BF16,
             _stream(b["qkv"])), "b200kv_rope_kv_write")
+
+    def _qkv_rope_kv(self, x, lin, kv):
+        """qkv = x @ W^T, RoPE on q and k, k and v into the cache: one launch
+        (b200kv_mxfp4_gemm_rope_kv) on tensor-core weights at M <= 8 with an fp8
+        cache and head_dim 128, else the product and the glue kernel."""
+        b, k, v = self.buf, kv["k"], kv["v"]
+        if (self._fuse_rope and lin[0] == "tc" and x.shape[0] <= h4mv.MAX_M and x.is_contiguous()
+                and k.dtype == torch.float8_e4m3fn and self.cfg.head_dim == 128):
+            W, S = lin[1], lin[2]
+            check(lib.b200kv_mxfp4_gemm_rope_kv(
+                W.data_ptr(), S.data_ptr(), x.data_ptr(), b["qkv"].data_ptr(), W.shape[0], W.shape[1] * 2,
+                x.shape[0], self.positions.data_ptr(), self.rope.data_ptr(), self.max_ctx,
+                self.slots.data_ptr(), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2),
+                v.stride(0), v.stride(1), v.stride(2), kv["ks"].data_ptr(), kv["vs"].data_ptr(), self.hq,
+                self.hkv, self.cfg.block_size, KV_FP8_E4M3, _stream(x)), "b200kv_mxfp4_gemm_rope_kv")
+            return
+        _gemm(x, lin, b["qkv"])
+        self._rope_kv(kv)
 
     def _row_parallel(self, x, lin, out):
         """out = the allreduced row-parallel product x @ W^T (o, down)."""
@@ -332,8 +354,7 @@ class MXFP4Decoder:
         self._rmsnorm(None, self.layers[0]["in_norm"] if self.layers else self.final_norm)
         for li, lay in enumerate(self.layers):
             kv = self.kv[li]
-            _gemm(b["x"], lay["qkv"], b["qkv"])
-            self._rope_kv(kv)
+            self._qkv_rope_kv(b["x"], lay["qkv"], kv)
             q = b["qkv"][:, :self.hq * d].unflatten(1, (self.hq, d))
             fp8kv_v3.run(q, kv["k"], kv["v"], b["attn"], self.qsl, self.seq_lens, self.block_table,
                          kv["ks"], kv["vs"], d ** -0.5, max_seq_len=self.max_ctx)

@@ -184,6 +184,25 @@ int b200kv_mxfp4_gemm_wide_swiglu(const void* W, const void* packed_scales, cons
                                   void* workspace, size_t workspace_bytes, void* act, int N, int K, int M,
                                   void* stream);
 
+/* The qkv projection of a decode step with the rotary embedding and the paged
+ * KV-cache write as its epilogue: one launch in place of b200kv_mxfp4_gemm
+ * followed by b200kv_rope_kv_write (no counterpart in the reference, whose
+ * engine runs them as separate kernels).  W holds the [q heads | k heads |
+ * v heads] rows of one rank (N = (num_q_heads + 2 num_kv_heads) * 128,
+ * head_dim 128); 1 <= M <= 8 tokens, with the plan of b200kv_mxfp4_gemm.  The
+ * q columns of qkv [M, N] receive the rotated q, bit for bit what the two
+ * calls leave there; k (rotated) and v go to the fp8 e4m3 cache at
+ * slot_mapping[m] exactly as b200kv_rope_kv_write writes them (arguments as
+ * there: cos_sin [max_pos][128], positions clamped to [0, max_pos), strides
+ * in elements, slots < 0 skipped).  The k and v columns of qkv are not
+ * written.  kv_dtype must be B200KV_KV_FP8_E4M3. */
+int b200kv_mxfp4_gemm_rope_kv(const void* W, const void* packed_scales, const void* X, void* qkv, int N,
+                              int K, int M, const int32_t* positions, const float* cos_sin, int max_pos,
+                              const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                              int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0, int64_t sv1, int64_t sv2,
+                              const float* k_scale, const float* v_scale, int num_q_heads, int num_kv_heads,
+                              int block_size, int kv_dtype, void* stream);
+
 /* Wide batches (prefill chunks, batched decode; any M >= 1, meant for M > 8):
  * the same product on tcgen05 kind::mxf8f6f4.block_scale MMAs, weights as e2m1
  * with the packed scale atoms above, x as two e4m3 terms with per-32 block
