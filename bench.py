@@ -789,6 +789,59 @@ def run_mxfp4_m1(args):
     print(json.dumps({"part": "mxfp4_m1", "launches": 4 * (args.warmup + args.steps)}))
 
 
+def run_decode_attn(args):
+    """Decode attention alone, 32 layers' pools at --batch sequences of --ctx
+    tokens with --kv-heads kv heads (8: one GPU; 1, 2, 4: the tensor-parallel
+    shards of the 7B model on one GPU): --warmup then --steps graph replays of
+    the 32 launches, timed with CUDA events (the case the committed ncu
+    summaries of decode_tma_kernel capture)."""
+    import fp8kv_v3
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, hkv = args.batch, args.kv_heads
+    hq = hkv * (HQ // HKV)
+    g = torch.Generator(device=dev).manual_seed(4321 + B)
+    nblk = args.ctx // PBLK
+    lays = []
+    for _ in range(args.layers):
+        nb = B * nblk
+        kv = [(4 * torch.randn(nb, PBLK, hkv, D, device=dev, generator=g)).to(torch.float8_e4m3fn)
+              for _ in range(2)]
+        bt = torch.randperm(nb, device=dev, generator=g).to(torch.int32).view(B, nblk)
+        lays.append((kv[0], kv[1], bt))
+    q = torch.randn(B, hq, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(B, hq, D, dtype=torch.bfloat16, device=dev)
+    qsl = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    slens = torch.full((B,), args.ctx, dtype=torch.int32, device=dev)
+    sc = torch.full((1,), 1 / 16, device=dev)
+
+    def run():
+        for k, v, bt in lays:
+            fp8kv_v3.run(q, k, v, out, qsl, slens, bt, sc, sc, D ** -0.5, max_seq_len=args.ctx)
+    graph = capture(run)
+    ms = time_graph(graph, args.steps, args.warmup)
+    byts = args.layers * B * (2 * args.ctx * hkv * D + 2 * hq * D * 2)
+    print(json.dumps({"part": "decode_attn", "batch": B, "kv_heads": hkv, "ctx": args.ctx,
+                      "us_per_call": ms * 1e3 / args.layers, "gbs": byts / (ms * 1e-3) / 1e9}))
+
+
+def run_decode_7b(args):
+    """The 7B decoder's token step alone (decoder.py, one GPU, --batch
+    sequences at position --ctx of an fp8 cache; no prompt pass): --warmup
+    then --steps graph replays, for an ncu launch list of the step."""
+    import decoder
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dec = decoder.MXFP4Decoder(decoder.SEVEN_B, dev, args.batch, args.ctx + args.steps + args.warmup + 8, seed=7)
+    dec.positions.fill_(args.ctx)
+    dec.step()
+    dec.step()
+    graph = capture(dec.step)
+    ms = time_graph(graph, args.steps, args.warmup)
+    print(json.dumps({"part": "decode_7b", "batch": args.batch, "ctx": args.ctx, "ms_per_token_step": ms,
+                      "tok_s": args.batch / (ms * 1e-3)}))
+
+
 def run_b200(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1094,9 +1147,13 @@ def main():
                     help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1)")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
                     help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
-    ap.add_argument("--part", choices=("all", "step", "mxfp4_m1"), default="all",
+    ap.add_argument("--part", choices=("all", "step", "mxfp4_m1", "decode_attn", "decode_7b"), default="all",
                     help="all: the full line; step: the headline step only (for an ncu launch list); "
-                         "mxfp4_m1: the four 7B MXFP4 launches at M = 1, --steps times (for an ncu capture)")
+                         "mxfp4_m1: the four 7B MXFP4 launches at M = 1, --steps times (for an ncu capture); "
+                         "decode_attn: 32 decode-attention launches at --batch / --kv-heads; "
+                         "decode_7b: the 7B decoder's token step at --batch")
+    ap.add_argument("--kv-heads", type=int, default=HKV,
+                    help="--part decode_attn: kv heads per GPU (1, 2, 4: the 7B model's TP8/4/2 shards)")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 300 if args.impl == "b200" else 10
@@ -1108,6 +1165,10 @@ def main():
         run_reference(args)
     elif args.part == "mxfp4_m1":
         run_mxfp4_m1(args)
+    elif args.part == "decode_attn":
+        run_decode_attn(args)
+    elif args.part == "decode_7b":
+        run_decode_7b(args)
     else:
         run_b200(args)
 
