@@ -30,18 +30,27 @@ __device__ __forceinline__ float round_bf(float x) { return __bfloat162float(__f
 // h <- bf16(h + delta) (when delta is given); x = w * bf16(h * rsqrt(mean(h^2) + eps))
 // (HF LlamaRMSNorm: statistics in fp32, normalised value rounded to the model
 // dtype before the weight multiply).  One CTA per row, 8 elements per 16-byte
-// access, hidden % 8 == 0 and hidden <= 8 * 8 * kNormThreads.
+// access, hidden % 8 == 0 and hidden <= 8 * 8 * kNormThreads.  The norm
+// weight is load-time data: it is read before this grid waits on the previous
+// kernel, so that load leaves the critical path.
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_residual_kernel(__nv_bfloat16* h, const __nv_bfloat16* delta, const __nv_bfloat16* w,
                             __nv_bfloat16* x, int hidden, float eps) {
   __shared__ float red[kNormThreads / 32];
   if (threadIdx.x == 0) griddep_launch_dependents();
-  griddep_wait();
   const int row = blockIdx.x;
   const int nv = hidden / 8;
+  constexpr int kMaxV = 8;  // vectors per thread
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4 wvs[kMaxV];
+#pragma unroll
+  for (int j = 0; j < kMaxV; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    wvs[j] = i < nv ? __ldg(wr + i) : make_uint4(0, 0, 0, 0);
+  }
+  griddep_wait();
   uint4* hr = reinterpret_cast<uint4*>(h + (size_t)row * hidden);
   const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + (size_t)row * hidden) : nullptr;
-  constexpr int kMaxV = 8;  // vectors per thread
   uint4 hv[kMaxV];
   float ss = 0.f;
 #pragma unroll
@@ -72,13 +81,12 @@ __global__ void __launch_bounds__(kNormThreads)
 #pragma unroll
   for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
   const float r = rsqrtf(tot / (float)hidden + eps);
-  const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* xr = reinterpret_cast<uint4*>(x + (size_t)row * hidden);
 #pragma unroll
   for (int j = 0; j < kMaxV; ++j) {
     const int i = threadIdx.x + j * kNormThreads;
     if (i < nv) {
-      const uint4 v = hv[j], wv = wr[i];
+      const uint4 v = hv[j], wv = wvs[j];
       const uint32_t a[4] = {v.x, v.y, v.z, v.w}, b[4] = {wv.x, wv.y, wv.z, wv.w};
       uint32_t o[4];
 #pragma unroll
