@@ -72,6 +72,8 @@ int comm_close(void* peer);
 int comm_free(void* buf);
 int allreduce_oneshot_launch(const void* in, void* out, int n, void* const* bufs, int rank, int tp,
                              void* stream);
+int argmax_rows_launch(const float* x, int64_t ld, int rows, int cols, float* max_val, int64_t* max_idx,
+                       void* stream);
 int decode_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_cache,
                        const void* v_cache, int64_t sk0, int64_t sk1, int64_t sk2, int64_t sv0,
                        int64_t sv1, int64_t sv2, void* out, int64_t o_st, int64_t o_sh,
@@ -188,6 +190,11 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
       out_stride_tok, out_stride_head, qsl, seq_lens, block_table, bt_stride, k_scale, v_scale,
       sm_scale, num_seqs, num_q_heads, num_kv_heads, head_dim, block_size, num_blocks,
       max_blocks_per_seq, max_seq_len_hint, kv_dtype, out_by_qsl ? 1 : 0, num_splits, stream);
+}
+
+int b200kv_argmax_rows(const float* x, int64_t ld, int rows, int cols, float* max_val, int64_t* max_idx,
+                       void* stream) {
+  return b200kv::argmax_rows_launch(x, ld, rows, cols, max_val, max_idx, stream);
 }
 
 int b200kv_prefill_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_head,

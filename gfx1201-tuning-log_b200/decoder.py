@@ -223,6 +223,8 @@ class MXFP4Decoder:
         self.seq_lens = torch.zeros(batch, dtype=torch.int32, device=device)
         self.slots = torch.zeros(batch, dtype=torch.int64, device=device)
         self.logits = torch.zeros(batch, vl, dtype=torch.float32, device=device)
+        self._top_val = torch.zeros(batch, dtype=torch.float32, device=device)
+        self._top_idx = torch.zeros(batch, dtype=torch.int64, device=device)
 
     # ---- glue kernels ---------------------------------------------------------
     def _rmsnorm(self, delta, w):
@@ -330,7 +332,10 @@ class MXFP4Decoder:
     def _argmax(self):
         """Greedy token per sequence from this rank's logits (vocab-parallel
         under tensor parallelism: local (max, index), then a gather)."""
-        val, idx = self.logits.max(dim=1)
+        val, idx = self._top_val, self._top_idx
+        lg = self.logits
+        check(lib.b200kv_argmax_rows(lg.data_ptr(), lg.stride(0), lg.shape[0], lg.shape[1], val.data_ptr(),
+                                     idx.data_ptr(), _stream(lg)), "b200kv_argmax_rows")
         if self.tp > 1:
             B, vl = self.B, self.cfg.vocab // self.tp
             mine = torch.stack([val, (idx + self.rank * vl).float()], 1)  # exact below 2^24

@@ -369,6 +369,16 @@ int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_
                     int num_tokens, int num_kv_heads, int head_dim, int block_size,
                     int kv_dtype, void* stream);
 
+/* ---- greedy argmax over logits rows ---------------------------------------------
+ *
+ * For each row r < rows of x (fp32, row stride ld elements): max_val[r] = the
+ * largest of x[r, 0 .. cols) and max_idx[r] = the lowest index holding it
+ * (torch.max(x, dim=1) on NaN-free rows).  max_val may be NULL.  One launch,
+ * a cluster of 8 CTAs per row, no scratch.  No counterpart in the reference
+ * (its engine's sampler does this). */
+int b200kv_argmax_rows(const float* x, int64_t ld, int rows, int cols, float* max_val, int64_t* max_idx,
+                       void* stream);
+
 /* ---- Decoder-layer glue for the 7B decode loop --------------------------------------
  *
  * The element-wise steps around the hot path (HF Llama semantics; the
