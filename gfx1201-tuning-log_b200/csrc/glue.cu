@@ -191,6 +191,27 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// The bookkeeping that opens a decode step, for sequence b = blockIdx.x at
+// position p = positions[b]: seq_lens[b] = p + 1, slots[b] = the cache slot of
+// position p through the block table, and h[b, :] = embed[tokens[b], :] (the
+// embedding lookup).  One CTA per sequence.
+__global__ void __launch_bounds__(256)
+    decode_step_prep_kernel(const int32_t* pos, const int64_t* tokens, const uint4* embed, int hidden_v,
+                            const int32_t* bt, int64_t bt_stride, int block_size, int32_t* seq_lens,
+                            int64_t* slots, uint4* h) {
+  if (threadIdx.x == 0) griddep_launch_dependents();
+  griddep_wait();  // positions and tokens are the previous step's
+  const int b = blockIdx.x;
+  const int p = max(pos[b], 0);
+  if (threadIdx.x == 0) {
+    seq_lens[b] = p + 1;
+    slots[b] = (int64_t)bt[(int64_t)b * bt_stride + p / block_size] * block_size + p % block_size;
+  }
+  const uint4* src = embed + (size_t)tokens[b] * hidden_v;
+  uint4* dst = h + (size_t)b * hidden_v;
+  for (int i = threadIdx.x; i < hidden_v; i += blockDim.x) dst[i] = __ldg(src + i);
+}
+
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t st) {
   cudaLaunchConfig_t lc = {};
   lc.gridDim = grid;
@@ -259,6 +280,22 @@ int rope_kv_write_launch(void* qkv, int64_t qkv_st, const int32_t* positions, co
                        : reinterpret_cast<const void*>(rope_kv_write_kernel<false>);
   return launch_pdl(fn, dim3(num_tokens), dim3(256), args, static_cast<cudaStream_t>(stream)) ==
                  cudaSuccess
+             ? B200KV_OK : B200KV_ERR_LAUNCH;
+}
+
+int decode_step_prep_launch(const int32_t* positions, const int64_t* tokens, const void* embed, int hidden,
+                            const int32_t* block_table, int64_t bt_stride, int block_size, int num_seqs,
+                            int32_t* seq_lens, int64_t* slots, void* h, void* stream) {
+  if (!positions || !tokens || !embed || !block_table || !seq_lens || !slots || !h) return B200KV_ERR_INVALID_ARG;
+  if (hidden <= 0 || block_size <= 0 || num_seqs <= 0) return B200KV_ERR_INVALID_ARG;
+  if (hidden % 8 || ((reinterpret_cast<uintptr_t>(embed) | reinterpret_cast<uintptr_t>(h)) & 15))
+    return B200KV_ERR_MISALIGNED;
+  const uint4* e = static_cast<const uint4*>(embed);
+  uint4* hp = static_cast<uint4*>(h);
+  int hv = hidden / 8;
+  void* args[] = {&positions, &tokens, &e, &hv, &block_table, &bt_stride, &block_size, &seq_lens, &slots, &hp};
+  return launch_pdl(reinterpret_cast<const void*>(decode_step_prep_kernel), dim3(num_seqs), dim3(256), args,
+                    static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? B200KV_OK : B200KV_ERR_LAUNCH;
 }
 

@@ -332,7 +332,8 @@ class MXFP4Decoder:
     def _argmax(self):
         """Greedy token per sequence from this rank's logits (vocab-parallel
         under tensor parallelism: local (max, index), then a gather)."""
-        val, idx = self._top_val, self._top_idx
+        # at tp 1 the greedy tokens go straight to self.tokens (the next step's input)
+        val, idx = self._top_val, (self.tokens if self.tp == 1 else self._top_idx)
         lg = self.logits
         check(lib.b200kv_argmax_rows(lg.data_ptr(), lg.stride(0), lg.shape[0], lg.shape[1], val.data_ptr(),
                                      idx.data_ptr(), _stream(lg)), "b200kv_argmax_rows")
@@ -351,11 +352,11 @@ class MXFP4Decoder:
         rank's logits and return the greedy next tokens (device int64 [B]);
         tokens and positions advance in place."""
         cfg, b, B, d, bs = self.cfg, self.buf, self.B, self.cfg.head_dim, self.cfg.block_size
-        pos = self.positions
-        self.seq_lens.copy_(pos + 1)
-        self.slots.copy_(self.block_table.gather(1, (pos // bs).long().unsqueeze(1)).squeeze(1).long() * bs
-                         + (pos % bs).long())
-        torch.index_select(self.embed, 0, self.tokens, out=b["h"])
+        # sequence lengths, KV slots and the embedding lookup: one launch
+        check(lib.b200kv_decode_step_prep(self.positions.data_ptr(), self.tokens.data_ptr(), self.embed.data_ptr(),
+                                          cfg.hidden, self.block_table.data_ptr(), self.block_table.stride(0), bs,
+                                          B, self.seq_lens.data_ptr(), self.slots.data_ptr(), b["h"].data_ptr(),
+                                          _stream(b["h"])), "b200kv_decode_step_prep")
         self._rmsnorm(None, self.layers[0]["in_norm"] if self.layers else self.final_norm)
         for li, lay in enumerate(self.layers):
             kv = self.kv[li]

@@ -369,6 +369,16 @@ int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_
                     int num_tokens, int num_kv_heads, int head_dim, int block_size,
                     int kv_dtype, void* stream);
 
+/* The bookkeeping that opens a decode step, one launch: for each sequence
+ * b < num_seqs at position p = positions[b] (int32; negative taken as 0):
+ * seq_lens[b] = p + 1, slot_mapping[b] = block_table[b, p / block_size] *
+ * block_size + p % block_size, and h[b, :] = embed[tokens[b], :] (bf16
+ * [vocab, hidden] rows, hidden % 8 == 0, 16-byte aligned).  No counterpart in
+ * the reference (its engine prepares these on the host). */
+int b200kv_decode_step_prep(const int32_t* positions, const int64_t* tokens, const void* embed, int hidden,
+                            const int32_t* block_table, int64_t bt_stride, int block_size, int num_seqs,
+                            int32_t* seq_lens, int64_t* slot_mapping, void* h, void* stream);
+
 /* ---- greedy argmax over logits rows ---------------------------------------------
  *
  * For each row r < rows of x (fp32, row stride ld elements): max_val[r] = the

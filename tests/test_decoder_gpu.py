@@ -264,3 +264,26 @@ def test_decoder_swiglu_epilogue_bit_equal_to_separate_kernel(cuda, monkeypatch)
         a.step()
         b.step()
         assert torch.equal(a.logits, b.logits)
+
+
+def test_decode_step_prep(cuda):
+    """b200kv_decode_step_prep: sequence lengths, KV slots through the block
+    table and the embedding rows of the tokens, against torch."""
+    from _b200kv import check, lib
+    g = torch.Generator().manual_seed(21)
+    B, H, V, bs = 5, 512, 300, 16
+    embed = torch.randn(V, H, generator=g).to(torch.bfloat16).to(cuda)
+    tokens = torch.randint(0, V, (B,), generator=g).to(cuda)
+    pos = torch.tensor([0, 15, 16, 1000, 63], dtype=torch.int32, device=cuda)
+    bt = torch.randperm(5 * 64, generator=g).to(torch.int32).view(5, 64).to(cuda)
+    seq_lens = torch.zeros(B, dtype=torch.int32, device=cuda)
+    slots = torch.zeros(B, dtype=torch.int64, device=cuda)
+    h = torch.zeros(B, H, dtype=torch.bfloat16, device=cuda)
+    check(lib.b200kv_decode_step_prep(pos.data_ptr(), tokens.data_ptr(), embed.data_ptr(), H, bt.data_ptr(),
+                                      bt.stride(0), bs, B, seq_lens.data_ptr(), slots.data_ptr(), h.data_ptr(),
+                                      torch.cuda.current_stream().cuda_stream), "b200kv_decode_step_prep")
+    torch.cuda.synchronize()
+    assert torch.equal(seq_lens, pos + 1)
+    want = bt.gather(1, (pos // bs).long().unsqueeze(1)).squeeze(1).long() * bs + (pos % bs).long()
+    assert torch.equal(slots, want)
+    assert torch.equal(h, embed[tokens])
