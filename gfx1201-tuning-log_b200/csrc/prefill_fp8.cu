@@ -277,37 +277,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = tmem_slot;  // S_A 0, S_B 128, O_A 256, O_B 384
 
   if (warp == kSoftWarps) {
-    // ---------------- TMA producer ----------------------------------------------
+    // ---------------- TMA producer (the whole warp) -------------------------------
+    // Lane l holds the block id of page 32 w + l of the current window w of
+    // the CTA's pages: one load per lane, where one dependent load per page
+    // had put a global round trip before each page's copies; a tile's pages
+    // never straddle two windows (pages per tile divide 32), and lane i of the
+    // tile issues page i's two copies.
+    const int32_t* bt_row = p.bt + (int64_t)seq * p.bt_stride;
+    const int pblk = 1 << p.pblk_shift;
+    const int ppt = kBN >> p.pblk_shift;                 // pages per tile
+    const int npg = (kv_hi + pblk - 1) >> p.pblk_shift;  // pages of the CTA
     if (lane == 0) {
       tma_prefetch_desc(&kmap);
       tma_prefetch_desc(&vmap);
-      const int32_t* bt_row = p.bt + (int64_t)seq * p.bt_stride;
-      const int pblk = 1 << p.pblk_shift;
-      const int ppt = kBN >> p.pblk_shift;  // pages per tile
-      bool failed = false;
-      int issued = nmax;
-      for (int j = 0; j < nmax; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages && !mbar_wait_bounded(&kv_empty[st], ((j / kStages) - 1) & 1)) {
-          failed = true;  // stop issuing; drain what is in flight
-          issued = j;
-          break;
-        }
-        const int keys = min(kBN, kv_hi - j * kBN);
-        const int npages = (keys + pblk - 1) >> p.pblk_shift;
-        mbar_arrive_expect_tx(&kv_full[st], (uint32_t)(npages * pblk * 128 * 2));
-        uint8_t* sk = smem + kOffK + st * kOp;
-        uint8_t* sv = smem + kOffV + st * kOp;
-        for (int i = 0; i < npages; ++i) {
-          const int blk = __ldg(bt_row + j * ppt + i);
-          tma_load_4d(sk + i * pblk * 128, &kmap, 0, kh, 0, blk, &kv_full[st]);
-          tma_load_4d(sv + i * pblk * 128, &vmap, 0, kh, 0, blk, &kv_full[st]);
-        }
+    }
+    int win = -1, ent = 0;
+    int issued = nmax;
+    for (int j = 0; j < nmax; ++j) {
+      const int st = j % kStages;
+      int ok = 1;
+      if (lane == 0 && j >= kStages) ok = mbar_wait_bounded(&kv_empty[st], ((j / kStages) - 1) & 1);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) {  // stop issuing; drain what is in flight
+        issued = j;
+        break;
       }
-      // drain: every load issued has landed before the CTA may exit
+      const int p0 = j * ppt;  // first page of tile j
+      if ((p0 >> 5) != win) {
+        win = p0 >> 5;
+        const int pg = 32 * win + lane;
+        ent = pg < npg ? __ldg(bt_row + pg) : 0;
+      }
+      const int keys = min(kBN, kv_hi - j * kBN);
+      const int npages = (keys + pblk - 1) >> p.pblk_shift;
+      if (lane == 0) mbar_arrive_expect_tx(&kv_full[st], (uint32_t)(npages * pblk * 128 * 2));
+      __syncwarp();
+      const int i = lane - (p0 & 31);
+      if (i >= 0 && i < npages) {
+        tma_load_4d(smem + kOffK + st * kOp + i * pblk * 128, &kmap, 0, kh, 0, ent, &kv_full[st]);
+        tma_load_4d(smem + kOffV + st * kOp + i * pblk * 128, &vmap, 0, kh, 0, ent, &kv_full[st]);
+      }
+    }
+    // drain: every load issued has landed before the CTA may exit
+    if (lane == 0)
       for (int j = max(0, issued - kStages); j < issued; ++j)
         mbar_wait_bounded(&kv_full[j % kStages], (j / kStages) & 1);
-    }
+    __syncwarp();
   } else if (warp == kSoftWarps + 1) {
     // ---------------- MMA issuer ------------------------------------------------
     if (lane == 0) {
@@ -382,25 +396,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kvX = X ? kvhiB : kvhiA;
     const int nX = X ? nB : nA;
 
-    // Q row -> per-row power-of-two prescale (max in [2^7, 2^8)) -> qh, ql; both
-    // halves scan the whole row for its max, each writes its own 64 elements
+    // Q row -> per-row power-of-two prescale (max in [2^7, 2^8)) -> qh, ql; each
+    // half loads its own 64 elements and the halves trade their maxima
     float score_c;
     {
       const __nv_bfloat16* qr = p.q + (int64_t)(qstart + (valid ? tok : 0)) * p.q_st +
-                                (int64_t)(kh * GQA + g) * p.q_sh;
-      uint4 raw[16];
+                                (int64_t)(kh * GQA + g) * p.q_sh + 64 * H;
+      uint4 raw[8];
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
+      for (int i = 0; i < 8; ++i)
         raw[i] = valid ? *reinterpret_cast<const uint4*>(qr + 8 * i) : make_uint4(0, 0, 0, 0);
       float mx = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const uint32_t w[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(w[e] << 16)),
                                fabsf(__uint_as_float(w[e] & 0xFFFF0000u))));
       }
+      xch[0][X][H][row] = mx;
+      named_bar_sync(bar_id, 256);
+      mx = fmaxf(mx, xch[0][X][H ^ 1][row]);
+      named_bar_sync(bar_id, 256);  // both halves read before the slot is reused
       const int E = (int)((__float_as_uint(mx) >> 23) & 0xFF);
       int sh = (E == 0xFF || mx == 0.f) ? 0 : 134 - E;
       sh = max(-126, min(127, sh));
@@ -413,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[16];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const uint4 r4 = H ? raw[2 * (4 + cc) + h] : raw[2 * cc + h];
+          const uint4 r4 = raw[2 * cc + h];
           const uint32_t w[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
