@@ -842,6 +842,15 @@ def run_decode_7b(args):
                       "tok_s": args.batch / (ms * 1e-3)}))
 
 
+def run_prefill(args):
+    """Config 3 alone (prefill_part: four sequences of 512-2048 tokens, one
+    varlen causal call per replay), for an ncu capture of prefill_fp8_kernel."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    us, flops = prefill_part(dev, args.steps, args.warmup)
+    print(json.dumps({"part": "prefill", "us_per_call": us, "tflops": flops / (us * 1e-6) / 1e12}))
+
+
 def run_b200(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1147,11 +1156,12 @@ def main():
                     help="time the config-5 serving step (about 70 GB of KV pool per GPU at tp 1)")
     ap.add_argument("--gemv", choices=("tc", "cuda-core"), default="tc",
                     help="MXFP4 kernel: block-scaled tensor cores (packed scales) or CUDA-core mma.sync")
-    ap.add_argument("--part", choices=("all", "step", "mxfp4_m1", "decode_attn", "decode_7b"), default="all",
+    ap.add_argument("--part", choices=("all", "step", "mxfp4_m1", "decode_attn", "decode_7b", "prefill"),
+                    default="all",
                     help="all: the full line; step: the headline step only (for an ncu launch list); "
                          "mxfp4_m1: the four 7B MXFP4 launches at M = 1, --steps times (for an ncu capture); "
                          "decode_attn: 32 decode-attention launches at --batch / --kv-heads; "
-                         "decode_7b: the 7B decoder's token step at --batch")
+                         "decode_7b: the 7B decoder's token step at --batch; prefill: config 3 alone")
     ap.add_argument("--kv-heads", type=int, default=HKV,
                     help="--part decode_attn: kv heads per GPU (1, 2, 4: the 7B model's TP8/4/2 shards)")
     args = ap.parse_args()
@@ -1169,6 +1179,8 @@ def main():
         run_decode_attn(args)
     elif args.part == "decode_7b":
         run_decode_7b(args)
+    elif args.part == "prefill":
+        run_prefill(args)
     else:
         run_b200(args)
 
