@@ -97,7 +97,8 @@ struct Fp8PrefillParams {
   int q0_single, qlen_single;
   int qpairs;      // gridDim.x: pairs of 128-row query tiles
   int only_multi;  // skip one-token sequences (the decode kernel's, in a mixed batch)
-  int compact;     // gridDim.x enumerates the (sequence, tile pair) items of the batch (gridDim.z = 1)
+  int compact;     // the item index enumerates the (sequence, tile pair) items of the batch (gridDim.z = 1)
+  int head_fast;   // grid (kv heads, items, z), else (items, kv heads, z)
   int num_seqs;
 };
 
@@ -194,9 +195,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int kh = blockIdx.y;
+  // The kv head is the fastest grid index (blockIdx.x; for more than 65535
+  // items, the grid's y limit, the item is): the CTAs of one
+  // (sequence, tile pair) item for every head are dispatched together, so the
+  // longest items start in the first waves instead of after the other heads'
+  // short ones (config 3 dispatched the 16-tile items of the last heads last).
+  const int kh = p.head_fast ? blockIdx.x : blockIdx.y;
+  const int item = p.head_fast ? blockIdx.y : blockIdx.x;
   int seq = blockIdx.z;
-  int pair = p.qpairs - 1 - (int)blockIdx.x;  // longest causal rows first
+  int pair = p.qpairs - 1 - item;  // longest causal rows first
   if (p.compact) {
     // The grid holds about as many CTAs (per kv head) as the batch has tile
     // pairs, not sequences x the longest sequence's pairs: a mixed batch's
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // sequences' pair counts, 32 sequences at a time.
     __shared__ int s_item[2];
     if (warp == 0) {
-      const int target = blockIdx.x;
+      const int target = item;
       int base = 0, fseq = -1, fpair = 0;
       for (int s0 = 0; s0 < p.num_seqs && fseq < 0; s0 += 32) {
         const int s = s0 + lane;
@@ -603,7 +610,8 @@ cudaError_t launch_fp8(const CUtensorMap& km, const CUtensorMap& vm, const Fp8Pr
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  prefill_fp8_kernel<GQA><<<dim3(gx, hkv, gz), kThreads, smem, st>>>(km, vm, p);
+  const dim3 grid = p.head_fast ? dim3(hkv, gx, gz) : dim3(gx, hkv, gz);
+  prefill_fp8_kernel<GQA><<<grid, kThreads, smem, st>>>(km, vm, p);
   return cudaGetLastError();
 }
 
@@ -653,6 +661,7 @@ int prefill_fp8_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k_
   const int64_t items = cu_seqlens_q && total_q > 0 ? cdiv(total_q, 2 * (kRows / gqa)) + (int64_t)num_seqs : dense;
   p.compact = items < dense && items <= 0x7fffffff;
   int grid_x = p.compact ? (int)items : p.qpairs, grid_z = p.compact ? 1 : num_seqs;
+  p.head_fast = grid_x <= 65535;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (gqa) {
