@@ -64,6 +64,7 @@ struct PrefillParams {
   int block_size, bs_shift;
   int q0_single, qlen_single;
   int only_multi;  // skip one-token sequences (the decode kernel's, in a mixed batch)
+  int head_fast;   // grid (kv heads, query tiles, sequences), else (query tiles, kv heads, sequences)
 };
 
 // Byte offset of the 16-byte chunk `c16` (0..15) of row `r` of a 128 x 128 f16
@@ -136,9 +137,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_attn_kernel(const Prefill
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
+  // The kv head is the fastest grid index and query tiles go longest causal
+  // rows first, so the longest tiles of every head start in the first waves
+  // (at most 65535 query tiles, the grid's y limit; else the tile is fastest).
   const int seq = blockIdx.z;
-  const int kh = blockIdx.y;
-  const int qt = blockIdx.x;
+  const int kh = p.head_fast ? blockIdx.x : blockIdx.y;
+  const int qt = p.head_fast ? (int)(gridDim.y - 1 - blockIdx.y) : blockIdx.x;
 
   const int qstart = p.cu_q ? p.cu_q[seq] : 0;
   const int qlen = p.cu_q ? p.cu_q[seq + 1] - qstart : p.qlen_single;
@@ -362,7 +366,8 @@ cudaError_t launch_prefill(const PrefillParams& p, int qtiles, int hkv, int ns, 
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  prefill_attn_kernel<GQA, FP8><<<dim3(qtiles, hkv, ns), kThreads, smem, st>>>(p);
+  const dim3 grid = p.head_fast ? dim3(hkv, qtiles, ns) : dim3(qtiles, hkv, ns);
+  prefill_attn_kernel<GQA, FP8><<<grid, kThreads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -440,6 +445,7 @@ int prefill_attn_launch(const void* q, int64_t q_st, int64_t q_sh, const void* k
   p.qlen_single = qlen_single;
   p.only_multi = only_multi;
   const int qtiles = cdiv(qmax, kRows / gqa);
+  p.head_fast = qtiles <= 65535;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (gqa * 2 + (fp8 ? 1 : 0)) {
