@@ -195,11 +195,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  // The kv head is the fastest grid index (blockIdx.x; for more than 65535
-  // items, the grid's y limit, the item is): the CTAs of one
-  // (sequence, tile pair) item for every head are dispatched together, so the
-  // longest items start in the first waves instead of after the other heads'
-  // short ones (config 3 dispatched the 16-tile items of the last heads last).
+  // The kv head is the fastest grid index (blockIdx.x), so the CTAs of one
+  // (sequence, tile pair) item start together for every head and the longest
+  // items run in the first waves; with the item fastest, the longest items of
+  // the last heads were dispatched last and set the end of the call.  Beyond
+  // 65535 items (the grid's y limit) the item is the fastest index.
   const int kh = p.head_fast ? blockIdx.x : blockIdx.y;
   const int item = p.head_fast ? blockIdx.y : blockIdx.x;
   int seq = blockIdx.z;
