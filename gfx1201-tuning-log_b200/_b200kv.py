@@ -65,7 +65,8 @@ lib.b200kv_mxfp4_gemm_rope_kv.argtypes = (
      _vp, _vp, _i32, _i32, _i32, _i32, _vp])  # k/v scale, hq, hkv, block_size, kv_dtype, stream
 
 lib.b200kv_decode_step_prep.restype = _i32
-lib.b200kv_decode_step_prep.argtypes = [_vp, _vp, _vp, _i32, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp]
+lib.b200kv_decode_step_prep.argtypes = [_vp, _vp, _vp, _i32, _i32, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp,
+                                        _vp]
 lib.b200kv_argmax_rows.restype = _i32
 lib.b200kv_argmax_rows.argtypes = [_vp, _i64, _i32, _i32, _vp, _vp, _vp]
 

@@ -15,6 +15,7 @@ enum DeviceStatus : int {
   kDevSplitOverflow = 0x102,     // seq_len larger than the context bound given
   kDevPeerTimeout = 0x103,       // a peer GPU's flag did not arrive in time
   kDevChainTimeout = 0x104,      // a chained GEMV's input tile was not ready in time
+  kDevIndexRange = 0x105,        // a token id or position outside its table
 };
 extern __device__ int g_device_status;
 

@@ -66,8 +66,9 @@ int rope_kv_write_launch(void* qkv, int64_t qkv_st, const int32_t* positions, co
                          int hq, int hkv, int head_dim, int block_size, int kv_dtype, void* stream);
 int swiglu_launch(const void* gate_up, void* act, int rows, int inter, void* stream);
 int decode_step_prep_launch(const int32_t* positions, const int64_t* tokens, const void* embed, int hidden,
-                            const int32_t* block_table, int64_t bt_stride, int block_size, int num_seqs,
-                            int32_t* seq_lens, int64_t* slots, void* h, void* stream);
+                            int vocab, const int32_t* block_table, int64_t bt_stride, int max_blocks,
+                            int block_size, int num_seqs, int32_t* seq_lens, int64_t* slots, void* h,
+                            void* stream);
 size_t comm_buffer_bytes();
 int comm_alloc(void** buf, void* ipc_handle);
 int comm_open(const void* ipc_handle, void** peer);
@@ -196,10 +197,12 @@ int b200kv_decode_attn(const void* q, int64_t q_stride_tok, int64_t q_stride_hea
 }
 
 int b200kv_decode_step_prep(const int32_t* positions, const int64_t* tokens, const void* embed, int hidden,
-                            const int32_t* block_table, int64_t bt_stride, int block_size, int num_seqs,
-                            int32_t* seq_lens, int64_t* slot_mapping, void* h, void* stream) {
-  return b200kv::decode_step_prep_launch(positions, tokens, embed, hidden, block_table, bt_stride, block_size,
-                                         num_seqs, seq_lens, slot_mapping, h, stream);
+                            int vocab, const int32_t* block_table, int64_t bt_stride, int max_blocks_per_seq,
+                            int block_size, int num_seqs, int32_t* seq_lens, int64_t* slot_mapping, void* h,
+                            void* stream) {
+  return b200kv::decode_step_prep_launch(positions, tokens, embed, hidden, vocab, block_table, bt_stride,
+                                         max_blocks_per_seq, block_size, num_seqs, seq_lens, slot_mapping, h,
+                                         stream);
 }
 
 int b200kv_argmax_rows(const float* x, int64_t ld, int rows, int cols, float* max_val, int64_t* max_idx,

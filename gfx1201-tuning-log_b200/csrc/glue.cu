@@ -194,21 +194,30 @@ __global__ void __launch_bounds__(256)
 // The bookkeeping that opens a decode step, for sequence b = blockIdx.x at
 // position p = positions[b]: seq_lens[b] = p + 1, slots[b] = the cache slot of
 // position p through the block table, and h[b, :] = embed[tokens[b], :] (the
-// embedding lookup).  One CTA per sequence.
+// embedding lookup).  One CTA per sequence.  Ids and positions outside their
+// tables read nothing: a zero row, slot -1, and the device status records it.
 __global__ void __launch_bounds__(256)
     decode_step_prep_kernel(const int32_t* pos, const int64_t* tokens, const uint4* embed, int hidden_v,
-                            const int32_t* bt, int64_t bt_stride, int block_size, int32_t* seq_lens,
-                            int64_t* slots, uint4* h) {
+                            int vocab, const int32_t* bt, int64_t bt_stride, int max_blocks, int block_size,
+                            int32_t* seq_lens, int64_t* slots, uint4* h) {
   if (threadIdx.x == 0) griddep_launch_dependents();
   griddep_wait();  // positions and tokens are the previous step's
   const int b = blockIdx.x;
   const int p = max(pos[b], 0);
+  const int64_t tok = tokens[b];
+  const bool tok_ok = tok >= 0 && tok < vocab;
   if (threadIdx.x == 0) {
     seq_lens[b] = p + 1;
-    slots[b] = (int64_t)bt[(int64_t)b * bt_stride + p / block_size] * block_size + p % block_size;
+    const int page = p / block_size;
+    slots[b] = page < max_blocks ? (int64_t)bt[(int64_t)b * bt_stride + page] * block_size + p % block_size : -1;
+    if (page >= max_blocks || !tok_ok) atomicExch(&g_device_status, kDevIndexRange);
   }
-  const uint4* src = embed + (size_t)tokens[b] * hidden_v;
   uint4* dst = h + (size_t)b * hidden_v;
+  if (!tok_ok) {
+    for (int i = threadIdx.x; i < hidden_v; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* src = embed + (size_t)tok * hidden_v;
   for (int i = threadIdx.x; i < hidden_v; i += blockDim.x) dst[i] = __ldg(src + i);
 }
 
@@ -284,16 +293,19 @@ int rope_kv_write_launch(void* qkv, int64_t qkv_st, const int32_t* positions, co
 }
 
 int decode_step_prep_launch(const int32_t* positions, const int64_t* tokens, const void* embed, int hidden,
-                            const int32_t* block_table, int64_t bt_stride, int block_size, int num_seqs,
-                            int32_t* seq_lens, int64_t* slots, void* h, void* stream) {
+                            int vocab, const int32_t* block_table, int64_t bt_stride, int max_blocks,
+                            int block_size, int num_seqs, int32_t* seq_lens, int64_t* slots, void* h,
+                            void* stream) {
   if (!positions || !tokens || !embed || !block_table || !seq_lens || !slots || !h) return B200KV_ERR_INVALID_ARG;
-  if (hidden <= 0 || block_size <= 0 || num_seqs <= 0) return B200KV_ERR_INVALID_ARG;
+  if (hidden <= 0 || vocab <= 0 || max_blocks <= 0 || block_size <= 0 || num_seqs <= 0)
+    return B200KV_ERR_INVALID_ARG;
   if (hidden % 8 || ((reinterpret_cast<uintptr_t>(embed) | reinterpret_cast<uintptr_t>(h)) & 15))
     return B200KV_ERR_MISALIGNED;
   const uint4* e = static_cast<const uint4*>(embed);
   uint4* hp = static_cast<uint4*>(h);
   int hv = hidden / 8;
-  void* args[] = {&positions, &tokens, &e, &hv, &block_table, &bt_stride, &block_size, &seq_lens, &slots, &hp};
+  void* args[] = {&positions, &tokens, &e,   &hv,    &vocab, &block_table, &bt_stride,
+                  &max_blocks, &block_size, &seq_lens, &slots, &hp};
   return launch_pdl(reinterpret_cast<const void*>(decode_step_prep_kernel), dim3(num_seqs), dim3(256), args,
                     static_cast<cudaStream_t>(stream)) == cudaSuccess
              ? B200KV_OK : B200KV_ERR_LAUNCH;

@@ -354,8 +354,9 @@ class MXFP4Decoder:
         cfg, b, B, d, bs = self.cfg, self.buf, self.B, self.cfg.head_dim, self.cfg.block_size
         # sequence lengths, KV slots and the embedding lookup: one launch
         check(lib.b200kv_decode_step_prep(self.positions.data_ptr(), self.tokens.data_ptr(), self.embed.data_ptr(),
-                                          cfg.hidden, self.block_table.data_ptr(), self.block_table.stride(0), bs,
-                                          B, self.seq_lens.data_ptr(), self.slots.data_ptr(), b["h"].data_ptr(),
+                                          cfg.hidden, self.embed.shape[0], self.block_table.data_ptr(),
+                                          self.block_table.stride(0), self.block_table.shape[1], bs, B,
+                                          self.seq_lens.data_ptr(), self.slots.data_ptr(), b["h"].data_ptr(),
                                           _stream(b["h"])), "b200kv_decode_step_prep")
         self._rmsnorm(None, self.layers[0]["in_norm"] if self.layers else self.final_norm)
         for li, lay in enumerate(self.layers):

@@ -57,12 +57,15 @@ int b200kv_last_error(void);
  * 0 = clean; B200KV_DEV_MBARRIER_TIMEOUT: an mbarrier (a copy or a peer warp)
  * never completed; B200KV_DEV_PEER_TIMEOUT: a peer GPU's allreduce flag did not
  * arrive; B200KV_DEV_CHAIN_TIMEOUT: an input tile of a chained GEMV
- * (b200kv_mxfp4_chain) was not ready in time.  Reading it synchronises the given stream.
- * b200kv_reset_device_status() clears it (async on stream).
+ * (b200kv_mxfp4_chain) was not ready in time; B200KV_DEV_INDEX_RANGE: a token
+ * id or position outside its table (b200kv_decode_step_prep).  Reading it
+ * synchronises the given stream.  b200kv_reset_device_status() clears it
+ * (async on stream).
  */
 #define B200KV_DEV_MBARRIER_TIMEOUT 0x101
 #define B200KV_DEV_PEER_TIMEOUT     0x103
 #define B200KV_DEV_CHAIN_TIMEOUT    0x104
+#define B200KV_DEV_INDEX_RANGE      0x105
 int b200kv_get_device_status(void* stream, int* status_out);
 int b200kv_reset_device_status(void* stream);
 
@@ -373,11 +376,15 @@ int b200kv_kv_write(const void* key, int64_t key_stride_tok, int64_t key_stride_
  * b < num_seqs at position p = positions[b] (int32; negative taken as 0):
  * seq_lens[b] = p + 1, slot_mapping[b] = block_table[b, p / block_size] *
  * block_size + p % block_size, and h[b, :] = embed[tokens[b], :] (bf16
- * [vocab, hidden] rows, hidden % 8 == 0, 16-byte aligned).  No counterpart in
- * the reference (its engine prepares these on the host). */
+ * [vocab, hidden] rows, hidden % 8 == 0, 16-byte aligned).  A token id
+ * outside [0, vocab) gives a zero row, a position past the row's
+ * max_blocks_per_seq pages gives slot -1 (skipped by the KV writes); both
+ * record B200KV_DEV_INDEX_RANGE.  No counterpart in the reference (its engine
+ * prepares these on the host). */
 int b200kv_decode_step_prep(const int32_t* positions, const int64_t* tokens, const void* embed, int hidden,
-                            const int32_t* block_table, int64_t bt_stride, int block_size, int num_seqs,
-                            int32_t* seq_lens, int64_t* slot_mapping, void* h, void* stream);
+                            int vocab, const int32_t* block_table, int64_t bt_stride, int max_blocks_per_seq,
+                            int block_size, int num_seqs, int32_t* seq_lens, int64_t* slot_mapping, void* h,
+                            void* stream);
 
 /* ---- greedy argmax over logits rows ---------------------------------------------
  *

@@ -279,11 +279,26 @@ def test_decode_step_prep(cuda):
     seq_lens = torch.zeros(B, dtype=torch.int32, device=cuda)
     slots = torch.zeros(B, dtype=torch.int64, device=cuda)
     h = torch.zeros(B, H, dtype=torch.bfloat16, device=cuda)
-    check(lib.b200kv_decode_step_prep(pos.data_ptr(), tokens.data_ptr(), embed.data_ptr(), H, bt.data_ptr(),
-                                      bt.stride(0), bs, B, seq_lens.data_ptr(), slots.data_ptr(), h.data_ptr(),
-                                      torch.cuda.current_stream().cuda_stream), "b200kv_decode_step_prep")
+    st = torch.cuda.current_stream().cuda_stream
+    check(lib.b200kv_decode_step_prep(pos.data_ptr(), tokens.data_ptr(), embed.data_ptr(), H, V, bt.data_ptr(),
+                                      bt.stride(0), bt.shape[1], bs, B, seq_lens.data_ptr(), slots.data_ptr(),
+                                      h.data_ptr(), st), "b200kv_decode_step_prep")
     torch.cuda.synchronize()
     assert torch.equal(seq_lens, pos + 1)
     want = bt.gather(1, (pos // bs).long().unsqueeze(1)).squeeze(1).long() * bs + (pos % bs).long()
     assert torch.equal(slots, want)
     assert torch.equal(h, embed[tokens])
+    import _b200kv
+    assert _b200kv.device_status() == 0
+    # an id past the vocabulary and a position past the row: nothing read out
+    # of the tables, a zero row, slot -1 and the index-range status
+    tokens[1] = V
+    pos[3] = 64 * bs
+    check(lib.b200kv_decode_step_prep(pos.data_ptr(), tokens.data_ptr(), embed.data_ptr(), H, V, bt.data_ptr(),
+                                      bt.stride(0), bt.shape[1], bs, B, seq_lens.data_ptr(), slots.data_ptr(),
+                                      h.data_ptr(), st), "b200kv_decode_step_prep")
+    torch.cuda.synchronize()
+    assert torch.all(h[1] == 0) and int(slots[3]) == -1
+    assert torch.equal(h[0], embed[tokens[0]]) and int(slots[0]) == int(want[0])
+    assert _b200kv.device_status() == 0x105
+    _b200kv.reset_device_status()
