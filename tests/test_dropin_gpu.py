@@ -153,8 +153,8 @@ def test_quark_w4a16_layer_prepacked_at_load_and_graph_capturable(cuda, monkeypa
     """vLLM's Quark OCP-MX scheme on a W4A16 MXFP4 layer as the engine loads it
     (weight [N, K/2], scales [N, K/32]): process_weights_after_loading (hooked)
     packs the scale atoms, so a CUDA-graph capture of apply_weights needs no
-    lazy repack; results within the reference's tolerance of the oracle for
-    M = 1, 4 and a 3-D batch of 12 tokens, bias added."""
+    lazy repack; results within two bf16 roundings of the oracle (the product
+    and the bias add) for M = 1, 4 and a 3-D batch of 12 tokens, bias added."""
     monkeypatch.setenv("FP8KV_HIPW4", "1")
     import fp8kv_hipw4 as hw
     assert hw._install() and hw.install_quark_hook()
@@ -169,9 +169,13 @@ def test_quark_w4a16_layer_prepacked_at_load_and_graph_capturable(cuda, monkeypa
     ckpt = layer._b200kv_scale_ckpt
     assert tuple(ckpt.shape) == (K // 32, N)
     assert ("p", ckpt.data_ptr(), tuple(ckpt.shape), ckpt.device) in hw._repack_cache
-    bias = torch.randn(N, device=cuda).to(torch.bfloat16)
+    g = torch.Generator().manual_seed(17)
+    bias = torch.randn(N, generator=g).to(torch.bfloat16).to(cuda)
+    # apply_weights rounds to bf16 twice, the product and then the bias add,
+    # each by at most 2^-8 of the value: 1e-2 of the maximum bounds both
+    tol = 1e-2
     for shape in ((1, K), (4, K), (3, 4, K)):
-        x = torch.randn(*shape).to(torch.bfloat16).to(cuda)
+        x = torch.randn(*shape, generator=g).to(torch.bfloat16).to(cuda)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         graph = torch.cuda.CUDAGraph()
@@ -183,4 +187,4 @@ def test_quark_w4a16_layer_prepacked_at_load_and_graph_capturable(cuda, monkeypa
         torch.cuda.synchronize()
         assert tuple(y.shape) == shape[:-1] + (N,)
         ref = MO.mxfp4_linear_reference(W, S, x.reshape(-1, K).cpu()) + bias.float().cpu()
-        assert MO.rel_to_max_err(y.reshape(-1, N).float().cpu(), ref) < 5e-3, shape
+        assert MO.rel_to_max_err(y.reshape(-1, N).float().cpu(), ref) < tol, shape
